@@ -1,0 +1,715 @@
+// attention.cu - fused causal self-attention (reference: src/model.c:514-563
+// forward, src/model.c:742-822 backward, src/fast.c:264-298 inference).
+//
+// The reference materialises S = QK^T/sqrt(hs), masks, softmaxes into P and
+// multiplies P V per (batch, head). Here every (batch, head, 64-query tile)
+// runs as one block that streams 64-key tiles through shared memory with an
+// online softmax, so no T x T matrix is written. The backward recomputes P
+// from the saved row log-sum-exp in two deterministic passes (dK/dV by key
+// tile, dQ by query tile) instead of accumulating dQ with atomics.
+//
+// Head size 64 (every BASELINE config) uses the tensor cores through
+// mma.sync m16n8k8 TF32; in 3xTF32 mode each product is split as
+// hi*hi + hi*lo + lo*hi. Other head sizes (the reference's unit tests use
+// hs = 8) take a CUDA-core kernel with one warp per query row.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cg {
+
+CG_DEV_ERROR_READER(attn_take_dev_error)
+
+namespace {
+
+constexpr int HS = 64;
+constexpr int TQ = 64, TK = 64;  // query / key tile
+constexpr int LDS = HS + 4;      // smem row pitch (floats)
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ void mma8(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// d += a * b with fp32 operands, TF32 or 3xTF32 depending on SPLIT.
+template <bool SPLIT>
+__device__ __forceinline__ void mma_f32(float (&d)[4], const float (&a)[4], const float (&b)[2]) {
+    uint32_t ah[4], bh[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ah[i] = to_tf32(a[i]);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) bh[i] = to_tf32(b[i]);
+    if (SPLIT) {
+        uint32_t al[4], bl[2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) al[i] = to_tf32(a[i] - __uint_as_float(ah[i]));
+#pragma unroll
+        for (int i = 0; i < 2; ++i) bl[i] = to_tf32(b[i] - __uint_as_float(bh[i]));
+        mma8(d, al, bh);
+        mma8(d, ah, bl);
+    }
+    mma8(d, ah, bh);
+}
+
+// Key order inside an 8-wide n-tile: accumulator column n holds key sig(n), so
+// a thread's C-fragment columns (2t, 2t+1) are keys (t, t+4) - exactly the
+// A-fragment columns it needs when the result feeds the next product.
+__device__ __forceinline__ int sig(int n) { return (n >> 1) + 4 * (n & 1); }
+
+// Load a [rows x 64] tile with row pitch `ld` (floats) into smem [rows][LDS];
+// rows >= valid are zero-filled.
+__device__ __forceinline__ void load_tile(float *dst, const float *src, long ld, int rows,
+                                          int valid) {
+    for (int i = threadIdx.x; i < rows * (HS / 4); i += blockDim.x) {
+        const int r = i / (HS / 4), c4 = i % (HS / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < valid) v = *(const float4 *)(src + (long)r * ld + c4 * 4);
+        *(float4 *)(dst + r * LDS + c4 * 4) = v;
+    }
+}
+
+// A fragment (16 rows x 8 cols starting at row r0, col k0) from smem [.][LDS]
+__device__ __forceinline__ void frag_a(float (&a)[4], const float *s, int r0, int k0, int g, int t) {
+    a[0] = s[(r0 + g) * LDS + k0 + t];
+    a[1] = s[(r0 + g + 8) * LDS + k0 + t];
+    a[2] = s[(r0 + g) * LDS + k0 + t + 4];
+    a[3] = s[(r0 + g + 8) * LDS + k0 + t + 4];
+}
+
+// B fragment where the operand's n index runs over smem rows (permuted by
+// sig) and k over smem columns: element (k, n) = s[(n0 + sig(n))][k0 + k].
+__device__ __forceinline__ void frag_b_rows(float (&b)[2], const float *s, int n0, int k0, int g,
+                                            int t) {
+    b[0] = s[(n0 + sig(g)) * LDS + k0 + t];
+    b[1] = s[(n0 + sig(g)) * LDS + k0 + t + 4];
+}
+
+// B fragment where k runs over smem rows and n over smem columns:
+// element (k, n) = s[(k0 + k)][n0 + n].
+__device__ __forceinline__ void frag_b_cols(float (&b)[2], const float *s, int k0, int n0, int g,
+                                            int t) {
+    b[0] = s[(k0 + t) * LDS + n0 + g];
+    b[1] = s[(k0 + t + 4) * LDS + n0 + g];
+}
+
+// ------------------------------------------------------------- forward
+template <bool SPLIT>
+__global__ void __launch_bounds__(128)
+attn_fwd_mma_kernel(const float *__restrict__ qkv, float *__restrict__ out, float *__restrict__ lse,
+                    int T, int C, int H, float scale) {
+    extern __shared__ float sm[];
+    float *sQ = sm, *sK = sm + TQ * LDS, *sV = sm + 2 * TQ * LDS;
+    const int nqt = (T + TQ - 1) / TQ;
+    const int qt = nqt - 1 - blockIdx.x;  // heaviest tiles first
+    const int bh = blockIdx.y, b = bh / H, h = bh % H;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const long ld = 3L * C;
+    const float *base = qkv + (long)b * T * ld;
+    const int q0 = qt * TQ;
+    load_tile(sQ, base + (long)q0 * ld + h * HS, ld, TQ, min(TQ, T - q0));
+
+    float o[8][4] = {};
+    float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+    const int row0 = q0 + warp * 16 + g, row1 = row0 + 8;
+
+    for (int kt = 0; kt <= qt; ++kt) {
+        const int k0 = kt * TK;
+        __syncthreads();
+        load_tile(sK, base + (long)k0 * ld + C + h * HS, ld, TK, min(TK, T - k0));
+        load_tile(sV, base + (long)k0 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k0));
+        __syncthreads();
+        float s[8][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < HS / 8; ++kk) {
+            float a[4];
+            frag_a(a, sQ, warp * 16, kk * 8, g, t);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float bb[2];
+                frag_b_rows(bb, sK, j * 8, kk * 8, g, t);
+                mma_f32<SPLIT>(s[j], a, bb);
+            }
+        }
+        // scale, mask (future keys and keys past T), row max
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = k0 + j * 8 + t + ((e & 1) ? 4 : 0);
+                const int row = (e < 2) ? row0 : row1;
+                float v = s[j][e] * scale;
+                if (key > row || key >= T) v = -INFINITY;
+                s[j][e] = v;
+                mx[e >> 1] = fmaxf(mx[e >> 1], v);
+            }
+        }
+        float corr[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            const float mnew = fmaxf(m_r[r], mx[r]);
+            corr[r] = (m_r[r] == -INFINITY) ? 0.f : expf(m_r[r] - mnew);
+            m_r[r] = mnew;
+        }
+        float ls[2] = {0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float mrow = m_r[e >> 1];
+                const float p = (s[j][e] == -INFINITY) ? 0.f : expf(s[j][e] - mrow);
+                s[j][e] = p;
+                ls[e >> 1] += p;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
+            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
+            l_r[r] = l_r[r] * corr[r] + ls[r];
+        }
+#pragma unroll
+        for (int dn = 0; dn < 8; ++dn) {
+            o[dn][0] *= corr[0];
+            o[dn][1] *= corr[0];
+            o[dn][2] *= corr[1];
+            o[dn][3] *= corr[1];
+        }
+        // O += P V ; P's C fragment of key tile j is the A fragment {c0, c2, c1, c3}
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float a[4] = {s[j][0], s[j][2], s[j][1], s[j][3]};
+#pragma unroll
+            for (int dn = 0; dn < 8; ++dn) {
+                float bb[2];
+                frag_b_cols(bb, sV, j * 8, dn * 8, g, t);
+                mma_f32<SPLIT>(o[dn], a, bb);
+            }
+        }
+    }
+    const float inv0 = 1.0f / l_r[0], inv1 = 1.0f / l_r[1];
+#pragma unroll
+    for (int dn = 0; dn < 8; ++dn) {
+        const int col = h * HS + dn * 8 + 2 * t;
+        if (row0 < T)
+            *(float2 *)(out + ((long)b * T + row0) * C + col) = make_float2(o[dn][0] * inv0, o[dn][1] * inv0);
+        if (row1 < T)
+            *(float2 *)(out + ((long)b * T + row1) * C + col) = make_float2(o[dn][2] * inv1, o[dn][3] * inv1);
+    }
+    if (lse && t == 0) {
+        if (row0 < T) lse[(long)bh * T + row0] = m_r[0] + logf(l_r[0]);
+        if (row1 < T) lse[(long)bh * T + row1] = m_r[1] + logf(l_r[1]);
+    }
+}
+
+// ------------------------------------------------------------- backward
+// D[bh, t] = sum_d dO[b,t,h*hs+d] * O[b,t,h*hs+d]
+__global__ void attn_bwd_dot_kernel(const float *__restrict__ out, const float *__restrict__ dout,
+                                    float *__restrict__ D, int B, int T, int C, int H, int hs) {
+    const long rows = (long)B * H * T;
+    const int lane = threadIdx.x & 31;
+    for (long r = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; r < rows;
+         r += ((long)gridDim.x * blockDim.x) >> 5) {
+        const long bh = r / T;
+        const int tt = (int)(r % T), b = (int)(bh / H), h = (int)(bh % H);
+        const float *o = out + ((long)b * T + tt) * C + h * hs;
+        const float *d = dout + ((long)b * T + tt) * C + h * hs;
+        float s = 0.f;
+        for (int i = lane; i < hs; i += 32) s += o[i] * d[i];
+        s = warp_sum(s);
+        if (lane == 0) D[r] = s;
+    }
+}
+
+// dK, dV for one 64-key tile; loops over query tiles qt >= kt.
+template <bool SPLIT>
+__global__ void __launch_bounds__(128)
+attn_bwd_dkdv_kernel(const float *__restrict__ qkv, const float *__restrict__ dout,
+                     const float *__restrict__ lse, const float *__restrict__ Dd,
+                     float *__restrict__ dqkv, int T, int C, int H, float scale) {
+    extern __shared__ float sm[];
+    float *sK = sm, *sV = sm + TK * LDS, *sQ = sm + 2 * TK * LDS, *sO = sm + 3 * TK * LDS;
+    float *sL = sm + 4 * TK * LDS, *sD = sL + TQ;
+    const int nkt = (T + TK - 1) / TK;
+    const int kt = blockIdx.x;  // tile 0 has the most work: launched first
+    const int bh = blockIdx.y, b = bh / H, h = bh % H;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const long ld = 3L * C;
+    const float *base = qkv + (long)b * T * ld;
+    const float *dob = dout + (long)b * T * C;
+    const int k0 = kt * TK;
+    load_tile(sK, base + (long)k0 * ld + C + h * HS, ld, TK, min(TK, T - k0));
+    load_tile(sV, base + (long)k0 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k0));
+    float dk[8][4] = {}, dv[8][4] = {};
+    const int key0 = k0 + warp * 16 + g, key1 = key0 + 8;
+    for (int qt = kt; qt < nkt; ++qt) {
+        const int q0 = qt * TQ;
+        __syncthreads();
+        load_tile(sQ, base + (long)q0 * ld + h * HS, ld, TQ, min(TQ, T - q0));
+        load_tile(sO, dob + (long)q0 * C + h * HS, C, TQ, min(TQ, T - q0));
+        for (int i = threadIdx.x; i < TQ; i += blockDim.x) {
+            const int q = q0 + i;
+            sL[i] = q < T ? lse[(long)bh * T + q] : 0.f;
+            sD[i] = q < T ? Dd[(long)bh * T + q] : 0.f;
+        }
+        __syncthreads();
+        // S^T = K Q^T and dP^T = V dO^T  (rows: this warp's 16 keys, cols: 64 queries)
+        float st[8][4] = {}, dpt[8][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < HS / 8; ++kk) {
+            float ak[4], av[4];
+            frag_a(ak, sK, warp * 16, kk * 8, g, t);
+            frag_a(av, sV, warp * 16, kk * 8, g, t);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float bq[2], bo[2];
+                frag_b_rows(bq, sQ, j * 8, kk * 8, g, t);
+                frag_b_rows(bo, sO, j * 8, kk * 8, g, t);
+                mma_f32<SPLIT>(st[j], ak, bq);
+                mma_f32<SPLIT>(dpt[j], av, bo);
+            }
+        }
+        // P^T = exp(S^T*scale - lse[q]) (0 where q < key), dS^T = P^T (dP^T - D[q])
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int qi = j * 8 + t + ((e & 1) ? 4 : 0);
+                const int q = q0 + qi;
+                const int key = (e < 2) ? key0 : key1;
+                float p = 0.f;
+                if (q >= key && q < T && key < T) p = expf(st[j][e] * scale - sL[qi]);
+                st[j][e] = p;
+                dpt[j][e] = p * (dpt[j][e] - sD[qi]);
+            }
+        }
+        // dV += P^T dO ; dK += dS^T Q
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float ap[4] = {st[j][0], st[j][2], st[j][1], st[j][3]};
+            const float as[4] = {dpt[j][0], dpt[j][2], dpt[j][1], dpt[j][3]};
+#pragma unroll
+            for (int dn = 0; dn < 8; ++dn) {
+                float bo[2], bq[2];
+                frag_b_cols(bo, sO, j * 8, dn * 8, g, t);
+                frag_b_cols(bq, sQ, j * 8, dn * 8, g, t);
+                mma_f32<SPLIT>(dv[dn], ap, bo);
+                mma_f32<SPLIT>(dk[dn], as, bq);
+            }
+        }
+    }
+    float *dkb = dqkv + (long)b * T * ld + C + h * HS;
+    float *dvb = dqkv + (long)b * T * ld + 2 * C + h * HS;
+#pragma unroll
+    for (int dn = 0; dn < 8; ++dn) {
+        const int col = dn * 8 + 2 * t;
+        if (key0 < T) {
+            *(float2 *)(dkb + (long)key0 * ld + col) = make_float2(dk[dn][0] * scale, dk[dn][1] * scale);
+            *(float2 *)(dvb + (long)key0 * ld + col) = make_float2(dv[dn][0], dv[dn][1]);
+        }
+        if (key1 < T) {
+            *(float2 *)(dkb + (long)key1 * ld + col) = make_float2(dk[dn][2] * scale, dk[dn][3] * scale);
+            *(float2 *)(dvb + (long)key1 * ld + col) = make_float2(dv[dn][2], dv[dn][3]);
+        }
+    }
+}
+
+// dQ for one 64-query tile; loops over key tiles kt <= qt.
+template <bool SPLIT>
+__global__ void __launch_bounds__(128)
+attn_bwd_dq_kernel(const float *__restrict__ qkv, const float *__restrict__ dout,
+                   const float *__restrict__ lse, const float *__restrict__ Dd,
+                   float *__restrict__ dqkv, int T, int C, int H, float scale) {
+    extern __shared__ float sm[];
+    float *sQ = sm, *sO = sm + TQ * LDS, *sK = sm + 2 * TQ * LDS, *sV = sm + 3 * TQ * LDS;
+    const int nqt = (T + TQ - 1) / TQ;
+    const int qt = nqt - 1 - blockIdx.x;
+    const int bh = blockIdx.y, b = bh / H, h = bh % H;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const long ld = 3L * C;
+    const float *base = qkv + (long)b * T * ld;
+    const int q0 = qt * TQ;
+    load_tile(sQ, base + (long)q0 * ld + h * HS, ld, TQ, min(TQ, T - q0));
+    load_tile(sO, dout + ((long)b * T + q0) * C + h * HS, C, TQ, min(TQ, T - q0));
+    const int row0 = q0 + warp * 16 + g, row1 = row0 + 8;
+    const float L0 = row0 < T ? lse[(long)bh * T + row0] : 0.f;
+    const float L1 = row1 < T ? lse[(long)bh * T + row1] : 0.f;
+    const float D0 = row0 < T ? Dd[(long)bh * T + row0] : 0.f;
+    const float D1 = row1 < T ? Dd[(long)bh * T + row1] : 0.f;
+    float dq[8][4] = {};
+    for (int kt = 0; kt <= qt; ++kt) {
+        const int k0 = kt * TK;
+        __syncthreads();
+        load_tile(sK, base + (long)k0 * ld + C + h * HS, ld, TK, min(TK, T - k0));
+        load_tile(sV, base + (long)k0 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k0));
+        __syncthreads();
+        float s[8][4] = {}, dp[8][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < HS / 8; ++kk) {
+            float aq[4], ao[4];
+            frag_a(aq, sQ, warp * 16, kk * 8, g, t);
+            frag_a(ao, sO, warp * 16, kk * 8, g, t);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float bk[2], bv[2];
+                frag_b_rows(bk, sK, j * 8, kk * 8, g, t);
+                frag_b_rows(bv, sV, j * 8, kk * 8, g, t);
+                mma_f32<SPLIT>(s[j], aq, bk);
+                mma_f32<SPLIT>(dp[j], ao, bv);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = k0 + j * 8 + t + ((e & 1) ? 4 : 0);
+                const int row = (e < 2) ? row0 : row1;
+                float p = 0.f;
+                if (key <= row && key < T && row < T)
+                    p = expf(s[j][e] * scale - ((e < 2) ? L0 : L1));
+                s[j][e] = p * (dp[j][e] - ((e < 2) ? D0 : D1));  // dS
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float a[4] = {s[j][0], s[j][2], s[j][1], s[j][3]};
+#pragma unroll
+            for (int dn = 0; dn < 8; ++dn) {
+                float bk[2];
+                frag_b_cols(bk, sK, j * 8, dn * 8, g, t);
+                mma_f32<SPLIT>(dq[dn], a, bk);
+            }
+        }
+    }
+    float *dqb = dqkv + (long)b * T * ld + h * HS;
+#pragma unroll
+    for (int dn = 0; dn < 8; ++dn) {
+        const int col = dn * 8 + 2 * t;
+        if (row0 < T) *(float2 *)(dqb + (long)row0 * ld + col) = make_float2(dq[dn][0] * scale, dq[dn][1] * scale);
+        if (row1 < T) *(float2 *)(dqb + (long)row1 * ld + col) = make_float2(dq[dn][2] * scale, dq[dn][3] * scale);
+    }
+}
+
+// ----------------------------------------------- CUDA-core kernels (any hs)
+// One warp per query row; lanes hold head dims d = lane + 32*i (hs <= 128).
+// Keys are processed in order with an online softmax.
+__global__ void attn_fwd_simt_kernel(const float *__restrict__ qkv, float *__restrict__ out,
+                                     float *__restrict__ lse, int B, int T, int C, int H, int hs,
+                                     float scale, int q0) {
+    const int lane = threadIdx.x & 31;
+    const long rows = (long)B * H * (T - q0);
+    for (long r = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; r < rows;
+         r += ((long)gridDim.x * blockDim.x) >> 5) {
+        const long bh = r / (T - q0);
+        const int tq = q0 + (int)(r % (T - q0)), b = (int)(bh / H), h = (int)(bh % H);
+        const long ld = 3L * C;
+        const float *qr = qkv + ((long)b * T + tq) * ld + h * hs;
+        float q[4], o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) q[i] = (lane + 32 * i < hs) ? qr[lane + 32 * i] : 0.f;
+        float m = -INFINITY, l = 0.f;
+        for (int j = 0; j <= tq; ++j) {
+            const float *kr = qkv + ((long)b * T + j) * ld + C + h * hs;
+            const float *vr = kr + C;
+            float d = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (lane + 32 * i < hs) d += q[i] * kr[lane + 32 * i];
+            const float sc = warp_sum(d) * scale;
+            const float mn = fmaxf(m, sc);
+            const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
+            const float p = expf(sc - mn);
+            l = l * corr + p;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (lane + 32 * i < hs) o[i] = o[i] * corr + p * vr[lane + 32 * i];
+            m = mn;
+        }
+        float *orow = out + ((long)b * T + tq) * C + h * hs;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (lane + 32 * i < hs) orow[lane + 32 * i] = o[i] / l;
+        if (lse && lane == 0) lse[bh * T + tq] = m + logf(l);
+    }
+}
+
+// dQ rows (mode 0, one warp per query row) or dK/dV rows (mode 1, one warp
+// per key row), recomputing P from the saved lse.
+__global__ void attn_bwd_simt_kernel(const float *__restrict__ qkv, const float *__restrict__ dout,
+                                     const float *__restrict__ lse, const float *__restrict__ Dd,
+                                     float *__restrict__ dqkv, int B, int T, int C, int H, int hs,
+                                     float scale, int mode) {
+    const int lane = threadIdx.x & 31;
+    const long rows = (long)B * H * T;
+    const long ld = 3L * C;
+    for (long r = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; r < rows;
+         r += ((long)gridDim.x * blockDim.x) >> 5) {
+        const long bh = r / T;
+        const int x = (int)(r % T), b = (int)(bh / H), h = (int)(bh % H);
+        const float *qb = qkv + (long)b * T * ld + h * hs;
+        const float *kb = qb + C, *vb = qb + 2 * C;
+        const float *ob = dout + (long)b * T * C + h * hs;
+        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+        if (mode == 0) {  // x = query row
+            const int lo = 0, hi = x;
+            for (int j = lo; j <= hi; ++j) {
+                float sd = 0.f, dpd = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < hs) {
+                        sd += qb[(long)x * ld + d] * kb[(long)j * ld + d];
+                        dpd += ob[(long)x * C + d] * vb[(long)j * ld + d];
+                    }
+                }
+                const float p = expf(warp_sum(sd) * scale - lse[bh * T + x]);
+                const float ds = p * (warp_sum(dpd) - Dd[bh * T + x]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < hs) acc0[i] += ds * kb[(long)j * ld + d];
+                }
+            }
+            float *dq = dqkv + ((long)b * T + x) * ld + h * hs;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (lane + 32 * i < hs) dq[lane + 32 * i] = acc0[i] * scale;
+        } else {  // x = key row
+            for (int q = x; q < T; ++q) {
+                float sd = 0.f, dpd = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < hs) {
+                        sd += qb[(long)q * ld + d] * kb[(long)x * ld + d];
+                        dpd += ob[(long)q * C + d] * vb[(long)x * ld + d];
+                    }
+                }
+                const float p = expf(warp_sum(sd) * scale - lse[bh * T + q]);
+                const float ds = p * (warp_sum(dpd) - Dd[bh * T + q]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < hs) {
+                        acc0[i] += ds * qb[(long)q * ld + d];   // dK
+                        acc1[i] += p * ob[(long)q * C + d];     // dV
+                    }
+                }
+            }
+            float *dk = dqkv + ((long)b * T + x) * ld + C + h * hs;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (lane + 32 * i < hs) {
+                    dk[lane + 32 * i] = acc0[i] * scale;
+                    dk[C + lane + 32 * i] = acc1[i];
+                }
+        }
+    }
+}
+
+// Decode: one block per (sequence, head); scores for all cached positions in
+// shared memory, then a block softmax and P V with threads over head dims.
+__global__ void __launch_bounds__(256)
+attn_decode_kernel(const float *__restrict__ q, long ldq, const float *__restrict__ kc,
+                   const float *__restrict__ vc, long Tmax, int len, float *__restrict__ out,
+                   int C, int H, int hs, float scale) {
+    extern __shared__ float sm[];
+    float *sq = sm, *sp = sm + hs, *red = sp + len;  // red: 64 floats
+    const int bh = blockIdx.x, b = bh / H, h = bh % H;
+    const float *qr = q + (long)b * ldq + h * hs;
+    for (int i = threadIdx.x; i < hs; i += blockDim.x) sq[i] = qr[i];
+    __syncthreads();
+    const float *kb = kc + (long)b * Tmax * C + h * hs;
+    const float *vb = vc + (long)b * Tmax * C + h * hs;
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < len; j += blockDim.x) {
+        const float *kr = kb + (long)j * C;
+        float d = 0.f;
+        for (int i = 0; i < hs; i += 4) {
+            const float4 kv = *(const float4 *)(kr + i);
+            d += sq[i] * kv.x + sq[i + 1] * kv.y + sq[i + 2] * kv.z + sq[i + 3] * kv.w;
+        }
+        d *= scale;
+        sp[j] = d;
+        mx = fmaxf(mx, d);
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    mx = warp_max(mx);
+    if (lane == 0) red[wid] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int k = 1; k < nw; ++k) mx = fmaxf(mx, red[k]);
+    __syncthreads();
+    float s = 0.f;
+    for (int j = threadIdx.x; j < len; j += blockDim.x) {
+        const float p = expf(sp[j] - mx);
+        sp[j] = p;
+        s += p;
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[wid] = s;
+    __syncthreads();
+    s = 0.f;
+    for (int k = 0; k < nw; ++k) s += red[k];
+    const float inv = 1.0f / s;
+    // P V: thread (group, d) sums keys j = group (mod G) for dim d
+    const int G = blockDim.x / hs;
+    const int d = threadIdx.x % hs, grp = threadIdx.x / hs;
+    float acc = 0.f;
+    if (grp < G)
+        for (int j = grp; j < len; j += G) acc += sp[j] * vb[(long)j * C + d];
+    __syncthreads();
+    float *part = red + 64;  // G * hs floats
+    if (grp < G) part[grp * hs + d] = acc;
+    __syncthreads();
+    if (threadIdx.x < hs) {
+        float o = 0.f;
+        for (int k = 0; k < G; ++k) o += part[k * hs + threadIdx.x];
+        out[(long)b * C + h * hs + threadIdx.x] = o * inv;
+    }
+}
+
+template <typename K>
+int set_smem(K kern, int bytes) {
+    CG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return OK;
+}
+
+}  // namespace
+
+#define LAUNCH_CHECK() do { ++g_launch_count; CG_CUDA(cudaGetLastError()); } while (0)
+
+int attention_fwd(const float *qkv, float *out, float *lse, int B, int T, int C, int H,
+                  cudaStream_t s) {
+    if (B <= 0 || T <= 0) return OK;
+    const int hs = C / H;
+    const float scale = 1.0f / sqrtf((float)hs);
+    if (hs == HS && precision() != PREC_FP32) {
+        const int smem = 3 * TQ * LDS * sizeof(float);
+        dim3 grid((T + TQ - 1) / TQ, B * H);
+        if (precision() == PREC_3XTF32) {
+            static bool a = false;
+            if (!a) { CG_TRY(set_smem(attn_fwd_mma_kernel<true>, smem)); a = true; }
+            attn_fwd_mma_kernel<true><<<grid, 128, smem, s>>>(qkv, out, lse, T, C, H, scale);
+        } else {
+            static bool a = false;
+            if (!a) { CG_TRY(set_smem(attn_fwd_mma_kernel<false>, smem)); a = true; }
+            attn_fwd_mma_kernel<false><<<grid, 128, smem, s>>>(qkv, out, lse, T, C, H, scale);
+        }
+        LAUNCH_CHECK();
+        return OK;
+    }
+    if (hs > 128) {
+        set_last_error(ERR_ARG, "attention: head size %d > 128 unsupported", hs);
+        return ERR_ARG;
+    }
+    const long rows = (long)B * H * T;
+    attn_fwd_simt_kernel<<<(int)std::min<long>((rows + 7) / 8, 148L * 64), 256, 0, s>>>(
+        qkv, out, lse, B, T, C, H, hs, scale, 0);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int attention_fwd_rows(const float *qkv, float *out, int B, int T, int C, int H, int q0,
+                       cudaStream_t s) {
+    const int hs = C / H;
+    if (hs > 128) {
+        set_last_error(ERR_ARG, "attention: head size %d > 128 unsupported", hs);
+        return ERR_ARG;
+    }
+    const long rows = (long)B * H * (T - q0);
+    if (rows <= 0) return OK;
+    attn_fwd_simt_kernel<<<(int)std::min<long>((rows + 7) / 8, 148L * 64), 256, 0, s>>>(
+        qkv, out, nullptr, B, T, C, H, hs, 1.0f / sqrtf((float)hs), q0);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+size_t attention_bwd_scratch_bytes(int B, int T, int H) { return (size_t)B * H * T * sizeof(float); }
+
+int attention_bwd(const float *qkv, const float *out, const float *dout, const float *lse,
+                  float *dqkv, float *scratch, int B, int T, int C, int H, cudaStream_t s) {
+    if (B <= 0 || T <= 0) return OK;
+    const int hs = C / H;
+    const float scale = 1.0f / sqrtf((float)hs);
+    float *D = scratch;
+    const long rows = (long)B * H * T;
+    attn_bwd_dot_kernel<<<(int)std::min<long>((rows + 7) / 8, 148L * 64), 256, 0, s>>>(out, dout, D, B,
+                                                                                      T, C, H, hs);
+    LAUNCH_CHECK();
+    if (hs == HS && precision() != PREC_FP32) {
+        const int nt = (T + 63) / 64;
+        const int smem_kv = (4 * TK * LDS + 2 * TQ) * sizeof(float);
+        const int smem_q = 4 * TQ * LDS * sizeof(float);
+        dim3 grid(nt, B * H);
+        if (precision() == PREC_3XTF32) {
+            static bool a = false;
+            if (!a) {
+                CG_TRY(set_smem(attn_bwd_dkdv_kernel<true>, smem_kv));
+                CG_TRY(set_smem(attn_bwd_dq_kernel<true>, smem_q));
+                a = true;
+            }
+            attn_bwd_dkdv_kernel<true><<<grid, 128, smem_kv, s>>>(qkv, dout, lse, D, dqkv, T, C, H, scale);
+            LAUNCH_CHECK();
+            attn_bwd_dq_kernel<true><<<grid, 128, smem_q, s>>>(qkv, dout, lse, D, dqkv, T, C, H, scale);
+        } else {
+            static bool a = false;
+            if (!a) {
+                CG_TRY(set_smem(attn_bwd_dkdv_kernel<false>, smem_kv));
+                CG_TRY(set_smem(attn_bwd_dq_kernel<false>, smem_q));
+                a = true;
+            }
+            attn_bwd_dkdv_kernel<false><<<grid, 128, smem_kv, s>>>(qkv, dout, lse, D, dqkv, T, C, H, scale);
+            LAUNCH_CHECK();
+            attn_bwd_dq_kernel<false><<<grid, 128, smem_q, s>>>(qkv, dout, lse, D, dqkv, T, C, H, scale);
+        }
+        LAUNCH_CHECK();
+        return OK;
+    }
+    if (hs > 128) {
+        set_last_error(ERR_ARG, "attention: head size %d > 128 unsupported", hs);
+        return ERR_ARG;
+    }
+    const int grid = (int)std::min<long>((rows + 7) / 8, 148L * 64);
+    attn_bwd_simt_kernel<<<grid, 256, 0, s>>>(qkv, dout, lse, D, dqkv, B, T, C, H, hs, scale, 0);
+    LAUNCH_CHECK();
+    attn_bwd_simt_kernel<<<grid, 256, 0, s>>>(qkv, dout, lse, D, dqkv, B, T, C, H, hs, scale, 1);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int attention_decode(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
+                     int len, float *out, int B, int C, int H, cudaStream_t s) {
+    const int hs = C / H;
+    if (hs % 4 != 0 || hs > 256 || len <= 0) {
+        set_last_error(ERR_ARG, "attention_decode: unsupported hs=%d len=%d", hs, len);
+        return ERR_ARG;
+    }
+    const int G = 256 / hs;
+    const size_t smem = (size_t)(hs + len + 64 + G * hs) * sizeof(float);
+    if (smem > 200 * 1024) {
+        set_last_error(ERR_ARG, "attention_decode: context %d too long", len);
+        return ERR_ARG;
+    }
+    static bool a = false;
+    if (!a) { CG_TRY(set_smem(attn_decode_kernel, 200 * 1024 + 4096)); a = true; }
+    attn_decode_kernel<<<B * H, 256, smem, s>>>(q, ldq, kcache, vcache, Tmax, len, out, C, H, hs,
+                                                1.0f / sqrtf((float)hs));
+    LAUNCH_CHECK();
+    return OK;
+}
+
+}  // namespace cg

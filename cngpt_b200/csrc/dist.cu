@@ -1,0 +1,130 @@
+// dist.cu - data-parallel gradient exchange over NCCL (one process per GPU).
+//
+// The reference has no distributed path. Data parallelism here follows the
+// plan of a single-process step over the global batch: every rank runs the
+// forward/backward of its own B x T slice (mean loss over B*T), then the
+// gradient arena is averaged across ranks (sum / world) before the clip norm
+// and AdamW, which therefore see the gradient of the mean loss over the
+// global batch on every rank.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+
+#include "abi_common.h"
+#include "model_ctx.h"
+
+extern "C" {
+#include "cngpt_cuda.h"
+}
+
+namespace cg {
+
+// NCCL is opened on first use rather than linked: a process that loads this
+// library before PyTorch must not pin the system libnccl.so.2 ahead of the
+// one PyTorch ships (and a process without data parallelism needs none).
+namespace {
+struct Nccl {
+    void *h = nullptr;
+    ncclResult_t (*getUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*commInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*allReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+    const char *(*errorString)(ncclResult_t) = nullptr;
+} g_nccl;
+
+int nccl_open() {
+    if (g_nccl.h) return OK;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+        set_last_error(ERR_NCCL, "cannot open libnccl.so.2: %s", dlerror());
+        return ERR_NCCL;
+    }
+    g_nccl.getUniqueId = (decltype(g_nccl.getUniqueId))dlsym(h, "ncclGetUniqueId");
+    g_nccl.commInitRank = (decltype(g_nccl.commInitRank))dlsym(h, "ncclCommInitRank");
+    g_nccl.allReduce = (decltype(g_nccl.allReduce))dlsym(h, "ncclAllReduce");
+    g_nccl.commDestroy = (decltype(g_nccl.commDestroy))dlsym(h, "ncclCommDestroy");
+    g_nccl.errorString = (decltype(g_nccl.errorString))dlsym(h, "ncclGetErrorString");
+    if (!g_nccl.getUniqueId || !g_nccl.commInitRank || !g_nccl.allReduce || !g_nccl.commDestroy ||
+        !g_nccl.errorString) {
+        set_last_error(ERR_NCCL, "libnccl.so.2 lacks an expected entry point");
+        return ERR_NCCL;
+    }
+    g_nccl.h = h;
+    return OK;
+}
+}  // namespace
+
+int dp_allreduce(ModelCtx *c, float *buf, size_t n, cudaStream_t s) {
+    if (c->world <= 1 || !c->nccl_comm) return OK;
+    ncclResult_t r = g_nccl.allReduce(buf, buf, n, ncclFloat, ncclAvg, (ncclComm_t)c->nccl_comm, s);
+    if (r != ncclSuccess) {
+        set_last_error(ERR_NCCL, "ncclAllReduce: %s", g_nccl.errorString(r));
+        return ERR_NCCL;
+    }
+    return OK;
+}
+
+}  // namespace cg
+
+using namespace cg;
+
+extern "C" int cngpt_cuda_dp_unique_id(unsigned char id[128]) {
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+    CG_TRY(nccl_open());
+    ncclUniqueId uid;
+    ncclResult_t r = g_nccl.getUniqueId(&uid);
+    if (r != ncclSuccess) {
+        set_last_error(ERR_NCCL, "ncclGetUniqueId: %s", g_nccl.errorString(r));
+        return ERR_NCCL;
+    }
+    memcpy(id, &uid, 128);
+    return OK;
+}
+
+extern "C" int cngpt_cuda_dp_init(GPT *m, const unsigned char id[128], int world, int rank) {
+    ModelCtx *c = model_ctx(m);
+    if (!c) return ERR_STATE;
+    if (world < 1 || rank < 0 || rank >= world) {
+        set_last_error(ERR_ARG, "dp_init: rank %d / world %d", rank, world);
+        return ERR_ARG;
+    }
+    if (world == 1) {
+        c->world = 1;
+        c->rank = 0;
+        return OK;
+    }
+    CG_TRY(nccl_open());
+    ncclUniqueId uid;
+    memcpy(&uid, id, 128);
+    ncclComm_t comm;
+    ncclResult_t r = g_nccl.commInitRank(&comm, world, uid, rank);
+    if (r != ncclSuccess) {
+        set_last_error(ERR_NCCL, "ncclCommInitRank: %s", g_nccl.errorString(r));
+        return ERR_NCCL;
+    }
+    c->nccl_comm = comm;
+    c->world = world;
+    c->rank = rank;
+    return OK;
+}
+
+extern "C" int cngpt_cuda_dp_allreduce_grads(GPT *m) {
+    ModelCtx *c = model_ctx(m);
+    if (!c) return ERR_STATE;
+    return dp_allreduce(c, m->grad_buf, (size_t)m->n_params, g_stream);
+}
+
+extern "C" int cngpt_cuda_dp_free(GPT *m) {
+    ModelCtx *c = model_ctx(m);
+    if (!c) return ERR_STATE;
+    if (c->nccl_comm) {
+        cudaStreamSynchronize(g_stream);
+        g_nccl.commDestroy((ncclComm_t)c->nccl_comm);
+        c->nccl_comm = nullptr;
+    }
+    c->world = 1;
+    c->rank = 0;
+    return OK;
+}

@@ -1,0 +1,325 @@
+// fast_abi.cu - cngpt/fast.h on the device, plus greedy decode with a KV cache.
+//
+// gpt_forward_fast follows src/fast.c:227-333: scratch sized once per (B, T)
+// and reused, attention straight from the packed qkv rows, the last layer
+// continued past attention for the final position of each sequence only,
+// residual adds folded into the projection epilogues (x += ...), GELU fused
+// into the fc epilogue, and the LM head for the final positions only.
+//
+// cngpt_cuda_generate adds what the reference does not have (it recomputes
+// the whole prefix for every token, src/model.c:1001-1015): the prefill
+// stores K and V of every layer, then each step runs one row per sequence
+// through the stack with single-query attention over the cache, and takes the
+// argmax of the last-position logits (lowest index on ties).
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "abi_common.h"
+#include "kernels.h"
+#include "model_ctx.h"
+
+extern "C" {
+#include "cngpt_cuda.h"
+}
+
+namespace cg {
+void fast_forget(const FastCtx *f);
+
+namespace {
+
+int fast_resize(FastCtx *f, FastDev *d, const GPT *m, int B, int T, bool managed) {
+    if (f->x && f->B == B && f->T == T) return OK;
+    cudaStreamSynchronize(g_stream);
+    float **bufs[] = {&f->x, &f->ln, &f->qkv, &f->aout, &f->hid, &f->mean, &f->rstd, &f->logits,
+                      &d->xl, &d->al};
+    for (auto b : bufs) {
+        dev_free(*b);
+        *b = nullptr;
+    }
+    f->scores = nullptr;  // the fused attention never forms T x T scores
+    const size_t C = m->cfg.n_embd, V = m->cfg.vocab_size, N = (size_t)B * T;
+    CG_TRY(dev_alloc((void **)&f->x, N * C * 4, managed));
+    CG_TRY(dev_alloc((void **)&f->ln, N * C * 4, managed));
+    CG_TRY(dev_alloc((void **)&f->qkv, N * 3 * C * 4, managed));
+    CG_TRY(dev_alloc((void **)&f->aout, N * C * 4, managed));
+    CG_TRY(dev_alloc((void **)&f->hid, N * 4 * C * 4, managed));
+    CG_TRY(dev_alloc((void **)&f->mean, N * 4, managed));
+    CG_TRY(dev_alloc((void **)&f->rstd, N * 4, managed));
+    CG_TRY(dev_alloc((void **)&f->logits, (size_t)B * V * 4, managed));
+    CG_TRY(dev_alloc((void **)&d->xl, (size_t)B * C * 4, false));
+    CG_TRY(dev_alloc((void **)&d->al, (size_t)B * C * 4, false));
+    f->B = B;
+    f->T = T;
+    return OK;
+}
+
+GemmEpi epi_store(float *D, long ldd, const float *bias) {
+    GemmEpi e;
+    e.mode = EPI_STORE;
+    e.D = D;
+    e.ldd = ldd;
+    e.bias = bias;
+    return e;
+}
+
+// x += A W^T + b  (src/fast.c:314-315, 322-323 with accumulate = 1)
+GemmEpi epi_resid_inplace(float *x, long ld, const float *bias) {
+    GemmEpi e;
+    e.mode = EPI_RESID;
+    e.bias = bias;
+    e.D2 = x;
+    e.ldd2 = ld;
+    e.R = x;
+    e.ldr = ld;
+    return e;
+}
+
+GemmEpi epi_gelu_only(float *out, long ld, const float *bias) {
+    GemmEpi e;
+    e.mode = EPI_GELU;
+    e.bias = bias;
+    e.D2 = out;
+    e.ldd2 = ld;
+    return e;
+}
+
+// One transformer block for `rows` rows of x (post-attention part).
+int block_tail(const GPT *m, int l, FastCtx *f, float *x, const float *aout, int rows, cudaStream_t s) {
+    const int C = m->cfg.n_embd;
+    const GPTWeights *w = &m->params;
+    CG_TRY(gemm(aout, C, false, w->c_proj_w[l], C, false, rows, C, C,
+                epi_resid_inplace(x, C, w->c_proj_b[l]), s));
+    CG_TRY(layernorm_fwd(x, C, w->ln2_w[l], w->ln2_b[l], f->ln, C, f->mean, f->rstd, rows, C, s));
+    CG_TRY(gemm(f->ln, C, false, w->mlp_fc_w[l], C, false, rows, 4 * C, C,
+                epi_gelu_only(f->hid, 4 * C, w->mlp_fc_b[l]), s));
+    CG_TRY(gemm(f->hid, 4 * C, false, w->mlp_proj_w[l], 4 * C, false, rows, C, 4 * C,
+                epi_resid_inplace(x, C, w->mlp_proj_b[l]), s));
+    return OK;
+}
+
+// Full-prefix forward; if kv is given, K/V of every layer are stored at
+// positions [0, T). Leaves the final-position logits in f->logits.
+int fast_forward(const GPT *m, FastCtx *f, FastDev *d, const int *tok, int B, int T, bool store_kv,
+                 cudaStream_t s) {
+    const int C = m->cfg.n_embd, V = m->cfg.vocab_size, L = m->cfg.n_layer, H = m->cfg.n_head;
+    const int BT = B * T;
+    const GPTWeights *w = &m->params;
+    CG_TRY(embed_fwd(tok, w->wte, w->wpe, f->x, BT, T, C, 0, s));
+    for (int l = 0; l < L; l++) {
+        const bool last = (l == L - 1);
+        CG_TRY(layernorm_fwd(f->x, C, w->ln1_w[l], w->ln1_b[l], f->ln, C, f->mean, f->rstd, BT, C, s));
+        CG_TRY(gemm(f->ln, C, false, w->c_attn_w[l], C, false, BT, 3 * C, C,
+                    epi_store(f->qkv, 3 * C, w->c_attn_b[l]), s));
+        if (store_kv) {
+            const size_t per = (size_t)d->kv_B * d->kv_T * C;
+            CG_TRY(kv_append(f->qkv, d->kc + l * per, d->vc + l * per, B, T, d->kv_T, 0, C, s));
+        }
+        if (!last) {
+            CG_TRY(attention_fwd(f->qkv, f->aout, nullptr, B, T, C, H, s));
+            CG_TRY(block_tail(m, l, f, f->x, f->aout, BT, s));
+        } else {
+            // only the final query row of each sequence (src/fast.c:287-311)
+            CG_TRY(attention_fwd_rows(f->qkv, f->aout, B, T, C, H, T - 1, s));
+            CG_TRY(gather_last(f->aout, d->al, B, T, C, s));
+            CG_TRY(gather_last(f->x, d->xl, B, T, C, s));
+            CG_TRY(block_tail(m, l, f, d->xl, d->al, B, s));
+        }
+    }
+    const float *xf = L > 0 ? d->xl : f->x;
+    if (L == 0) {
+        CG_TRY(gather_last(f->x, d->xl, B, T, C, s));
+        xf = d->xl;
+    }
+    CG_TRY(layernorm_fwd(xf, C, w->ln_f_w, w->ln_f_b, f->ln, C, f->mean, f->rstd, B, C, s));
+    CG_TRY(gemm(f->ln, C, false, w->wte, C, false, B, V, C, epi_store(f->logits, V, nullptr), s));
+    return OK;
+}
+
+// One decode step: tokens tok[B] at position pos; K/V appended at pos.
+int decode_step(const GPT *m, FastCtx *f, FastDev *d, const int *tok, int B, int pos, cudaStream_t s) {
+    const int C = m->cfg.n_embd, V = m->cfg.vocab_size, L = m->cfg.n_layer, H = m->cfg.n_head;
+    const GPTWeights *w = &m->params;
+    float *x = d->xl;
+    CG_TRY(embed_fwd(tok, w->wte, w->wpe, x, B, 1, C, pos, s));
+    const size_t per = (size_t)d->kv_B * d->kv_T * C;
+    for (int l = 0; l < L; l++) {
+        CG_TRY(layernorm_fwd(x, C, w->ln1_w[l], w->ln1_b[l], f->ln, C, f->mean, f->rstd, B, C, s));
+        CG_TRY(gemm(f->ln, C, false, w->c_attn_w[l], C, false, B, 3 * C, C,
+                    epi_store(f->qkv, 3 * C, w->c_attn_b[l]), s));
+        CG_TRY(kv_append(f->qkv, d->kc + l * per, d->vc + l * per, B, 1, d->kv_T, pos, C, s));
+        CG_TRY(attention_decode(f->qkv, 3L * C, d->kc + l * per, d->vc + l * per, d->kv_T, pos + 1,
+                                d->al, B, C, H, s));
+        CG_TRY(block_tail(m, l, f, x, d->al, B, s));
+    }
+    CG_TRY(layernorm_fwd(x, C, w->ln_f_w, w->ln_f_b, f->ln, C, f->mean, f->rstd, B, C, s));
+    CG_TRY(gemm(f->ln, C, false, w->wte, C, false, B, V, C, epi_store(f->logits, V, nullptr), s));
+    return OK;
+}
+
+}  // namespace
+}  // namespace cg
+
+using namespace cg;
+
+extern "C" void fast_init(FastCtx *f) {
+    fast_forget(f);
+    memset(f, 0, sizeof(*f));
+}
+
+extern "C" void fast_free(FastCtx *f) {
+    cudaStreamSynchronize(g_stream);
+    float *bufs[] = {f->x, f->ln, f->qkv, f->aout, f->hid, f->mean, f->rstd, f->logits};
+    for (auto b : bufs) dev_free(b);
+    FastDev *d = fast_dev(f, false);
+    if (d) {
+        dev_free(d->xl);
+        dev_free(d->al);
+        dev_free(d->tok);
+        dev_free(d->kc);
+        dev_free(d->vc);
+        dev_free(d->next);
+        dev_free(d->gen);
+        fast_forget(f);
+    }
+    memset(f, 0, sizeof(*f));
+}
+
+extern "C" void fast_set_threads(int n) { (void)n; }
+
+extern "C" const float *gpt_forward_fast(GPT *m, FastCtx *f, const int *tokens, int B, int T) {
+    ModelCtx *c = model_ctx(m);
+    if (!c) return nullptr;
+    if (B <= 0 || T <= 0 || T > m->cfg.block_size) {
+        set_last_error(ERR_ARG, "gpt_forward_fast: bad shape B=%d T=%d", B, T);
+        return nullptr;
+    }
+    FastDev *d = fast_dev(f, true);
+    if (fast_resize(f, d, m, B, T, c->managed) != OK) return nullptr;
+    const int *tok = nullptr;
+    if (stage_tokens(tokens, (size_t)B * T, &d->tok, &d->tok_cap, &tok, g_stream) != OK) return nullptr;
+    if (fast_forward(m, f, d, tok, B, T, false, g_stream) != OK) {
+        fprintf(stderr, "gpt_forward_fast: %s\n", last_message());
+        return nullptr;
+    }
+    if (c->managed) cudaStreamSynchronize(g_stream);
+    return f->logits;
+}
+
+extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B, int T, int n_new,
+                                   int *out_tokens) {
+    ModelCtx *c = model_ctx(m);
+    if (!c) return ERR_STATE;
+    if (B <= 0 || T <= 0 || n_new <= 0 || T + n_new - 1 > m->cfg.block_size) {
+        set_last_error(ERR_ARG, "generate: B=%d T=%d n_new=%d exceeds block_size %d", B, T, n_new,
+                       m->cfg.block_size);
+        return ERR_ARG;
+    }
+    cudaStream_t s = g_stream;
+    FastDev *d = fast_dev(f, true);
+    CG_TRY(fast_resize(f, d, m, B, T, c->managed));
+    const int Tmax = T + n_new;
+    const size_t C = m->cfg.n_embd, L = m->cfg.n_layer, V = m->cfg.vocab_size;
+    if (d->kv_B != B || d->kv_T < Tmax) {
+        CG_CUDA(cudaStreamSynchronize(s));
+        dev_free(d->kc);
+        dev_free(d->vc);
+        dev_free(d->next);
+        d->kc = d->vc = nullptr;
+        d->next = nullptr;
+        CG_TRY(dev_alloc((void **)&d->kc, L * B * Tmax * C * 4, false));
+        CG_TRY(dev_alloc((void **)&d->vc, L * B * Tmax * C * 4, false));
+        CG_TRY(dev_alloc((void **)&d->next, (size_t)B * 4, false));
+        d->kv_B = B;
+        d->kv_T = Tmax;
+    }
+    if ((size_t)B * n_new > d->gen_cap) {
+        dev_free(d->gen);
+        d->gen = nullptr;
+        CG_TRY(dev_alloc((void **)&d->gen, (size_t)B * n_new * 4, false));
+        d->gen_cap = (size_t)B * n_new;
+    }
+    const int *tok = nullptr;
+    CG_TRY(stage_tokens(prompt, (size_t)B * T, &d->tok, &d->tok_cap, &tok, s));
+    CG_TRY(fast_forward(m, f, d, tok, B, T, true, s));
+    // gen is laid out [step][B]; transposed to [B][step] on the host
+    CG_TRY(argmax_rows(f->logits, V, B, (int)V, d->gen, nullptr, s));
+    for (int i = 1; i < n_new; ++i) {
+        CG_TRY(decode_step(m, f, d, d->gen + (size_t)(i - 1) * B, B, T + i - 1, s));
+        CG_TRY(argmax_rows(f->logits, V, B, (int)V, d->gen + (size_t)i * B, nullptr, s));
+    }
+    std::vector<int> h((size_t)B * n_new);
+    CG_CUDA(cudaMemcpyAsync(h.data(), d->gen, h.size() * 4, cudaMemcpyDeviceToHost, s));
+    CG_CUDA(cudaStreamSynchronize(s));
+    CG_TRY(check_device_error());
+    for (int b = 0; b < B; ++b)
+        for (int i = 0; i < n_new; ++i) out_tokens[(size_t)b * n_new + i] = h[(size_t)i * B + b];
+    return OK;
+}
+
+// ---------------------------------------------------------------- gpt_sample
+// Temperature / top-k sampling with the host rand() stream, the same steps as
+// src/model.c:927-989; logits come from the device fast forward (the final
+// position of the cropped context, src/model.c:1001-1011).
+namespace {
+int sample_top_k(const float *logits, int V, float temp, int top_k) {
+    std::vector<float> sc((size_t)V);
+    for (int i = 0; i < V; i++) sc[i] = logits[i] / (temp > 0.0f ? temp : 1.0f);
+    float mx = sc[0];
+    for (int i = 1; i < V; i++)
+        if (sc[i] > mx) mx = sc[i];
+    float sum = 0.0f;
+    for (int i = 0; i < V; i++) {
+        sc[i] = expf(sc[i] - mx);
+        sum += sc[i];
+    }
+    for (int i = 0; i < V; i++) sc[i] /= sum;
+    if (top_k > 0 && top_k < V) {
+        std::vector<float> cp(sc);
+        for (int k = 0; k < top_k && k < V; k++)
+            for (int i = k + 1; i < V; i++)
+                if (cp[i] > cp[k]) std::swap(cp[i], cp[k]);
+        const float threshold = cp[top_k - 1];
+        float ns = 0.0f;
+        for (int i = 0; i < V; i++) {
+            if (sc[i] < threshold) sc[i] = 0.0f;
+            ns += sc[i];
+        }
+        if (ns > 0.0f)
+            for (int i = 0; i < V; i++) sc[i] /= ns;
+    }
+    const float r = (float)rand() / ((float)RAND_MAX + 1.0f);
+    float cdf = 0.0f;
+    int tok = V - 1;
+    for (int i = 0; i < V; i++) {
+        cdf += sc[i];
+        if (r < cdf) {
+            tok = i;
+            break;
+        }
+    }
+    return tok;
+}
+}  // namespace
+
+extern "C" void gpt_sample(GPT *m, const int *prompt_tokens, int prompt_len, int *out_tokens,
+                           int max_new_tokens, float temp, int top_k) {
+    const int block = m->cfg.block_size, V = m->cfg.vocab_size;
+    memcpy(out_tokens, prompt_tokens, (size_t)prompt_len * sizeof(int));
+    FastCtx f;
+    fast_init(&f);
+    std::vector<float> lg((size_t)V);
+    for (int i = 0; i < max_new_tokens; i++) {
+        const int total = prompt_len + i;
+        const int start = total > block ? total - block : 0;
+        const float *d = gpt_forward_fast(m, &f, out_tokens + start, 1, total - start);
+        if (!d || cudaMemcpy(lg.data(), d, (size_t)V * 4, cudaMemcpyDefault) != cudaSuccess) {
+            fprintf(stderr, "gpt_sample: forward failed: %s\n", last_message());
+            break;
+        }
+        out_tokens[total] = sample_top_k(lg.data(), V, temp, top_k);
+    }
+    fast_free(&f);
+}

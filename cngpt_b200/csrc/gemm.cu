@@ -1,0 +1,535 @@
+// gemm.cu - fp32-in / fp32-out GEMMs on the sm_100a tensor cores.
+//
+// One persistent, warp-specialised kernel covers every contraction of the
+// reference's linear layers (src/ops.c:109-149 and the call sites in
+// src/model.c / src/fast.c):
+//
+//   warp 0      TMA producer: 128B-swizzled tiles of A and B into a ring of
+//               shared-memory stages (plain per-CTA loads, no multicast)
+//   warp 1      MMA issuer: tcgen05.mma.kind::tf32, 128 x BN x 8 per
+//               instruction, accumulating into one of two TMEM buffers
+//   warps 2-5   epilogue: tcgen05.ld of the finished accumulator, then the
+//               fused bias / GELU / residual / accumulate / GELU-backward
+//               step and the global stores, overlapping the next tile's
+//               main loop (double-buffered TMEM)
+//   warps 6-9   (3xTF32 only) split transform: each staged fp32 tile x is
+//               rewritten as hi = rna_tf32(x) in place and lo = rna_tf32(x-hi)
+//               into a twin buffer, and the MMA warp issues lo*hi + hi*lo +
+//               hi*hi into a fresh accumulator per 32-wide k-block; the
+//               epilogue warps add those partials in fp32 registers. The
+//               tensor core accumulates with truncation, so its error grows
+//               with the number of accumulation steps (measured: ~7e-9*K
+//               normwise for one accumulator over K); per-k-block partials keep
+//               3xTF32 at fp32-level accuracy for any K
+//
+// Operands may be K-major or MN-major in global memory (the instruction
+// descriptor's transpose bits), so X W^T (forward), dY W (dX) and dY^T X (dW)
+// all load straight from their row-major buffers without a transpose pass.
+// Shapes or pointers TMA cannot describe (row pitch not a multiple of 16
+// bytes, unaligned base) run a CUDA-core fp32 kernel instead.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace cg {
+
+unsigned long long g_launch_count = 0;
+
+CG_DEV_ERROR_READER(gemm_take_dev_error)
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;              // fp32 elements per k-block = one 128B swizzle row
+constexpr int KB_BYTES = BK * 4;    // 128
+constexpr int MMA_K = 8;            // tf32 K per tcgen05.mma
+
+template <int BN, bool SPLIT>
+struct Cfg {
+    static constexpr int A_BYTES = BM * KB_BYTES;
+    static constexpr int B_BYTES = BN * KB_BYTES;
+    static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
+    static constexpr int STAGES = SPLIT ? 3 : (BN == 256 ? 4 : 6);
+    static constexpr int THREADS = SPLIT ? 320 : 192;
+    static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 4 * 32 * 33 * 4;
+};
+
+struct SmemCtl {
+    uint64_t full[8];
+    uint64_t empty[8];
+    uint64_t ready[8];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+
+// Fused epilogue for one output element (m, n) holding the raw product a.
+__device__ __forceinline__ void epi_apply(const GemmEpi &e, long m, int n, float a, float bias) {
+    a *= e.alpha;
+    switch (e.mode) {
+        case EPI_STORE:
+            e.D[m * e.ldd + n] = a + bias;
+            break;
+        case EPI_ACCUM: {
+            float *d = e.D + m * e.ldd + n;
+            *d = (*d + a) + bias;
+            break;
+        }
+        case EPI_GELU:
+            a += bias;
+            if (e.D) e.D[m * e.ldd + n] = a;
+            e.D2[m * e.ldd2 + n] = gelu_tanh(a);
+            break;
+        case EPI_RESID:
+            a += bias;
+            if (e.D) e.D[m * e.ldd + n] = a;
+            e.D2[m * e.ldd2 + n] = e.R[m * e.ldr + n] + a;
+            break;
+        case EPI_GELU_BWD:
+            e.D[m * e.ldd + n] = a * gelu_tanh_grad(e.G[m * e.ldg + n]);
+            break;
+    }
+}
+
+template <int BN, bool A_MN, bool B_MN, bool SPLIT>
+__global__ void __launch_bounds__(Cfg<BN, SPLIT>::THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               int M, int N, int K, int tiles_m, int tiles_n, GemmEpi epi) {
+    using C = Cfg<BN, SPLIT>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    SmemCtl *ctl = (SmemCtl *)(base + C::STAGES * C::STAGE_BYTES);
+    auto sA = [&](int s) { return base + s * C::STAGE_BYTES; };
+    auto sB = [&](int s) { return base + s * C::STAGE_BYTES + C::A_BYTES; };
+    auto sAlo = [&](int s) { return base + s * C::STAGE_BYTES + C::A_BYTES + C::B_BYTES; };
+    auto sBlo = [&](int s) { return base + s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_tiles = tiles_m * tiles_n;
+    const int kblocks = (K + BK - 1) / BK;
+    volatile int *abort = &ctl->abort;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&ctl->full[s], 1);
+            mbar_init(&ctl->empty[s], 1);
+            mbar_init(&ctl->ready[s], 4);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ctl->tfull[b], 1);
+            mbar_init(&ctl->tempty[b], 4);
+        }
+        ctl->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(&ctl->tmem_base, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = ctl->tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int tm = tile % tiles_m, tn = tile / tiles_m;
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, DEV_ERR_GEMM_PRODUCER, abort))
+                        goto done;
+                    mbar_arrive_expect_tx(&ctl->full[stage], C::A_BYTES + C::B_BYTES);
+                    if (A_MN) {
+#pragma unroll
+                        for (int j = 0; j < BM / 32; ++j)
+                            tma_load_2d(sA(stage) + j * (BK * 128), &tmA, &ctl->full[stage],
+                                        tm * BM + j * 32, kb * BK);
+                    } else {
+                        tma_load_2d(sA(stage), &tmA, &ctl->full[stage], kb * BK, tm * BM);
+                    }
+                    if (B_MN) {
+#pragma unroll
+                        for (int j = 0; j < BN / 32; ++j)
+                            tma_load_2d(sB(stage) + j * (BK * 128), &tmB, &ctl->full[stage],
+                                        tn * BN + j * 32, kb * BK);
+                    } else {
+                        tma_load_2d(sB(stage), &tmB, &ctl->full[stage], kb * BK, tn * BN);
+                    }
+                    if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+            // K-major (128B swizzle): rows of 128B, 8-row atoms 1024B apart; a
+            // k-step of 8 elements advances the start address by 32B in the atom.
+            // MN-major (128B swizzle, 32B atoms): 32-element MN atoms 4096B apart
+            // (one TMA box of BK rows each), 4-row K groups 512B apart; a k-step
+            // of 8 rows advances by 1024B.
+            auto descA = [&](uint8_t *p, int kk) -> uint64_t {
+                return A_MN ? smem_desc(smem_u32(p) + kk * 1024, BK * 128, 512, 1)
+                            : smem_desc(smem_u32(p) + kk * 32, 16, 1024, 2);
+            };
+            auto descB = [&](uint8_t *p, int kk) -> uint64_t {
+                return B_MN ? smem_desc(smem_u32(p) + kk * 1024, BK * 128, 512, 1)
+                            : smem_desc(smem_u32(p) + kk * 32, 16, 1024, 2);
+            };
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                if constexpr (SPLIT) {
+                    // one fresh TMEM accumulator per k-block: the epilogue adds
+                    // the k-block partials in fp32 (round to nearest), which
+                    // bounds the tensor core's truncating accumulation to 12
+                    // steps per partial
+                    for (int kb = 0; kb < kblocks; ++kb) {
+                        if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, DEV_ERR_GEMM_MMA, abort))
+                            goto done;
+                        if (!mbar_wait(&ctl->ready[stage], phase, DEV_ERR_GEMM_MMA, abort)) goto done;
+                        tc_fence_after();
+                        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+#pragma unroll
+                        for (int kk = 0; kk < BK / MMA_K; ++kk) {
+                            const uint64_t a = descA(sA(stage), kk), b = descB(sB(stage), kk);
+                            mma_tf32(d_tmem, descA(sAlo(stage), kk), b, idesc, kk != 0);
+                            mma_tf32(d_tmem, a, descB(sBlo(stage), kk), idesc, 1);
+                            mma_tf32(d_tmem, a, b, idesc, 1);
+                        }
+                        mma_commit(&ctl->empty[stage]);
+                        mma_commit(&ctl->tfull[acc]);
+                        if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+                        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+                    }
+                } else {
+                    if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, DEV_ERR_GEMM_MMA, abort))
+                        goto done;
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                    for (int kb = 0; kb < kblocks; ++kb) {
+                        if (!mbar_wait(&ctl->full[stage], phase, DEV_ERR_GEMM_MMA, abort)) goto done;
+                        tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < BK / MMA_K; ++kk)
+                            mma_tf32(d_tmem, descA(sA(stage), kk), descB(sB(stage), kk), idesc,
+                                     (kb | kk) != 0);
+                        mma_commit(&ctl->empty[stage]);
+                        if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+                    }
+                    mma_commit(&ctl->tfull[acc]);
+                    if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+                }
+            }
+        }
+    } else if (warp < 6) {
+        // --------------------------------------------------- epilogue
+        // Each warp owns TMEM lanes [32q, 32q+32). A 32x32 block is read with one
+        // tcgen05.ld (thread = row), transposed through padded shared memory, and
+        // written back by rows so every global access of the warp is coalesced.
+        const int q = warp & 3;
+        float *stile = (float *)(base + C::STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        auto store_block = [&](const float (&v)[32], int m0, int n0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) stile[lane * 33 + j] = v[j];
+            __syncwarp();
+            const int n = n0 + lane;
+            if (n < N) {
+                const float b = epi.bias ? epi.bias[n] : 0.0f;
+                const int rows = min(32, M - m0);
+#pragma unroll 4
+                for (int r = 0; r < rows; ++r) epi_apply(epi, m0 + r, n, stile[r * 33 + lane], b);
+            }
+            __syncwarp();
+        };
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int tm = tile % tiles_m, tn = tile / tiles_m;
+            const int m0 = tm * BM + q * 32;
+            if constexpr (SPLIT) {
+                float sum[BN];
+#pragma unroll
+                for (int j = 0; j < BN; ++j) sum[j] = 0.0f;
+                bool ok = true;
+                for (int kb = 0; kb < kblocks && ok; ++kb) {
+                    if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < BN / 32; ++c) {
+                        float v[32];
+                        tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + c * 32) +
+                                               ((uint32_t)(q * 32) << 16), v);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) sum[c * 32 + j] += v[j];
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
+                    if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+                }
+                if (!ok) break;
+#pragma unroll
+                for (int c = 0; c < BN / 32; ++c) {
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = sum[c * 32 + j];
+                    store_block(v, m0, tn * BN + c * 32);
+                }
+            } else {
+                if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    float v[32];
+                    tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + c * 32) +
+                                           ((uint32_t)(q * 32) << 16), v);
+                    store_block(v, m0, tn * BN + c * 32);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+        }
+    } else if (SPLIT) {
+        // ---------------------------------------- 3xTF32 split transform
+        const int t = threadIdx.x - 192;  // 0..127
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(&ctl->full[stage], phase, DEV_ERR_GEMM_TRANSFORM, abort)) goto done;
+                float4 *hi = (float4 *)sA(stage);
+                float4 *lo = (float4 *)sAlo(stage);
+                constexpr int n4 = (C::A_BYTES + C::B_BYTES) / 16;
+                for (int i = t; i < n4; i += 128) {
+                    float4 x = hi[i], h, l;
+                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.x) : "f"(x.x));
+                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.y) : "f"(x.y));
+                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.z) : "f"(x.z));
+                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.w) : "f"(x.w));
+                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.x) : "f"(x.x - h.x));
+                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.y) : "f"(x.y - h.y));
+                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.z) : "f"(x.z - h.z));
+                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.w) : "f"(x.w - h.w));
+                    hi[i] = h;
+                    lo[i] = l;
+                }
+                // generic-proxy smem writes -> visible to the tensor core (async proxy)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->ready[stage]);
+                if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------ CUDA-core fp32 fallback
+// 64x64 output tile per 256-thread block, 4x4 outputs per thread, fp32 FMA.
+__global__ void __launch_bounds__(256)
+gemm_simt_kernel(const float *__restrict__ A, long lda, int a_mn, const float *__restrict__ B,
+                 long ldb, int b_mn, int M, int N, int K, GemmEpi epi) {
+    __shared__ float As[16][64 + 4];
+    __shared__ float Bs[16][64 + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+            int kk = i / 64, r = i % 64;
+            int m = m0 + r, n = n0 + r, k = k0 + kk;
+            float a = 0.f, b = 0.f;
+            if (m < M && k < K) a = a_mn ? A[(long)k * lda + m] : A[(long)m * lda + k];
+            if (n < N && k < K) b = b_mn ? B[(long)k * ldb + n] : B[(long)n * ldb + k];
+            As[kk][r] = a;
+            Bs[kk][r] = b;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + tx * 4 + j;
+            if (n < N) epi_apply(epi, m, n, acc[i][j], epi.bias ? epi.bias[n] : 0.0f);
+        }
+    }
+}
+
+// ------------------------------------------------------- tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::mutex g_mu;
+
+int get_encoder() {
+    if (g_encode) return OK;
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        set_last_error(ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        return ERR_CUDA;
+    }
+    g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    return OK;
+}
+
+struct MapKey {
+    const void *p;
+    long inner, outer, ld;
+    int box0, box1;
+    bool operator==(const MapKey &o) const {
+        return p == o.p && inner == o.inner && outer == o.outer && ld == o.ld && box0 == o.box0 &&
+               box1 == o.box1;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        size_t h = std::hash<const void *>()(k.p);
+        h ^= std::hash<long>()(k.inner * 1315423911L + k.outer * 2654435761L + k.ld) + 0x9e3779b9 +
+             (h << 6) + (h >> 2);
+        h ^= (size_t)k.box0 * 31 + (size_t)k.box1;
+        return h;
+    }
+};
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+// 2-D fp32 tensor map: dim0 (contiguous) of extent `inner`, dim1 of extent
+// `outer` with a pitch of `ld` elements; OOB reads fill zero. K-major
+// operands use the 128B swizzle, MN-major ones the 128B swizzle with 32B
+// atoms (the layout tcgen05 requires for MN-major tf32).
+int make_map(CUtensorMap *out, const float *p, long inner, long outer, long ld, int box0,
+             int box1, bool mn_major) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    MapKey key{p, inner, outer, ld, box0, box1 | (mn_major ? 0x10000 : 0)};
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+        *out = it->second;
+        return OK;
+    }
+    CG_TRY(get_encoder());
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    cuuint32_t box[2] = {(cuuint32_t)box0, (cuuint32_t)box1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)p, dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_last_error(ERR_ARG, "cuTensorMapEncodeTiled failed (%d) inner=%ld outer=%ld ld=%ld",
+                       (int)r, inner, outer, ld);
+        return ERR_ARG;
+    }
+    if (g_maps.size() > 8192) g_maps.clear();
+    g_maps.emplace(key, *out);
+    return OK;
+}
+
+template <int BN, bool A_MN, bool B_MN, bool SPLIT>
+int launch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, int K,
+              const GemmEpi &epi, cudaStream_t s) {
+    using C = Cfg<BN, SPLIT>;
+    static bool attr_set = false;
+    auto kern = gemm_tc_kernel<BN, A_MN, B_MN, SPLIT>;
+    if (!attr_set) {
+        CG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_set = true;
+    }
+    CUtensorMap ta, tb;
+    if (A_MN) CG_TRY(make_map(&ta, A, M, K, lda, 32, BK, true));
+    else      CG_TRY(make_map(&ta, A, K, M, lda, BK, BM, false));
+    if (B_MN) CG_TRY(make_map(&tb, B, N, K, ldb, 32, BK, true));
+    else      CG_TRY(make_map(&tb, B, K, N, ldb, BK, BN, false));
+    const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+    const int tiles = tiles_m * tiles_n;
+    const int grid = std::min(tiles, num_sms());
+    kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, epi);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    return OK;
+}
+
+template <bool A_MN, bool B_MN>
+int dispatch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, int K,
+                const GemmEpi &epi, cudaStream_t s, bool split) {
+    if (split) return launch_tc<128, A_MN, B_MN, true>(A, lda, B, ldb, M, N, K, epi, s);
+    // wide tiles when there are enough of them to fill the machine
+    const long tiles256 = (long)((M + BM - 1) / BM) * ((N + 255) / 256);
+    if (N > 128 && tiles256 >= num_sms())
+        return launch_tc<256, A_MN, B_MN, false>(A, lda, B, ldb, M, N, K, epi, s);
+    return launch_tc<128, A_MN, B_MN, false>(A, lda, B, ldb, M, N, K, epi, s);
+}
+
+bool tma_ok(const float *p, long ld) {
+    return ((uintptr_t)p % 16) == 0 && (ld % 4) == 0 && ld > 0;
+}
+
+}  // namespace
+
+int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_mn, int M, int N,
+         int K, const GemmEpi &epi, cudaStream_t s) {
+    if (M < 0 || N < 0 || K < 0) {
+        set_last_error(ERR_ARG, "gemm: negative shape M=%d N=%d K=%d", M, N, K);
+        return ERR_ARG;
+    }
+    if (M == 0 || N == 0) return OK;
+    const int prec = precision();
+    const bool big = (long)M * N * (long)std::max(K, 1) >= (1L << 18) && K > 0;
+    const bool tc = prec != PREC_FP32 && big && tma_ok(A, lda) && tma_ok(B, ldb) &&
+                    (a_mn ? lda >= M : lda >= K) && (b_mn ? ldb >= N : ldb >= K);
+    if (tc) {
+        const bool split = prec == PREC_3XTF32;
+        if (!a_mn && !b_mn) return dispatch_tc<false, false>(A, lda, B, ldb, M, N, K, epi, s, split);
+        if (!a_mn && b_mn) return dispatch_tc<false, true>(A, lda, B, ldb, M, N, K, epi, s, split);
+        if (a_mn && b_mn) return dispatch_tc<true, true>(A, lda, B, ldb, M, N, K, epi, s, split);
+        return dispatch_tc<true, false>(A, lda, B, ldb, M, N, K, epi, s, split);
+    }
+    dim3 grid((N + 63) / 64, (M + 63) / 64);
+    gemm_simt_kernel<<<grid, 256, 0, s>>>(A, lda, a_mn, B, ldb, b_mn, M, N, K, epi);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    return OK;
+}
+
+}  // namespace cg

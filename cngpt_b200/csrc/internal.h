@@ -1,0 +1,92 @@
+// internal.h - host-side internal API of libcngpt_cuda (not exported).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstdio>
+
+namespace cg {
+
+// ---------------------------------------------------------------- errors
+// Library status codes (mirrored in include/cngpt_cuda.h).
+enum Status : int {
+    OK = 0,
+    ERR_CUDA = 1,        // a CUDA runtime call failed
+    ERR_ARG = 2,         // invalid shape / pointer / alignment
+    ERR_ALLOC = 3,       // device allocation failed
+    ERR_DEVICE_WAIT = 4, // a bounded device-side wait gave up (see dev error code)
+    ERR_NCCL = 5,        // a collective failed
+    ERR_STATE = 6,       // call order / unknown model handle
+};
+
+// Device wait sites, recorded in the device error word.
+enum DevError : int {
+    DEV_ERR_GEMM_PRODUCER = 101,
+    DEV_ERR_GEMM_MMA = 102,
+    DEV_ERR_GEMM_EPILOGUE = 103,
+    DEV_ERR_GEMM_TRANSFORM = 104,
+};
+
+void set_last_error(int status, const char *fmt, ...);
+int last_status();
+const char *last_message();
+int check_device_error();  // reads and clears the device error words
+int gemm_take_dev_error();
+int attn_take_dev_error();
+
+#define CG_CUDA(call)                                                                 \
+    do {                                                                              \
+        cudaError_t e_ = (call);                                                      \
+        if (e_ != cudaSuccess) {                                                      \
+            ::cg::set_last_error(::cg::ERR_CUDA, "%s:%d %s: %s", __FILE__, __LINE__,  \
+                                 #call, cudaGetErrorString(e_));                      \
+            return ::cg::ERR_CUDA;                                                    \
+        }                                                                             \
+    } while (0)
+
+#define CG_TRY(call)                     \
+    do {                                 \
+        int s_ = (call);                 \
+        if (s_ != ::cg::OK) return s_;   \
+    } while (0)
+
+// ------------------------------------------------------------- precision
+enum Precision : int { PREC_TF32 = 0, PREC_3XTF32 = 1, PREC_FP32 = 2 };
+int precision();
+void set_precision(int p);
+
+// ------------------------------------------------------------------ GEMM
+enum EpiMode : int {
+    EPI_STORE = 0,     // D = alpha*acc + bias
+    EPI_ACCUM = 1,     // D = D + alpha*acc (+ bias)
+    EPI_GELU = 2,      // t = acc + bias; D = t (if D); D2 = gelu(t)
+    EPI_RESID = 3,     // t = acc + bias; D = t (if D); D2 = R + t
+    EPI_GELU_BWD = 4,  // D = acc * gelu'(G)
+};
+
+struct GemmEpi {
+    int mode = EPI_STORE;
+    float alpha = 1.0f;
+    float *D = nullptr;
+    long ldd = 0;
+    const float *bias = nullptr;
+    float *D2 = nullptr;
+    long ldd2 = 0;
+    const float *R = nullptr;
+    long ldr = 0;
+    const float *G = nullptr;
+    long ldg = 0;
+};
+
+// out[M,N] = op(A)[M,K] * op(B)[N,K]^T, with the epilogue applied per element.
+// A element (m,k) is A[m*lda+k] (a_mn=false, K-major) or A[k*lda+m] (a_mn=true).
+// B element (n,k) is B[n*ldb+k] (b_mn=false, K-major) or B[k*ldb+n] (b_mn=true).
+int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_mn,
+         int M, int N, int K, const GemmEpi &epi, cudaStream_t s);
+
+// Counts of kernel launches issued by this library (for benchmarks).
+extern unsigned long long g_launch_count;
+
+int num_sms();
+
+}  // namespace cg

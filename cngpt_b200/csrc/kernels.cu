@@ -1,0 +1,705 @@
+// kernels.cu - the non-GEMM device kernels of the hot path.
+//
+// All reductions have a fixed order (per-thread sequential sums, fixed-shape
+// tree or partial-buffer reductions), so every kernel here is bit-for-bit
+// deterministic run to run; no floating-point atomics are used.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cg {
+
+namespace {
+
+inline int grid_for(long n, int threads, int cap = 148 * 16) {
+    long g = (n + threads - 1) / threads;
+    return (int)std::max(1L, std::min(g, (long)cap));
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// One warp per row; eps 1e-5; biased variance; two passes over the row as in
+// src/ops.c:231-247 (mean first, then the sum of squared deviations).
+__global__ void layernorm_fwd_kernel(const float *__restrict__ x, long ldx,
+                                     const float *__restrict__ w, const float *__restrict__ b,
+                                     float *__restrict__ out, long ldo, float *__restrict__ mean,
+                                     float *__restrict__ rstd, int T, int C) {
+    const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    for (long t = (long)blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += (long)gridDim.x * warps) {
+        const float *xr = x + t * ldx;
+        float s = 0.f;
+        for (int c = lane; c < C; c += 32) s += xr[c];
+        const float m = warp_sum(s) / (float)C;
+        float v = 0.f;
+        for (int c = lane; c < C; c += 32) {
+            float d = xr[c] - m;
+            v += d * d;
+        }
+        const float rs = 1.0f / sqrtf(warp_sum(v) / (float)C + 1e-5f);
+        if (lane == 0) {
+            if (mean) mean[t] = m;
+            if (rstd) rstd[t] = rs;
+        }
+        float *orow = out + t * ldo;
+        for (int c = lane; c < C; c += 32) orow[c] = (xr[c] - m) * rs * w[c] + b[c];
+    }
+}
+
+// dx += rstd (dn - mean(dn) - xhat mean(dn xhat)) per row (src/ops.c:305-329);
+// dw/db column partials per block in registers, written to `part`
+// [gridDim.x][2][C]; layernorm_bwd_reduce adds them to dw/db in block order.
+template <int CPL>  // columns per lane (ceil(C/32))
+__global__ void __launch_bounds__(256)
+layernorm_bwd_kernel(const float *__restrict__ dout, const float *__restrict__ x,
+                     const float *__restrict__ w, const float *__restrict__ mean,
+                     const float *__restrict__ rstd, float *__restrict__ dx,
+                     float *__restrict__ part, int T, int C, int rows_per_block) {
+    __shared__ float red[2][32 * CPL];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float pdw[CPL], pdb[CPL];
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) pdw[i] = pdb[i] = 0.f;
+    const long r0 = (long)blockIdx.x * rows_per_block;
+    const long r1 = std::min<long>(T, r0 + rows_per_block);
+    for (long t = r0 + wid; t < r1; t += 8) {
+        const float *dr = dout + t * C, *xr = x + t * C;
+        const float m = mean[t], rs = rstd[t];
+        float xh[CPL], dn[CPL], s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < C) {
+                xh[i] = (xr[c] - m) * rs;
+                dn[i] = dr[c] * w[c];
+                s1 += dn[i];
+                s2 += dn[i] * xh[i];
+                pdw[i] += dr[c] * xh[i];
+                pdb[i] += dr[c];
+            }
+        }
+        s1 = warp_sum(s1) / (float)C;
+        s2 = warp_sum(s2) / (float)C;
+        float *dxr = dx + t * C;
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < C) dxr[c] += rs * (dn[i] - s1 - xh[i] * s2);
+        }
+    }
+    // warps add their column partials into shared memory one after another
+    // (fixed order), then the block's partial goes to `part`
+    for (int k = 0; k < 8; ++k) {
+        if (wid == k) {
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                red[0][lane + 32 * i] = k == 0 ? pdw[i] : red[0][lane + 32 * i] + pdw[i];
+                red[1][lane + 32 * i] = k == 0 ? pdb[i] : red[1][lane + 32 * i] + pdb[i];
+            }
+        }
+        __syncthreads();
+    }
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        part[((long)blockIdx.x * 2 + 0) * C + c] = red[0][c];
+        part[((long)blockIdx.x * 2 + 1) * C + c] = red[1][c];
+    }
+}
+
+__global__ void layernorm_bwd_reduce(const float *__restrict__ part, int nblocks, int C,
+                                     float *__restrict__ dw, float *__restrict__ db) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    float a = 0.f, b = 0.f;
+    for (int k = 0; k < nblocks; ++k) {
+        a += part[((long)k * 2 + 0) * C + c];
+        b += part[((long)k * 2 + 1) * C + c];
+    }
+    dw[c] += a;
+    db[c] += b;
+}
+
+// ---------------------------------------------------------------- GELU
+__global__ void gelu_fwd_kernel(const float *__restrict__ x, float *__restrict__ out, long n) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        out[i] = gelu_tanh(x[i]);
+}
+
+__global__ void gelu_bwd_kernel(const float *__restrict__ dout, const float *__restrict__ x,
+                                float *__restrict__ dx, long n) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        dx[i] += dout[i] * gelu_tanh_grad(x[i]);
+}
+
+// ---------------------------------------------------------------- softmax
+// One block per row: max, sum of exp, normalise (src/ops.c:464-480).
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float *sh) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = is_max ? warp_max(v) : warp_sum(v);
+    __syncthreads();
+    if (lane == 0) sh[wid] = v;
+    __syncthreads();
+    float r = lane < nw ? sh[lane] : (is_max ? -INFINITY : 0.f);
+    r = is_max ? warp_max(r) : warp_sum(r);
+    return r;
+}
+
+__global__ void softmax_rows_kernel(float *__restrict__ x, int cols) {
+    __shared__ float sh[32];
+    float *row = x + (long)blockIdx.x * cols;
+    float mx = -INFINITY;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) mx = fmaxf(mx, row[c]);
+    mx = block_reduce(mx, true, sh);
+    float s = 0.f;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        float e = expf(row[c] - mx);
+        row[c] = e;
+        s += e;
+    }
+    s = block_reduce(s, false, sh);
+    const float inv = 1.0f / s;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) row[c] *= inv;
+}
+
+__global__ void causal_mask_kernel(float *__restrict__ s, int T) {
+    const long n = (long)T * T;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const long r = i / T, c = i % T;
+        if (c > r) s[i] = -1e9f;
+    }
+}
+
+// ---------------------------------------------------------------- cross-entropy
+// One block per row of logits [rows, V] (pitch ldl). Writes probs (optional,
+// pitch ldp), dlogits = scale * (probs - onehot) (optional, pitch ldd; the
+// pad columns [V, ldd) are zeroed) and the row's NLL term
+// (l[tgt] - max) - log(sum) to rowterm[row] (src/ops.c:551-570).
+__global__ void __launch_bounds__(512)
+ce_fwd_kernel(const float *__restrict__ logits, long ldl, const int *__restrict__ targets,
+              float *__restrict__ probs, long ldp, float *__restrict__ dlogits, long ldd,
+              float scale, float *__restrict__ rowterm, int V) {
+    __shared__ float sh[32];
+    const long r = blockIdx.x;
+    const float *lg = logits + r * ldl;
+    float mx = -INFINITY;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) mx = fmaxf(mx, lg[v]);
+    mx = block_reduce(mx, true, sh);
+    float s = 0.f;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) s += expf(lg[v] - mx);
+    s = block_reduce(s, false, sh);
+    const float inv = 1.0f / s;
+    const int tgt = targets ? targets[r] : -1;
+    if (probs || dlogits) {
+        float *pr = probs ? probs + r * ldp : nullptr;
+        float *dl = dlogits ? dlogits + r * ldd : nullptr;
+        for (int v = threadIdx.x; v < V; v += blockDim.x) {
+            const float p = expf(lg[v] - mx) * inv;
+            if (pr) pr[v] = p;
+            if (dl) dl[v] = scale * (p - (v == tgt ? 1.0f : 0.0f));
+        }
+        if (dl)
+            for (long v = V + threadIdx.x; v < ldd; v += blockDim.x) dl[v] = 0.f;
+    }
+    if (threadIdx.x == 0 && rowterm) rowterm[r] = tgt >= 0 ? (lg[tgt] - mx) - logf(s) : 0.f;
+}
+
+// loss = -(sum of row terms, in row order) / rows, as one float accumulator
+// like src/ops.c:503,548,573. Single thread: rows <= a few 10^4.
+__global__ void ce_loss_kernel(const float *__restrict__ rowterm, int rows, float *__restrict__ loss) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    float acc = 0.f;
+    for (int r = 0; r < rows; ++r) acc -= rowterm[r];
+    *loss = acc / (float)rows;
+}
+
+__global__ void ce_bwd_kernel(float *__restrict__ dlogits, const float *__restrict__ probs,
+                              const int *__restrict__ targets, float scale, int rows, int V) {
+    const long n = (long)rows * V;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const long r = i / V;
+        const int v = (int)(i % V);
+        dlogits[i] += scale * (probs[i] - (v == targets[r] ? 1.0f : 0.0f));
+    }
+}
+
+// dlogits[r, v] = scale * (probs[r, v] - onehot) with pitch ldd (pad zeroed):
+// the reference's calloc + cross_entropy_bwd (src/model.c:644,665).
+__global__ void ce_grad_kernel(const float *__restrict__ probs, long ldp, const int *__restrict__ targets,
+                               float scale, float *__restrict__ dl, long ldd, int V) {
+    const long r = blockIdx.x;
+    const int tgt = targets[r];
+    for (long v = threadIdx.x; v < ldd; v += blockDim.x)
+        dl[r * ldd + v] = v < V ? scale * (probs[r * ldp + v] - (v == tgt ? 1.0f : 0.0f)) : 0.0f;
+}
+
+// kc[b, pos0 + t, :] = qkv[b*T + t, C:2C], vc likewise from [2C:3C]
+__global__ void kv_append_kernel(const float *__restrict__ qkv, float *__restrict__ kc,
+                                 float *__restrict__ vc, int B, int T, long Tmax, int pos0, int C) {
+    const long n = (long)B * T * C;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const long r = i / C;
+        const int c = (int)(i % C), b = (int)(r / T), t = (int)(r % T);
+        const float *src = qkv + r * 3L * C;
+        const long dst = ((long)b * Tmax + pos0 + t) * C + c;
+        kc[dst] = src[C + c];
+        vc[dst] = src[2 * C + c];
+    }
+}
+
+// dst[b, :] = src[b*T + T-1, :]
+__global__ void gather_last_kernel(const float *__restrict__ src, float *__restrict__ dst, int B, int T,
+                                   int C) {
+    const long n = (long)B * C;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const long b = i / C;
+        const int c = (int)(i % C);
+        dst[i] = src[(b * T + T - 1) * C + c];
+    }
+}
+
+// ---------------------------------------------------------------- misc
+__global__ void axpy_kernel(float *__restrict__ dst, const float *__restrict__ src, long n) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        dst[i] += src[i];
+}
+
+__global__ void add3_kernel(float *__restrict__ dst, const float *__restrict__ a,
+                            const float *__restrict__ b, long n) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        dst[i] = a[i] + b[i];
+}
+
+__global__ void scale_kernel(float *__restrict__ x, long n, const float *__restrict__ sp, float s) {
+    const float f = sp ? *sp : s;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        x[i] *= f;
+}
+
+__global__ void mask_mul_kernel(float *__restrict__ x, const unsigned char *__restrict__ mask,
+                                long n, float scale) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        x[i] *= mask[i] ? scale : 0.0f;
+}
+
+// sum of squares, double accumulation: per-block partials then a fixed-order
+// final pass.
+__global__ void sumsq_partial_kernel(const float *__restrict__ g, long n, double *__restrict__ part) {
+    __shared__ double sh[32];
+    double s = 0.0;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+        s += (double)g[i] * (double)g[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += sh[k];
+        part[blockIdx.x] = t;
+    }
+}
+
+// norm = sqrt(sum part); if clip > 0: factor = norm > clip ? clip / norm : 1
+__global__ void norm_final_kernel(const double *__restrict__ part, int nparts, float *__restrict__ norm,
+                                  float *__restrict__ clip_factor, float clip) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    double s = 0.0;
+    for (int k = 0; k < nparts; ++k) s += part[k];
+    const float nv = (float)sqrt(s);
+    if (norm) *norm = nv;
+    if (clip_factor) *clip_factor = (clip > 0.f && nv > clip) ? clip / nv : 1.0f;
+}
+
+// ---------------------------------------------------------------- embeddings
+// emb[i] = wte[tok[i]] + wpe[i % T] (src/model.c:460-470)
+__global__ void embed_fwd_kernel(const int *__restrict__ tok, const float *__restrict__ wte,
+                                 const float *__restrict__ wpe, float *__restrict__ out, int BT,
+                                 int T, int C, int pos0) {
+    const long n = (long)BT * C;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const long r = i / C;
+        const int c = (int)(i % C);
+        const int t = (int)(r % T) + pos0;
+        out[i] = wte[(long)tok[r] * C + c] + wpe[(long)t * C + c];
+    }
+}
+
+// d_wpe[t] += sum_b dx[b, t] in b order (src/model.c:853-857)
+__global__ void embed_bwd_wpe_kernel(const float *__restrict__ dx, float *__restrict__ dwpe, int B,
+                                     int T, int C) {
+    const long n = (long)T * C;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        float acc = dwpe[i];
+        for (int b = 0; b < B; ++b) acc += dx[(long)b * n + i];
+        dwpe[i] = acc;
+    }
+}
+
+// d_wte[tok[i]] += dx[i], positions applied in increasing i as in
+// src/model.c:861-867. One warp per position; a position whose token occurs
+// earlier is skipped, the first occurrence ("leader") accumulates all later
+// occurrences in order into registers. Tokens are staged in shared memory.
+template <int CPL>
+__global__ void __launch_bounds__(256)
+embed_bwd_wte_kernel(const int *__restrict__ tok, const float *__restrict__ dx,
+                     float *__restrict__ dwte, int BT, int C) {
+    extern __shared__ int stok[];
+    for (int i = threadIdx.x; i < BT; i += blockDim.x) stok[i] = tok[i];
+    __syncthreads();
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < BT; i += gridDim.x * warps) {
+        const int v = stok[i];
+        bool leader = true;
+        for (int base = 0; base < i; base += 32) {
+            const int j = base + lane;
+            if (__any_sync(0xffffffffu, j < i && stok[j] == v)) { leader = false; break; }
+        }
+        if (!leader) continue;
+        float *row = dwte + (long)v * C;
+        float acc[CPL];
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            const int c = lane + 32 * q;
+            acc[q] = c < C ? row[c] + dx[(long)i * C + c] : 0.f;
+        }
+        for (int base = i + 1; base < BT; base += 32) {
+            const int j = base + lane;
+            unsigned mk = __ballot_sync(0xffffffffu, j < BT && stok[j] == v);
+            while (mk) {
+                const int jj = base + __ffs(mk) - 1;
+                mk &= mk - 1;
+#pragma unroll
+                for (int q = 0; q < CPL; ++q) {
+                    const int c = lane + 32 * q;
+                    if (c < C) acc[q] += dx[(long)jj * C + c];
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+            const int c = lane + 32 * q;
+            if (c < C) row[c] = acc[q];
+        }
+    }
+}
+
+// ---------------------------------------------------------------- AdamW
+// One fused pass (src/model.c:901-920): grads are first multiplied by the
+// clip factor computed on the device (identity when no clipping applies).
+__global__ void adamw_kernel(float *__restrict__ p, float *__restrict__ g, float *__restrict__ m,
+                             float *__restrict__ v, const unsigned char *__restrict__ decay, long n,
+                             const float *__restrict__ clip_factor, float lr, float b1, float b2,
+                             float eps, float wd, float bc1, float bc2) {
+    const float cf = clip_factor ? *clip_factor : 1.0f;
+    const bool scale = cf != 1.0f;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        float gi = g[i];
+        if (scale) {
+            gi *= cf;
+            g[i] = gi;
+        }
+        const float mi = b1 * m[i] + (1.0f - b1) * gi;
+        const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
+        m[i] = mi;
+        v[i] = vi;
+        const float mh = mi / bc1, vh = vi / bc2;
+        const float ewd = decay[i] ? wd : 0.0f;
+        p[i] = p[i] * (1.0f - lr * ewd) - lr * mh / (sqrtf(vh) + eps);
+    }
+}
+
+// ---------------------------------------------------------------- column sums
+// db[n] += sum_m dY[m, n]: row-chunk partials then an in-order final pass.
+__global__ void colsum_partial_kernel(const float *__restrict__ y, long ldy, int M, int N,
+                                      int rows_per_chunk, float *__restrict__ part) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    const long r0 = (long)blockIdx.y * rows_per_chunk;
+    const long r1 = std::min<long>(M, r0 + rows_per_chunk);
+    float s = 0.f;
+    for (long r = r0; r < r1; ++r) s += y[r * ldy + n];
+    part[(long)blockIdx.y * N + n] = s;
+}
+
+__global__ void colsum_final_kernel(const float *__restrict__ part, int chunks, int N,
+                                    float *__restrict__ db) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    float s = 0.f;
+    for (int k = 0; k < chunks; ++k) s += part[(long)k * N + n];
+    db[n] += s;
+}
+
+// ---------------------------------------------------------------- argmax
+// Greedy token per row: largest logit, lowest index on ties (the first index
+// whose CDF exceeds r in src/model.c:982-985 with top_k = 1).
+__global__ void argmax_kernel(const float *__restrict__ x, long ldx, int V, int *__restrict__ out,
+                              float *__restrict__ outval) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float *row = x + (long)blockIdx.x * ldx;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float f = row[v];
+        if (f > best) { best = f; bi = v; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float f = __shfl_xor_sync(0xffffffffu, best, o);
+        const int j = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (f > best || (f == best && j < bi)) { best = f; bi = j; }
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) { sv[wid] = best; si[wid] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+            if (sv[k] > best || (sv[k] == best && si[k] < bi)) { best = sv[k]; bi = si[k]; }
+        out[blockIdx.x] = bi;
+        if (outval) outval[blockIdx.x] = best;
+    }
+}
+
+}  // namespace
+
+// ========================================================== launchers
+
+#define LAUNCH_CHECK() do { ++g_launch_count; CG_CUDA(cudaGetLastError()); } while (0)
+
+int layernorm_fwd(const float *x, long ldx, const float *w, const float *b, float *out, long ldo,
+                  float *mean, float *rstd, int T, int C, cudaStream_t s) {
+    if (T <= 0) return OK;
+    const int warps = 8;
+    layernorm_fwd_kernel<<<grid_for(T, warps, 148 * 8), warps * 32, 0, s>>>(x, ldx, w, b, out, ldo,
+                                                                           mean, rstd, T, C);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+size_t layernorm_bwd_scratch_bytes(int T, int C) {
+    const int rpb = 64;
+    const long nb = (T + rpb - 1) / rpb;
+    return (size_t)nb * 2 * C * sizeof(float);
+}
+
+int layernorm_bwd(const float *dout, const float *x, const float *w, const float *mean,
+                  const float *rstd, float *dx, float *dw, float *db, int T, int C, float *scratch,
+                  cudaStream_t s) {
+    if (T <= 0) return OK;
+    if (C > 2048) {
+        set_last_error(ERR_ARG, "layernorm_bwd: C=%d > 2048 unsupported", C);
+        return ERR_ARG;
+    }
+    const int rpb = 64;
+    const int nb = (T + rpb - 1) / rpb;
+    const int cpl = (C + 31) / 32;
+#define LNB(N) layernorm_bwd_kernel<N><<<nb, 256, 0, s>>>(dout, x, w, mean, rstd, dx, scratch, T, C, rpb)
+    if (cpl <= 4) LNB(4);
+    else if (cpl <= 8) LNB(8);
+    else if (cpl <= 16) LNB(16);
+    else if (cpl <= 32) LNB(32);
+    else if (cpl <= 50) LNB(50);
+    else LNB(64);
+#undef LNB
+    LAUNCH_CHECK();
+    layernorm_bwd_reduce<<<(C + 255) / 256, 256, 0, s>>>(scratch, nb, C, dw, db);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int gelu_fwd(const float *x, float *out, long n, cudaStream_t s) {
+    if (n <= 0) return OK;
+    gelu_fwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, out, n);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int gelu_bwd(const float *dout, const float *x, float *dx, long n, cudaStream_t s) {
+    if (n <= 0) return OK;
+    gelu_bwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(dout, x, dx, n);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int softmax_rows(float *x, int rows, int cols, cudaStream_t s) {
+    if (rows <= 0 || cols <= 0) return OK;
+    const int th = cols >= 1024 ? 512 : (cols >= 128 ? 128 : 32);
+    softmax_rows_kernel<<<rows, th, 0, s>>>(x, cols);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int causal_mask(float *scores, int T, cudaStream_t s) {
+    if (T <= 1) return OK;
+    causal_mask_kernel<<<grid_for((long)T * T, 256), 256, 0, s>>>(scores, T);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int cross_entropy_rows(const float *logits, long ldl, const int *targets, float *probs, long ldp,
+                       float *dlogits, long ldd, float scale, float *rowterm, int rows, int V,
+                       cudaStream_t s) {
+    if (rows <= 0) return OK;
+    ce_fwd_kernel<<<rows, 512, 0, s>>>(logits, ldl, targets, probs, ldp, dlogits, ldd, scale,
+                                       rowterm, V);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int cross_entropy_loss(const float *rowterm, int rows, float *loss, cudaStream_t s) {
+    ce_loss_kernel<<<1, 32, 0, s>>>(rowterm, rows, loss);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int cross_entropy_bwd(float *dlogits, const float *probs, const int *targets, float scale, int rows,
+                      int V, cudaStream_t s) {
+    if (rows <= 0) return OK;
+    ce_bwd_kernel<<<grid_for((long)rows * V, 256), 256, 0, s>>>(dlogits, probs, targets, scale, rows, V);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int axpy1(float *dst, const float *src, long n, cudaStream_t s) {
+    if (n <= 0) return OK;
+    axpy_kernel<<<grid_for(n, 256), 256, 0, s>>>(dst, src, n);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int add3(float *dst, const float *a, const float *b, long n, cudaStream_t s) {
+    if (n <= 0) return OK;
+    add3_kernel<<<grid_for(n, 256), 256, 0, s>>>(dst, a, b, n);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int scale(float *x, long n, const float *dev_factor, float factor, cudaStream_t s) {
+    if (n <= 0) return OK;
+    scale_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, dev_factor, factor);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int mask_mul(float *x, const unsigned char *mask, long n, float sc, cudaStream_t s) {
+    if (n <= 0) return OK;
+    mask_mul_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, mask, n, sc);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+size_t norm_scratch_bytes() { return 1024 * sizeof(double); }
+
+int grad_norm(const float *g, long n, double *scratch, float *norm, float *clip_factor, float clip,
+              cudaStream_t s) {
+    const int nb = std::max(1, std::min(1024, (int)((n + 255) / 256)));
+    sumsq_partial_kernel<<<nb, 256, 0, s>>>(g, n, scratch);
+    LAUNCH_CHECK();
+    norm_final_kernel<<<1, 32, 0, s>>>(scratch, nb, norm, clip_factor, clip);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int embed_fwd(const int *tok, const float *wte, const float *wpe, float *out, int BT, int T, int C,
+              int pos0, cudaStream_t s) {
+    if (BT <= 0) return OK;
+    embed_fwd_kernel<<<grid_for((long)BT * C, 256), 256, 0, s>>>(tok, wte, wpe, out, BT, T, C, pos0);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int embed_bwd(const int *tok, const float *dx, float *dwte, float *dwpe, int B, int T, int C,
+              cudaStream_t s) {
+    const int BT = B * T;
+    if (BT <= 0) return OK;
+    embed_bwd_wpe_kernel<<<grid_for((long)T * C, 256), 256, 0, s>>>(dx, dwpe, B, T, C);
+    LAUNCH_CHECK();
+    const size_t sm = (size_t)BT * sizeof(int);
+    if (sm > 200 * 1024) {
+        set_last_error(ERR_ARG, "embed_bwd: B*T=%d exceeds the staged-token limit", BT);
+        return ERR_ARG;
+    }
+    if (C > 2048) {
+        set_last_error(ERR_ARG, "embed_bwd: C=%d > 2048 unsupported", C);
+        return ERR_ARG;
+    }
+    const int grid = std::min(num_sms() * 2, (BT + 7) / 8), cpl = (C + 31) / 32;
+#define EBW(N)                                                                                \
+    do {                                                                                      \
+        static bool attr = false;                                                             \
+        if (!attr) {                                                                          \
+            CG_CUDA(cudaFuncSetAttribute(embed_bwd_wte_kernel<N>,                             \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 204800)); \
+            attr = true;                                                                      \
+        }                                                                                     \
+        embed_bwd_wte_kernel<N><<<grid, 256, sm, s>>>(tok, dx, dwte, BT, C);                  \
+    } while (0)
+    if (cpl <= 8) EBW(8);
+    else if (cpl <= 16) EBW(16);
+    else if (cpl <= 24) EBW(24);
+    else if (cpl <= 32) EBW(32);
+    else if (cpl <= 50) EBW(50);
+    else EBW(64);
+#undef EBW
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int adamw(float *p, float *g, float *m, float *v, const unsigned char *decay, long n,
+          const float *clip_factor, float lr, float b1, float b2, float eps, float wd, float bc1,
+          float bc2, cudaStream_t s) {
+    if (n <= 0) return OK;
+    adamw_kernel<<<grid_for(n, 256, 148 * 32), 256, 0, s>>>(p, g, m, v, decay, n, clip_factor, lr, b1,
+                                                            b2, eps, wd, bc1, bc2);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+size_t colsum_scratch_bytes(int M, int N) {
+    const int chunks = std::max(1, std::min(64, (M + 127) / 128));
+    return (size_t)chunks * N * sizeof(float);
+}
+
+int colsum_add(const float *y, long ldy, int M, int N, float *db, float *scratch, cudaStream_t s) {
+    if (M <= 0 || N <= 0) return OK;
+    const int chunks = std::max(1, std::min(64, (M + 127) / 128));
+    const int rpc = (M + chunks - 1) / chunks;
+    dim3 g((N + 255) / 256, chunks);
+    colsum_partial_kernel<<<g, 256, 0, s>>>(y, ldy, M, N, rpc, scratch);
+    LAUNCH_CHECK();
+    colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(scratch, chunks, N, db);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int ce_grad(const float *probs, long ldp, const int *targets, float sc, float *dl, long ldd, int rows,
+            int V, cudaStream_t s) {
+    if (rows <= 0) return OK;
+    ce_grad_kernel<<<rows, 512, 0, s>>>(probs, ldp, targets, sc, dl, ldd, V);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int kv_append(const float *qkv, float *kc, float *vc, int B, int T, long Tmax, int pos0, int C,
+              cudaStream_t s) {
+    if (B * T <= 0) return OK;
+    kv_append_kernel<<<grid_for((long)B * T * C, 256), 256, 0, s>>>(qkv, kc, vc, B, T, Tmax, pos0, C);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int gather_last(const float *src, float *dst, int B, int T, int C, cudaStream_t s) {
+    if (B <= 0) return OK;
+    gather_last_kernel<<<grid_for((long)B * C, 256), 256, 0, s>>>(src, dst, B, T, C);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int argmax_rows(const float *x, long ldx, int rows, int V, int *out, float *outval, cudaStream_t s) {
+    if (rows <= 0) return OK;
+    argmax_kernel<<<rows, 512, 0, s>>>(x, ldx, V, out, outval);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+}  // namespace cg

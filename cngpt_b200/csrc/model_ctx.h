@@ -1,0 +1,64 @@
+// model_ctx.h - device-side state attached to a caller's GPT / FastCtx
+// (internal). The reference's structs are kept byte-identical, so the extra
+// state lives in side tables keyed by the struct's address.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+extern "C" {
+#include "cngpt/fast.h"
+#include "cngpt/model.h"
+}
+
+namespace cg {
+
+struct ModelCtx {
+    GPTConfig cfg{};
+    bool managed = false;
+    // activation arena capacity (floats / bytes); the current layout is (B, T)
+    size_t act_cap = 0, mask_cap = 0;
+    int B = 0, T = 0;
+    // buffers beyond the reference arena, sized for (B, T)
+    size_t extra_BT = 0;      // B*T the extras were sized for
+    float *dlogits = nullptr;  // [BT, ldlog], ldlog = V rounded up to 4 (TMA pitch)
+    long ldlog = 0;
+    float *d_x = nullptr, *d_ln = nullptr, *d_mlp = nullptr, *d_ao = nullptr, *d_qkv = nullptr;
+    float *scratch = nullptr;  // LN / column-sum / attention / CE partials
+    size_t scratch_bytes = 0;
+    int *tok = nullptr, *tgt = nullptr;  // staged token ids
+    float *dev_scalars = nullptr;        // [0] loss, [1] grad norm, [2] clip factor
+    double *norm_scratch = nullptr;      // grad-norm partials (allocated by gpt_init)
+    float *host_loss = nullptr;          // pinned
+    const int *fwd_targets = nullptr;    // caller's targets pointer of the last forward
+    bool dlogits_valid = false;
+    // data parallel
+    void *nccl_comm = nullptr;
+    int world = 1, rank = 0;
+};
+
+struct FastDev {
+    size_t cap_BT = 0;
+    int cap_B = 0;
+    float *xl = nullptr, *al = nullptr;  // last-row gathers [B, C]
+    int *tok = nullptr;
+    size_t tok_cap = 0;
+    // KV cache for greedy decode: [L][B][Tmax][C] each
+    float *kc = nullptr, *vc = nullptr;
+    int kv_B = 0, kv_T = 0;
+    int *next = nullptr;   // [B] argmax tokens
+    int *gen = nullptr;    // [B * n_new]
+    size_t gen_cap = 0;
+};
+
+ModelCtx *model_ctx(const GPT *m);  // nullptr (and ERR_STATE recorded) if unknown
+FastDev *fast_dev(const FastCtx *f, bool create);
+int dev_alloc(void **p, size_t bytes, bool managed);
+void dev_free(void *p);
+// copy token ids to the device unless they already are device-accessible
+int stage_tokens(const int *src, size_t n, int **buf, size_t *cap, const int **out, cudaStream_t s);
+int dp_allreduce(ModelCtx *c, float *buf, size_t n, cudaStream_t s);
+
+}  // namespace cg

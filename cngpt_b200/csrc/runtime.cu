@@ -1,0 +1,58 @@
+// runtime.cu - library-wide state: error channel, precision mode, device info.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace cg {
+
+namespace {
+int g_status = OK;
+char g_msg[512] = "";
+int g_precision = PREC_3XTF32;
+int g_sms = 0;
+}  // namespace
+
+void set_last_error(int status, const char *fmt, ...) {
+    g_status = status;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    if (getenv("CNGPT_CUDA_VERBOSE")) fprintf(stderr, "libcngpt_cuda: %s\n", g_msg);
+}
+
+int last_status() { return g_status; }
+const char *last_message() { return g_msg; }
+
+int check_device_error() {
+    int (*readers[])() = {gemm_take_dev_error, attn_take_dev_error};
+    for (auto rd : readers) {
+        int code = rd();
+        if (code < 0) {
+            set_last_error(ERR_CUDA, "reading the device error word failed");
+            return ERR_CUDA;
+        }
+        if (code != 0) {
+            set_last_error(ERR_DEVICE_WAIT, "device-side bounded wait gave up (site %d)", code);
+            return ERR_DEVICE_WAIT;
+        }
+    }
+    return OK;
+}
+
+int precision() { return g_precision; }
+void set_precision(int p) { g_precision = p; }
+
+int num_sms() {
+    if (g_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_sms <= 0) g_sms = 148;
+    }
+    return g_sms;
+}
+
+}  // namespace cg

@@ -1,0 +1,121 @@
+/*
+ * cngpt_cuda.h - extensions of libcngpt_cuda beyond the reference's C API.
+ *
+ * The drop-in entry points keep the reference's names and signatures
+ * (cngpt/ops.h, cngpt/model.h, cngpt/fast.h). The reference has no GPU, no
+ * error channel, no precision modes, no KV cache and no collectives, so the
+ * calls below have no counterpart in it; each comment names the reference
+ * behaviour it extends.
+ */
+#ifndef CNGPT_CUDA_H
+#define CNGPT_CUDA_H
+
+#include <stddef.h>
+
+#include "cngpt/model.h"
+#include "cngpt/fast.h"
+#include "cngpt/ops.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status ------------------------------------------------------------
+ * The reference reports failure by return value -1 / NULL / 0.0f and stderr
+ * (src/model.c:179-188, 452-455). Every call here also records a status. */
+#define CNGPT_OK              0
+#define CNGPT_ERR_CUDA        1  /* a CUDA runtime call failed */
+#define CNGPT_ERR_ARG         2  /* invalid shape, pointer or alignment */
+#define CNGPT_ERR_ALLOC       3  /* device allocation failed */
+#define CNGPT_ERR_DEVICE_WAIT 4  /* a bounded device-side wait gave up */
+#define CNGPT_ERR_NCCL        5  /* a collective failed */
+#define CNGPT_ERR_STATE       6  /* wrong call order or unknown model */
+
+int         cngpt_cuda_last_status(void);   /* status of the last failing call */
+const char *cngpt_cuda_last_message(void);
+void        cngpt_cuda_clear_status(void);
+/* synchronise the library stream and read the device error words */
+int         cngpt_cuda_check(void);
+
+/* ---- configuration ------------------------------------------------------ */
+#define CNGPT_PREC_TF32   0  /* one tcgen05 kind::tf32 pass (~1e-3 relative) */
+#define CNGPT_PREC_3XTF32 1  /* hi*hi + hi*lo + lo*hi split (fp32-level); default */
+#define CNGPT_PREC_FP32   2  /* CUDA-core fp32 FMA kernels (reference-exact math) */
+int   cngpt_cuda_set_precision(int mode);
+int   cngpt_cuda_get_precision(void);
+/* cudaStream_t for every following call; NULL = the legacy default stream */
+int   cngpt_cuda_set_stream(void *stream);
+void *cngpt_cuda_get_stream(void);
+/* arenas allocated after this call use cudaMallocManaged (host-dereferenceable) */
+int   cngpt_cuda_set_managed(int on);
+/* number of kernels this library has launched so far */
+unsigned long long cngpt_cuda_launch_count(void);
+
+/* ---- GEMM with fused epilogue --------------------------------------------
+ * out[M,N] = alpha * op(A)[M,K] op(B)[N,K]^T, then the epilogue:
+ *   CNGPT_EPI_STORE     D = acc + bias
+ *   CNGPT_EPI_ACCUM     D = D + acc (+ bias)
+ *   CNGPT_EPI_GELU      t = acc + bias; D = t (if D); D2 = gelu(t)
+ *   CNGPT_EPI_RESID     t = acc + bias; D = t (if D); D2 = R + t
+ *   CNGPT_EPI_GELU_BWD  D = acc * gelu'(G)
+ * a_mn: A stored [K][lda] instead of [M][lda]; b_mn: B stored [K][ldb]
+ * instead of [N][ldb]. All pointers are device pointers. This is the kernel
+ * behind linear_fwd / linear_bwd_dx / linear_bwd_dw (src/ops.c:109-149). */
+#define CNGPT_EPI_STORE    0
+#define CNGPT_EPI_ACCUM    1
+#define CNGPT_EPI_GELU     2
+#define CNGPT_EPI_RESID    3
+#define CNGPT_EPI_GELU_BWD 4
+int cngpt_cuda_gemm(const float *A, long lda, int a_mn, const float *B, long ldb, int b_mn,
+                    int M, int N, int K, int epi_mode, float alpha,
+                    float *D, long ldd, const float *bias, float *D2, long ldd2,
+                    const float *R, long ldr, const float *G, long ldg);
+
+/* ---- fused attention (src/model.c:514-563, 742-822) -----------------------
+ * qkv [B,T,3C] device; out [B,T,C]; lse [B*H*T] (may be NULL). */
+int cngpt_cuda_attention_fwd(const float *qkv, float *out, float *lse,
+                             int B, int T, int C, int H);
+int cngpt_cuda_attention_bwd(const float *qkv, const float *out, const float *dout,
+                             const float *lse, float *dqkv, int B, int T, int C, int H);
+
+/* ---- training ------------------------------------------------------------
+ * One full step of the reference's train loop (src/cngpt.c:154-163):
+ * zero_grad, forward, backward, [DP allreduce], AdamW with clipping.
+ * tokens/targets may be host or device int[B*T]. loss_out (host) may be
+ * NULL, in which case nothing synchronises and the loss stays on the device
+ * (read it with cngpt_cuda_last_loss). */
+int cngpt_cuda_train_step(GPT *m, const int *tokens, const int *targets, int B, int T,
+                          float lr, float beta1, float beta2, float eps, float wd,
+                          float grad_clip, float *loss_out);
+int cngpt_cuda_last_loss(GPT *m, float *loss_out);
+
+/* parameter / gradient / optimizer state transfer (n_params floats) */
+int cngpt_cuda_params_to_host(GPT *m, float *dst);
+int cngpt_cuda_params_from_host(GPT *m, const float *src);
+int cngpt_cuda_grads_to_host(GPT *m, float *dst);
+int cngpt_cuda_copy(void *dst, const void *src, size_t bytes); /* any direction, synchronous */
+
+/* ---- greedy decode with a KV cache ---------------------------------------
+ * The reference recomputes the whole prefix per token (src/model.c:991-1016);
+ * this keeps K and V per layer and runs one row per sequence per step. The
+ * greedy token is the argmax of the last-position logits, lowest index on
+ * ties (sample_top_k with top_k = 1, src/model.c:945-985).
+ * prompt: host or device int[B*T]; out_tokens: host int[B*n_new].
+ * T + n_new must not exceed block_size. */
+int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B, int T, int n_new,
+                        int *out_tokens);
+
+/* ---- data-parallel training over NCCL -------------------------------------
+ * One process per GPU. Rank 0 creates the id and shares it out of band. After
+ * dp_init, gpt_backward is followed by a sum-allreduce of the gradient arena
+ * scaled by 1/world (the mean over the global batch) inside
+ * cngpt_cuda_train_step, and explicitly by cngpt_cuda_dp_allreduce_grads. */
+int cngpt_cuda_dp_unique_id(unsigned char id[128]);
+int cngpt_cuda_dp_init(GPT *m, const unsigned char id[128], int world, int rank);
+int cngpt_cuda_dp_allreduce_grads(GPT *m);
+int cngpt_cuda_dp_free(GPT *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CNGPT_CUDA_H */

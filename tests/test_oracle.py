@@ -1,0 +1,194 @@
+"""The oracle is pinned before it is trusted (CPU only).
+
+1. The reference's own unit tests (tests/check_{ops,grad,fast}.c), built by
+   oracle/Makefile against the reference's sources, pass.
+2. The C restatement (oracle/cngpt_oracle.c) reproduces the known answers of
+   tests/check_ops.c:69-248.
+3. The restatement agrees with the reference's compiled code op by op and
+   for whole forward / backward / AdamW steps, and with the committed golden
+   fixtures that tests/golden/make_golden.py generated from the reference.
+"""
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from tests.models import nwerr
+
+ROOT = Path(__file__).resolve().parents[1]
+GOLDEN = ROOT / "tests" / "golden"
+REF = oracle.reference_available()
+needs_ref = pytest.mark.skipif(not REF, reason="oracle/_ref not built (reference tree absent)")
+P = oracle.ptr
+f32 = np.float32
+
+
+@pytest.fixture(scope="module")
+def o():
+    return oracle.restatement()
+
+
+@needs_ref
+@pytest.mark.parametrize("t", ["ops", "grad", "fast"])
+def test_reference_unit_tests_pass(t):
+    exe = ROOT / "oracle" / "_ref" / f"check_{t}_ref"
+    assert exe.exists()
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert " 0 failed" in r.stdout
+
+
+# -------------------------------------------------- known answers (check_ops)
+def test_known_linear(o):
+    X = np.array([1, 0, 0, 1], f32); W = np.array([2, 3, 4, 5], f32); b = np.array([1, -1], f32)
+    Y = np.zeros(4, f32)
+    o.orc_linear_fwd(P(X), P(W), P(b), P(Y), 2, 2, 2)
+    assert np.allclose(Y, [3, 3, 4, 4], atol=1e-5)          # tests/check_ops.c:78-81
+    dX = np.zeros(4, f32)
+    o.orc_linear_bwd_dx(P(X), P(W), P(dX), 2, 2, 2)
+    assert np.allclose(dX, [2, 3, 4, 5], atol=1e-5)         # tests/check_ops.c:101-104
+
+
+def test_known_layernorm_gelu_softmax_ce(o):
+    x = np.array([1, 2, 3, 4], f32); w = np.ones(4, f32); b = np.zeros(4, f32)
+    out, mean, rstd = np.zeros(4, f32), np.zeros(1, f32), np.zeros(1, f32)
+    o.orc_layernorm_fwd(P(x), P(w), P(b), P(out), P(mean), P(rstd), 1, 4)
+    assert abs(mean[0] - 2.5) < 1e-4                         # tests/check_ops.c:127-135
+    assert np.allclose(out, [-1.3416, -0.4472, 0.4472, 1.3416], atol=1e-3)
+    g = np.array([0, 1, -1, 2], f32); go = np.zeros(4, f32)
+    o.orc_gelu_fwd(P(g), P(go), 4)
+    assert np.allclose(go, [0, 0.8413, -0.1587, 1.9545], atol=1e-3)   # tests/check_ops.c:153-156
+    s = np.array([1, 2, 3, 100, 100, 100], f32)
+    o.orc_softmax_inplace(P(s), 2, 3)
+    assert np.allclose(s[:3], [0.0900, 0.2447, 0.6652], atol=1e-3)     # tests/check_ops.c:171-181
+    assert np.allclose(s[3:], 1 / 3, atol=1e-5)
+    lg = np.array([10, 0, 0, 10], f32); tg = np.array([0, 1], np.int32)
+    pr, loss = np.zeros(4, f32), np.zeros(1, f32)
+    o.orc_cross_entropy_fwd(P(lg), P(tg), P(pr), P(loss), 1, 2, 2)
+    assert loss[0] < 0.01 and pr[0] > 0.99 and pr[3] > 0.99          # tests/check_ops.c:200-202
+    lg2 = np.array([0, 10, 10, 0], f32)
+    o.orc_cross_entropy_fwd(P(lg2), P(tg), P(pr), P(loss), 1, 2, 2)
+    assert loss[0] > 5.0                                               # tests/check_ops.c:209
+
+
+def test_known_layernorm_bwd_fd(o):
+    C_ = 4
+    x = np.array([0.5, -0.3, 1.2, -0.8], f32); w = np.array([1, 2, 0.5, 1.5], f32)
+    b = np.array([0.1, -0.1, 0.2, -0.2], f32); dout = np.array([0.3, -0.5, 0.7, -0.2], f32)
+    out, mean, rstd = np.zeros(4, f32), np.zeros(1, f32), np.zeros(1, f32)
+    o.orc_layernorm_fwd(P(x), P(w), P(b), P(out), P(mean), P(rstd), 1, C_)
+    dx, dw, db = np.zeros(4, f32), np.zeros(4, f32), np.zeros(4, f32)
+    o.orc_layernorm_bwd(P(dout), P(x), P(w), P(mean), P(rstd), P(dx), P(dw), P(db), 1, C_)
+    eps = 1e-4
+
+    def loss(xx):
+        oo, m_, r_ = np.zeros(4, f32), np.zeros(1, f32), np.zeros(1, f32)
+        o.orc_layernorm_fwd(P(xx), P(w), P(b), P(oo), P(m_), P(r_), 1, C_)
+        return float(np.sum(dout * oo))
+    xp, xm = x.copy(), x.copy()
+    xp[0] += eps
+    xm[0] -= eps
+    assert abs(dx[0] - (loss(xp) - loss(xm)) / (2 * eps)) < 1e-3     # tests/check_ops.c:247
+
+
+# -------------------------------------------------- restatement vs reference
+def rnd(*shape, seed=0):
+    return np.random.default_rng(seed).standard_normal(shape).astype(f32)
+
+
+@needs_ref
+def test_ops_match_reference(o):
+    r = oracle.reference()
+    M, K, N = 37, 45, 29
+    X, W, b, dY = rnd(M, K), rnd(N, K, seed=1), rnd(N, seed=2), rnd(M, N, seed=3)
+    for fn_o, fn_r, args, outs in [
+        ("orc_linear_fwd", "linear_fwd", lambda o_: (P(X), P(W), P(b), P(o_[0]), M, K, N), [(M, N)]),
+        ("orc_linear_bwd_dx", "linear_bwd_dx", lambda o_: (P(dY), P(W), P(o_[0]), M, K, N), [(M, K)]),
+        ("orc_linear_bwd_dw", "linear_bwd_dw", lambda o_: (P(dY), P(X), P(o_[0]), P(o_[1]), M, K, N),
+         [(N, K), (N,)]),
+    ]:
+        oa = [np.full(s, 0.25, f32) for s in outs]
+        ra = [np.full(s, 0.25, f32) for s in outs]
+        getattr(o, fn_o)(*args(oa))
+        getattr(r, fn_r)(*args(ra))
+        for a, c in zip(oa, ra):
+            assert nwerr(a, c) < 1e-6, fn_o
+    T, Cm = 19, 48
+    x, w, bb, dout = rnd(T, Cm, seed=4), rnd(Cm, seed=5), rnd(Cm, seed=6), rnd(T, Cm, seed=7)
+    outs = {}
+    for name, L in (("o", o), ("r", r)):
+        out, mn, rs = np.zeros((T, Cm), f32), np.zeros(T, f32), np.zeros(T, f32)
+        (L.orc_layernorm_fwd if name == "o" else L.layernorm_fwd)(P(x), P(w), P(bb), P(out), P(mn), P(rs), T, Cm)
+        dx, dw, db = np.ones((T, Cm), f32), np.ones(Cm, f32), np.ones(Cm, f32)
+        (L.orc_layernorm_bwd if name == "o" else L.layernorm_bwd)(P(dout), P(x), P(w), P(mn), P(rs),
+                                                                   P(dx), P(dw), P(db), T, Cm)
+        g = np.zeros(T * Cm, f32)
+        (L.orc_gelu_fwd if name == "o" else L.gelu_fwd)(P(x), P(g), T * Cm)
+        gb = np.ones(T * Cm, f32)
+        wt = np.ascontiguousarray(np.tile(w, T))
+        (L.orc_gelu_bwd if name == "o" else L.gelu_bwd)(P(wt), P(x), P(gb), T * Cm)
+        sm = x.copy()
+        (L.orc_softmax_inplace if name == "o" else L.softmax_inplace)(P(sm), T, Cm)
+        outs[name] = [out, mn, rs, dx, dw, db, g, gb, sm]
+    # the reference's softmax uses its AVX2 exp polynomial (src/ops.c:54-83),
+    # a few ulp from libm's expf
+    for k, (a, c) in enumerate(zip(outs["o"], outs["r"])):
+        assert nwerr(a, c) < (1e-5 if k == 8 else 2e-6), k
+
+
+# -------------------------------------------------- model-level
+CASES = {"grad": (2, 4, 32, 64, 8), "fast": (3, 4, 32, 70, 16), "hs64": (2, 2, 128, 96, 128),
+         "tiny": (2, 6, 384, 65, 256)}
+
+
+def golden(name):
+    return np.load(GOLDEN / f"{name}.npz")
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_restatement_matches_golden(name):
+    g = golden(name)
+    L, H, Cm, V, block, B, T, seed = (int(v) for v in g["cfg"])
+    c = oracle.cfg(L, H, Cm, V, block)
+    p = oracle.init_weights(c, None if seed < 0 else seed)
+    idx = g["idx"]
+    assert np.array_equal(p[idx], g["p0_sample"]), "weight init must reproduce the reference stream"
+    tok, tgt = g["tokens"], g["targets"]
+    loss, grads = oracle.forward_backward(c, p, tok, tgt, B, T)
+    assert abs(loss - float(g["loss"])) / float(g["loss"]) < 2e-6
+    _, logits = oracle.forward(c, p, tok, None, B, T)
+    # the restatement sums products in double; the reference's fp32 sgemm is
+    # itself ~1e-5 (normwise) from that at these widths: its noise floor
+    assert nwerr(logits, g["logits"]) < 2e-5
+    assert nwerr(grads[idx], g["grad_sample"]) < 5e-5
+    assert abs(np.linalg.norm(grads.astype(np.float64)) - float(g["grad_norm"])) / float(g["grad_norm"]) < 1e-5
+    m, v = np.zeros_like(p), np.zeros_like(p)
+    oracle.adamw(c, p, grads, m, v, 0, 1e-3, 0.9, 0.99, 1e-8, 0.1, 1.0)
+    # AdamW's first step moves each weight by ~lr*sign(g): compare where the
+    # reference gradient is clearly non-zero
+    big = np.abs(g["grad_sample"]) > 1e-3 * np.abs(g["grad_sample"]).max()
+    assert np.max(np.abs(p[idx] - g["p1_sample"])[big]) < 1e-5
+    last = np.zeros((B, V), f32)
+    oracle.restatement().orc_forward_last(C.byref(c), P(p), P(tok), B, T, P(last))
+    assert nwerr(last, g["fast_logits"]) < 2e-5
+
+
+@needs_ref
+def test_restatement_full_grads_match_reference():
+    """every gradient element of the check_grad model, live against the reference"""
+    from tests.models import RefModel
+    L, H, Cm, V, block = CASES["grad"]
+    ref = RefModel(L, H, Cm, V, block, 1234)
+    c = oracle.cfg(L, H, Cm, V, block)
+    p = ref.params()
+    tok = oracle.lcg_tokens(13, V)
+    ref.zero_grad()
+    lr_ = ref.forward(tok[:-1], tok[1:], 2, 6)
+    ref.backward(tok[:-1], tok[1:], 2, 6)
+    lo, go = oracle.forward_backward(c, p, tok[:-1].copy(), tok[1:].copy(), 2, 6)
+    assert abs(lo - lr_) < 1e-5
+    assert nwerr(go, ref.grads()) < 1e-5
+    ref.free()
