@@ -1,0 +1,408 @@
+"""Benchmark: GPT-2 small training step (fwd + bwd + AdamW) through libcngpt_cuda.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: GPT-2 small 124M (12L / 12H / 768C, V=50257,
+block 1024), random-init fp32 weights (the reference's init from the C
+library's rand() stream), B=8 x T=1024 token ids per GPU from the reference
+bench's LCG (uniform over [0, 50257)), next-token targets, cosine LR with
+warmup, AdamW (betas 0.9/0.95, eps 1e-8, wd 0.1, clip 1.0). N > 1 GPUs run
+data parallel (one process per GPU under torchrun, NCCL gradient average):
+weak scaling, global batch 8N.
+
+One JSON line on rank 0:
+  value   tokens/s of the whole job with token ids already in HBM (device
+          timed with CUDA events, max over ranks), TF32 tensor-core mode
+  e2e     the same through cngpt_cuda_train_step with pinned host token
+          buffers: H2D of the ids and D2H of the loss inside every step
+  roofline  the tcgen05 GEMM kernel, replaying one step's GEMM shapes alone
+  cpu_baseline  the reference's own CPU build (oracle/_ref) on this host
+--impl reference times only the reference's CPU build (all host threads).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L_, H_, C_, V_, BLOCK = 12, 12, 768, 50257, 1024
+B_, T_ = 8, 1024
+LR, LR_MIN, WARMUP_LR, TOTAL_ITERS = 3e-4, 1e-5, 100, 5000
+METRIC = "GPT-2 small tokens/sec (train step: fwd+bwd+AdamW)"
+BASELINE_METRIC = "GPT-2 tokens/sec (train step, prefill, decode); GEMM % of TF32/HBM roofline"
+
+
+def bench_config(world: int) -> dict:
+    return {"workload": "GPT-2 small 124M training step (fwd+bwd+AdamW), B=8 T=1024 per GPU "
+                        "(BASELINE configs[1])", "global_batch": B_ * world, "seq_len": T_,
+            "parallelism": f"dp{world}", "l2": "inputs larger than L2 (17 GB of activations per step)",
+            "baseline_metric": BASELINE_METRIC}
+
+
+def lr_schedule(step: int) -> float:
+    """cosine schedule with linear warmup (src/cngpt.c:68-78)"""
+    if step < WARMUP_LR:
+        return LR * (step + 1) / WARMUP_LR
+    if step >= TOTAL_ITERS:
+        return LR_MIN
+    p = (step - WARMUP_LR) / (TOTAL_ITERS - WARMUP_LR)
+    return LR_MIN + 0.5 * (LR - LR_MIN) * (1.0 + math.cos(3.14159265 * p))
+
+
+def lcg_tokens(n: int, vocab: int, seed: int) -> np.ndarray:
+    """the reference bench's generator (src/cngpt.c:338-342), vectorised"""
+    out = np.empty(n, dtype=np.int64)
+    s = seed & 0xFFFFFFFF
+    for i in range(n):
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        out[i] = (s >> 8) % vocab
+    return out.astype(np.int32)
+
+
+def step_flops(B: int, T: int) -> dict:
+    """algorithmic FLOPs of one training step (causal attention counted once
+    per (query, key<=query) pair; no recompute; backward = 2x forward)"""
+    BT = B * T
+    lin = 2 * BT * C_ * (12 * C_) * L_                 # qkv + proj + fc + mlp_proj
+    head = 2 * BT * V_ * C_
+    attn = 2 * 2 * B * H_ * (T * (T + 1) // 2) * (C_ // H_) * L_   # QK^T and PV
+    return {"gemm": 3 * (lin + head), "attn": 3 * attn, "total": 3 * (lin + head + attn)}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region"""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ reference arm
+def cpu_reference_step_sample(steps: int, warmup: int, threads: int) -> dict:
+    """The reference's own CPU build: one sequence of the workload (B=1, T=1024)
+    per step through gpt_zero_grad / gpt_forward / gpt_backward / gpt_adamw."""
+    os.environ["OPENBLAS_NUM_THREADS"] = str(threads)
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    from cngpt_b200 import abi
+    from oracle import oracle
+    lib = oracle.reference()
+    m = abi.GPT()
+    assert lib.gpt_init(C.byref(m), abi.GPTConfig(L_, H_, C_, V_, BLOCK, 0.0)) == 0
+    C.CDLL(None).srand(1)
+    lib.gpt_init_weights(C.byref(m))
+    ids = lcg_tokens(T_ + 1, V_, 12345)
+    tok, tgt = ids[:-1].copy(), ids[1:].copy()
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        lib.gpt_zero_grad(C.byref(m))
+        loss = lib.gpt_forward(C.byref(m), tok.ctypes.data, tgt.ctypes.data, 1, T_)
+        lib.gpt_backward(C.byref(m), tok.ctypes.data, tgt.ctypes.data, 1, T_)
+        lib.gpt_adamw(C.byref(m), lr_schedule(i), 0.9, 0.95, 1e-8, 0.1, 1.0)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    lib.gpt_free(C.byref(m))
+    t = float(np.mean(times))
+    return {"value": T_ / t, "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"{steps} timed step(s) after {warmup} warm-up of 1 sequence (B=1, T=1024) of the "
+                      f"B=8 workload, OpenBLAS threads={threads}, last loss {loss:.4f}",
+            "s_per_step": t}
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cb = cpu_reference_step_sample(args.steps, args.warmup, threads)
+    world = args.gpus
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cb["s_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic (reference LCG token ids)",
+            "config": bench_config(world),
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def gemm_replay(lib, torch, dev, prec: int, iters: int) -> dict:
+    """Time the tcgen05 GEMM alone on one training step's GEMM shapes (same
+    operand majorness and epilogues as the model), CUDA events on the stream
+    the kernels run on (the legacy default stream)."""
+    from cngpt_b200 import abi
+    BT, Vp = B_ * T_, (V_ + 3) & ~3
+    f = lambda *s: torch.randn(*s, device=dev) * 0.02  # noqa: E731
+    X = f(BT, 4 * C_)
+    W = f(V_, C_)
+    Y = torch.empty(BT, Vp, device=dev)
+    DL = f(BT, Vp)
+    Dw = torch.zeros(V_, C_, device=dev)
+    bias = torch.zeros(4 * C_, device=dev)
+    G = f(BT, 4 * C_)
+    # (M, N, K, a_mn, b_mn, lda, ldb, epi, ldd)
+    shapes = []
+    for _ in range(L_):
+        shapes += [(BT, 3 * C_, C_, 0, 0, C_, C_, abi.EPI_STORE, 3 * C_),
+                   (BT, C_, C_, 0, 0, C_, C_, abi.EPI_RESID, C_),
+                   (BT, 4 * C_, C_, 0, 0, C_, C_, abi.EPI_GELU, 4 * C_),
+                   (BT, C_, 4 * C_, 0, 0, 4 * C_, 4 * C_, abi.EPI_RESID, C_),
+                   (BT, 4 * C_, C_, 0, 1, C_, 4 * C_, abi.EPI_GELU_BWD, 4 * C_),
+                   (C_, 4 * C_, BT, 1, 1, C_, 4 * C_, abi.EPI_ACCUM, 4 * C_),
+                   (BT, C_, 4 * C_, 0, 1, 4 * C_, C_, abi.EPI_STORE, C_),
+                   (4 * C_, C_, BT, 1, 1, 4 * C_, C_, abi.EPI_ACCUM, C_),
+                   (BT, C_, C_, 0, 1, C_, C_, abi.EPI_STORE, C_),
+                   (C_, C_, BT, 1, 1, C_, C_, abi.EPI_ACCUM, C_),
+                   (BT, C_, 3 * C_, 0, 1, 3 * C_, C_, abi.EPI_STORE, C_),
+                   (3 * C_, C_, BT, 1, 1, 3 * C_, C_, abi.EPI_ACCUM, C_)]
+    shapes += [(BT, V_, C_, 0, 0, C_, C_, abi.EPI_STORE, V_),
+               (BT, C_, V_, 0, 1, Vp, C_, abi.EPI_STORE, C_),
+               (V_, C_, BT, 1, 1, Vp, C_, abi.EPI_ACCUM, C_)]
+    flops = sum(2.0 * M * N * K for (M, N, K, *_r) in shapes)
+    lib.cngpt_cuda_set_precision(prec)
+
+    def run_all():
+        for (M, N, K, amn, bmn, lda, ldb, epi, ldd) in shapes:
+            a = DL if lda == Vp else X
+            # the operand that spans the vocabulary is the [V, C] weight
+            b = W if ((not bmn and N == V_) or (bmn and K == V_)) else X
+            st = lib.cngpt_cuda_gemm(a.data_ptr(), lda, amn, b.data_ptr(), ldb, bmn, M, N, K, epi, 1.0,
+                                     (Dw if epi == abi.EPI_ACCUM and M == V_ else Y).data_ptr(), ldd,
+                                     bias.data_ptr() if epi in (abi.EPI_RESID, abi.EPI_GELU) else None,
+                                     G.data_ptr(), ldd, G.data_ptr(), ldd, G.data_ptr(), ldd)
+            if st:
+                raise RuntimeError(lib.cngpt_cuda_last_message().decode())
+    run_all()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        run_all()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    n = len(shapes)
+    return {"flops_per_step": flops, "ms_per_step": ms, "launches": n,
+            "tflops": flops / (ms * 1e-3) / 1e12, "flops_per_launch": flops / n, "ms_per_launch": ms / n}
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+    from cngpt_b200 import abi
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    lib = abi.load()
+    m = abi.GPT()
+    abi.check(lib, 0 if lib.gpt_init(C.byref(m), abi.GPTConfig(L_, H_, C_, V_, BLOCK, 0.0)) == 0 else 3,
+              "gpt_init")
+    C.CDLL(None).srand(1)   # "seed 0": the C library's default stream (src/cngpt.c:112)
+    lib.gpt_init_weights(C.byref(m))
+    if world > 1:
+        uid = (C.c_ubyte * 128)()
+        if rank == 0:
+            abi.check(lib, lib.cngpt_cuda_dp_unique_id(uid), "dp id")
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0)
+        uid = (C.c_ubyte * 128).from_buffer_copy(obj[0])
+        abi.check(lib, lib.cngpt_cuda_dp_init(C.byref(m), uid, world, rank), "dp init")
+
+    ids = lcg_tokens(B_ * T_ + 1, V_, 12345 + rank)
+    tok_h = torch.from_numpy(ids[:-1].copy()).pin_memory()
+    tgt_h = torch.from_numpy(ids[1:].copy()).pin_memory()
+    tok_d, tgt_d = tok_h.to(dev), tgt_h.to(dev)
+    step_no = [0]
+
+    def train_step(tok_ptr, tgt_ptr, loss_ptr):
+        st = lib.cngpt_cuda_train_step(C.byref(m), tok_ptr, tgt_ptr, B_, T_, lr_schedule(step_no[0]),
+                                       0.9, 0.95, 1e-8, 0.1, 1.0, loss_ptr)
+        step_no[0] += 1
+        if st:
+            raise RuntimeError(lib.cngpt_cuda_last_message().decode())
+
+    def timed(prec: int, host_io: bool, K: int, W: int, clocks=None):
+        lib.cngpt_cuda_set_precision(prec)
+        loss = C.c_float()
+        args_ = ((tok_h.data_ptr(), tgt_h.data_ptr(), C.addressof(loss)) if host_io
+                 else (tok_d.data_ptr(), tgt_d.data_ptr(), None))
+        for _ in range(W):
+            train_step(*args_)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        l0 = lib.cngpt_cuda_launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ctx = clocks if clocks is not None else _Null()
+        with ctx:
+            e0.record()
+            for _ in range(K):
+                train_step(*args_)
+            e1.record()
+            torch.cuda.synchronize()
+        barrier()
+        launches = lib.cngpt_cuda_launch_count() - l0
+        ms = max_over_ranks(e0.elapsed_time(e1)) / K
+        last = C.c_float()
+        abi.check(lib, lib.cngpt_cuda_last_loss(C.byref(m), C.byref(last)), "loss")
+        abi.check(lib, lib.cngpt_cuda_check(), "device check")
+        return ms, launches // K, float(last.value)
+
+    clocks = ClockSampler(local)
+    ms, launches, loss = timed(abi.PREC_TF32, False, args.steps, args.warmup, clocks)
+    if not math.isfinite(loss):
+        raise RuntimeError(f"non-finite loss {loss}")
+    tokens = B_ * T_ * world
+    value = tokens / (ms * 1e-3)
+    ms_e2e, _, _ = timed(abi.PREC_TF32, True, max(3, args.steps // 2), 1)
+    ms_3x, _, loss_3x = timed(abi.PREC_3XTF32, False, max(3, args.steps // 2), 1)
+    fl = step_flops(B_, T_)
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    tf32_peak = peaks.get("bf16_tflops", 1590.0) / 2.0
+    peak_src = ("of measured (bf16 cuBLAS burst / 2: the tf32 tensor rate is half the bf16 rate)"
+                if "bf16_tflops" in peaks else "of fallback (1.59 PF bf16 / 2)")
+    replay = gemm_replay(lib, torch, dev, abi.PREC_TF32, 3)
+    traffic = None
+    prof = ROOT / "profiles" / "gemm_tc_traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "tf32", "data": "synthetic (reference LCG token ids, random-init "
+        "weights from the reference's rand() init)",
+        "config": bench_config(world),
+        "e2e": {"value": tokens / (ms_e2e * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 3 * B_ * T_ * 4, "d2h_bytes_per_step": 4,
+                "api": "cngpt_cuda_train_step with pinned host token buffers and the loss read back"},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": replay["tflops"], "peak": tf32_peak,
+                     "unit": "TFLOP/s", "frac": replay["tflops"] / tf32_peak, "traffic": traffic,
+                     "kernel": "gemm_tc_kernel (tcgen05 kind::tf32)", "peak_source": peak_src,
+                     "flops_per_launch": replay["flops_per_launch"], "ms_per_launch": replay["ms_per_launch"]},
+        "step_tflops": fl["total"] / (ms * 1e-3) / 1e12,
+        "step_frac_of_tf32_peak": fl["total"] / (ms * 1e-3) / 1e12 / tf32_peak,
+        "loss_after_steps": loss,
+        "modes": {"3xtf32": {"value": tokens / (ms_3x * 1e-3), "ms_per_step": ms_3x, "loss": loss_3x}},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_reference_step_sample(1, 1, os.cpu_count() or 1)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        lib.cngpt_cuda_dp_free(C.byref(m))
+        dist.destroy_process_group()
+    lib.gpt_free(C.byref(m))
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

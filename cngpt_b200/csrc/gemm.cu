@@ -8,11 +8,11 @@
 //               shared-memory stages (plain per-CTA loads, no multicast)
 //   warp 1      MMA issuer: tcgen05.mma.kind::tf32, 128 x BN x 8 per
 //               instruction, accumulating into one of two TMEM buffers
-//   warps 2-5   epilogue: tcgen05.ld of the finished accumulator, then the
+//   warps 2-9   epilogue: tcgen05.ld of the finished accumulator, then the
 //               fused bias / GELU / residual / accumulate / GELU-backward
 //               step and the global stores, overlapping the next tile's
 //               main loop (double-buffered TMEM)
-//   warps 6-9   (3xTF32 only) split transform: each staged fp32 tile x is
+//   warps 10-13 (3xTF32 only) split transform: each staged fp32 tile x is
 //               rewritten as hi = rna_tf32(x) in place and lo = rna_tf32(x-hi)
 //               into a twin buffer, and the MMA warp issues lo*hi + hi*lo +
 //               hi*hi into a fresh accumulator per 32-wide k-block; the
@@ -55,9 +55,10 @@ struct Cfg {
     static constexpr int B_BYTES = BN * KB_BYTES;
     static constexpr int STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
     static constexpr int STAGES = SPLIT ? 3 : (BN == 256 ? 4 : 6);
-    static constexpr int THREADS = SPLIT ? 320 : 192;
+    static constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each half the columns
+    static constexpr int THREADS = (2 + EPI_WARPS + (SPLIT ? 4 : 0)) * 32;
     static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 4 * 32 * 33 * 4;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + EPI_WARPS * 32 * 33 * 4;
 };
 
 struct SmemCtl {
@@ -70,18 +71,19 @@ struct SmemCtl {
     int abort;
 };
 
-// Fused epilogue for one output element (m, n) holding the raw product a.
-__device__ __forceinline__ void epi_apply(const GemmEpi &e, long m, int n, float a, float bias) {
+// Fused epilogue for one output element (m, n) holding the raw product a;
+// `aux` is the element's prefetched second operand (D for ACCUM, R for RESID,
+// G for GELU_BWD).
+__device__ __forceinline__ void epi_apply(const GemmEpi &e, long m, int n, float a, float bias,
+                                          float aux) {
     a *= e.alpha;
     switch (e.mode) {
         case EPI_STORE:
             e.D[m * e.ldd + n] = a + bias;
             break;
-        case EPI_ACCUM: {
-            float *d = e.D + m * e.ldd + n;
-            *d = (*d + a) + bias;
+        case EPI_ACCUM:
+            e.D[m * e.ldd + n] = (aux + a) + bias;
             break;
-        }
         case EPI_GELU:
             a += bias;
             if (e.D) e.D[m * e.ldd + n] = a;
@@ -90,11 +92,20 @@ __device__ __forceinline__ void epi_apply(const GemmEpi &e, long m, int n, float
         case EPI_RESID:
             a += bias;
             if (e.D) e.D[m * e.ldd + n] = a;
-            e.D2[m * e.ldd2 + n] = e.R[m * e.ldr + n] + a;
+            e.D2[m * e.ldd2 + n] = aux + a;
             break;
         case EPI_GELU_BWD:
-            e.D[m * e.ldd + n] = a * gelu_tanh_grad(e.G[m * e.ldg + n]);
+            e.D[m * e.ldd + n] = a * gelu_tanh_grad(aux);
             break;
+    }
+}
+
+__device__ __forceinline__ const float *epi_aux(const GemmEpi &e, long &ld) {
+    switch (e.mode) {
+        case EPI_ACCUM: ld = e.ldd; return e.D;
+        case EPI_RESID: ld = e.ldr; return e.R;
+        case EPI_GELU_BWD: ld = e.ldg; return e.G;
+        default: ld = 0; return nullptr;
     }
 }
 
@@ -124,7 +135,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->tfull[b], 1);
-            mbar_init(&ctl->tempty[b], 4);
+            mbar_init(&ctl->tempty[b], C::EPI_WARPS);
         }
         ctl->abort = 0;
         fence_mbar_init();
@@ -236,35 +247,111 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
             }
         }
-    } else if (warp < 6) {
+    } else if (warp < 2 + C::EPI_WARPS) {
         // --------------------------------------------------- epilogue
-        // Each warp owns TMEM lanes [32q, 32q+32). A 32x32 block is read with one
-        // tcgen05.ld (thread = row), transposed through padded shared memory, and
-        // written back by rows so every global access of the warp is coalesced.
-        const int q = warp & 3;
+        // Warp w owns TMEM lanes [32q, 32q+32), q = w % 4, and half of the
+        // tile's columns. A 32x32 block is read with one tcgen05.ld (thread =
+        // row), transposed through padded shared memory, and written back by
+        // rows so every global access of the warp is coalesced; the block's
+        // second operand rows (residual / GELU input / accumulator) are all
+        // loaded before use so 32 loads are in flight per thread.
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        constexpr int CH = BN / 64;  // 32-column chunks per warp
         float *stile = (float *)(base + C::STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
         int acc = 0;
         uint32_t acc_phase = 0;
+        long ldaux = 0;
+        const float *aux = epi_aux(epi, ldaux);
+        // Writes one 32x32 block (thread = row on entry). After the shared-memory
+        // transpose, lane l handles row (4i + l/8) and columns 4(l%8)..+3 for
+        // i = 0..7: conflict-free shared reads, 16-byte global accesses, and
+        // the epilogue mode switch outside the element loop.
         auto store_block = [&](const float (&v)[32], int m0, int n0) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) stile[lane * 33 + j] = v[j];
             __syncwarp();
-            const int n = n0 + lane;
-            if (n < N) {
-                const float b = epi.bias ? epi.bias[n] : 0.0f;
-                const int rows = min(32, M - m0);
-#pragma unroll 4
-                for (int r = 0; r < rows; ++r) epi_apply(epi, m0 + r, n, stile[r * 33 + lane], b);
+            const int rsub = lane >> 3, c4 = (lane & 7) * 4;
+            const int n = n0 + c4;
+            if (epi.vec4 && n + 3 < N) {
+                const float4 b4 = epi.bias ? *(const float4 *)(epi.bias + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float al = epi.alpha;
+                auto run = [&](auto op) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = i * 4 + rsub;
+                        if (m0 + r < M) {
+                            const float *sp = stile + r * 33 + c4;
+                            float4 a = make_float4(sp[0] * al, sp[1] * al, sp[2] * al, sp[3] * al);
+                            op((long)(m0 + r), a);
+                        }
+                    }
+                };
+                switch (epi.mode) {
+                    case EPI_STORE:
+                        run([&](long m, float4 a) {
+                            *(float4 *)(epi.D + m * epi.ldd + n) =
+                                make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
+                        });
+                        break;
+                    case EPI_ACCUM:
+                        run([&](long m, float4 a) {
+                            float4 *d = (float4 *)(epi.D + m * epi.ldd + n);
+                            const float4 o = *d;
+                            *d = make_float4((o.x + a.x) + b4.x, (o.y + a.y) + b4.y, (o.z + a.z) + b4.z,
+                                             (o.w + a.w) + b4.w);
+                        });
+                        break;
+                    case EPI_GELU:
+                        run([&](long m, float4 a) {
+                            a = make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
+                            if (epi.D) *(float4 *)(epi.D + m * epi.ldd + n) = a;
+                            *(float4 *)(epi.D2 + m * epi.ldd2 + n) =
+                                make_float4(gelu_tanh(a.x), gelu_tanh(a.y), gelu_tanh(a.z), gelu_tanh(a.w));
+                        });
+                        break;
+                    case EPI_RESID:
+                        run([&](long m, float4 a) {
+                            a = make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
+                            if (epi.D) *(float4 *)(epi.D + m * epi.ldd + n) = a;
+                            const float4 r = *(const float4 *)(epi.R + m * epi.ldr + n);
+                            *(float4 *)(epi.D2 + m * epi.ldd2 + n) =
+                                make_float4(r.x + a.x, r.y + a.y, r.z + a.z, r.w + a.w);
+                        });
+                        break;
+                    case EPI_GELU_BWD:
+                        run([&](long m, float4 a) {
+                            const float4 g = *(const float4 *)(epi.G + m * epi.ldg + n);
+                            *(float4 *)(epi.D + m * epi.ldd + n) =
+                                make_float4(a.x * gelu_tanh_grad(g.x), a.y * gelu_tanh_grad(g.y),
+                                            a.z * gelu_tanh_grad(g.z), a.w * gelu_tanh_grad(g.w));
+                        });
+                        break;
+                }
+            } else {
+                // ragged edge or unaligned operands: one element at a time
+#pragma unroll 1
+                for (int i = 0; i < 8; ++i) {
+                    const int r = i * 4 + rsub;
+                    if (m0 + r >= M) continue;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int nj = n + j;
+                        if (nj >= N) break;
+                        const float x = aux ? aux[(long)(m0 + r) * ldaux + nj] : 0.0f;
+                        epi_apply(epi, m0 + r, nj, stile[r * 33 + c4 + j], epi.bias ? epi.bias[nj] : 0.0f, x);
+                    }
+                }
             }
             __syncwarp();
         };
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
             const int tm = tile % tiles_m, tn = tile / tiles_m;
             const int m0 = tm * BM + q * 32;
+            const int c0 = half * CH;
             if constexpr (SPLIT) {
-                float sum[BN];
+                float sum[CH * 32];
 #pragma unroll
-                for (int j = 0; j < BN; ++j) sum[j] = 0.0f;
+                for (int j = 0; j < CH * 32; ++j) sum[j] = 0.0f;
                 bool ok = true;
                 for (int kb = 0; kb < kblocks && ok; ++kb) {
                     if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) {
@@ -273,9 +360,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                     tc_fence_after();
 #pragma unroll
-                    for (int c = 0; c < BN / 32; ++c) {
+                    for (int c = 0; c < CH; ++c) {
                         float v[32];
-                        tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + c * 32) +
+                        tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) +
                                                ((uint32_t)(q * 32) << 16), v);
 #pragma unroll
                         for (int j = 0; j < 32; ++j) sum[c * 32 + j] += v[j];
@@ -287,21 +374,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 }
                 if (!ok) break;
 #pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
+                for (int c = 0; c < CH; ++c) {
                     float v[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = sum[c * 32 + j];
-                    store_block(v, m0, tn * BN + c * 32);
+                    store_block(v, m0, tn * BN + (c0 + c) * 32);
                 }
             } else {
                 if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) break;
                 tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
+                for (int c = 0; c < CH; ++c) {
                     float v[32];
-                    tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + c * 32) +
+                    tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) +
                                            ((uint32_t)(q * 32) << 16), v);
-                    store_block(v, m0, tn * BN + c * 32);
+                    store_block(v, m0, tn * BN + (c0 + c) * 32);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -311,7 +398,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else if (SPLIT) {
         // ---------------------------------------- 3xTF32 split transform
-        const int t = threadIdx.x - 192;  // 0..127
+        const int t = threadIdx.x - (2 + C::EPI_WARPS) * 32;  // 0..127
         int stage = 0;
         uint32_t phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -392,7 +479,11 @@ gemm_simt_kernel(const float *__restrict__ A, long lda, int a_mn, const float *_
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int n = n0 + tx * 4 + j;
-            if (n < N) epi_apply(epi, m, n, acc[i][j], epi.bias ? epi.bias[n] : 0.0f);
+            if (n < N) {
+                long ld = 0;
+                const float *ax = epi_aux(epi, ld);
+                epi_apply(epi, m, n, acc[i][j], epi.bias ? epi.bias[n] : 0.0f, ax ? ax[(long)m * ld + n] : 0.0f);
+            }
         }
     }
 }
@@ -514,16 +605,23 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
         return ERR_ARG;
     }
     if (M == 0 || N == 0) return OK;
+    GemmEpi e2 = epi;
+    {
+        auto al = [](const void *p) { return ((uintptr_t)p % 16) == 0; };
+        e2.vec4 = al(epi.D) && al(epi.D2) && al(epi.R) && al(epi.G) && al(epi.bias) &&
+                  (!epi.D || epi.ldd % 4 == 0) && (!epi.D2 || epi.ldd2 % 4 == 0) &&
+                  (!epi.R || epi.ldr % 4 == 0) && (!epi.G || epi.ldg % 4 == 0);
+    }
     const int prec = precision();
     const bool big = (long)M * N * (long)std::max(K, 1) >= (1L << 18) && K > 0;
     const bool tc = prec != PREC_FP32 && big && tma_ok(A, lda) && tma_ok(B, ldb) &&
                     (a_mn ? lda >= M : lda >= K) && (b_mn ? ldb >= N : ldb >= K);
     if (tc) {
         const bool split = prec == PREC_3XTF32;
-        if (!a_mn && !b_mn) return dispatch_tc<false, false>(A, lda, B, ldb, M, N, K, epi, s, split);
-        if (!a_mn && b_mn) return dispatch_tc<false, true>(A, lda, B, ldb, M, N, K, epi, s, split);
-        if (a_mn && b_mn) return dispatch_tc<true, true>(A, lda, B, ldb, M, N, K, epi, s, split);
-        return dispatch_tc<true, false>(A, lda, B, ldb, M, N, K, epi, s, split);
+        if (!a_mn && !b_mn) return dispatch_tc<false, false>(A, lda, B, ldb, M, N, K, e2, s, split);
+        if (!a_mn && b_mn) return dispatch_tc<false, true>(A, lda, B, ldb, M, N, K, e2, s, split);
+        if (a_mn && b_mn) return dispatch_tc<true, true>(A, lda, B, ldb, M, N, K, e2, s, split);
+        return dispatch_tc<true, false>(A, lda, B, ldb, M, N, K, e2, s, split);
     }
     dim3 grid((N + 63) / 64, (M + 63) / 64);
     gemm_simt_kernel<<<grid, 256, 0, s>>>(A, lda, a_mn, B, ldb, b_mn, M, N, K, epi);

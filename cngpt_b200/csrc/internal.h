@@ -76,6 +76,7 @@ struct GemmEpi {
     long ldr = 0;
     const float *G = nullptr;
     long ldg = 0;
+    int vec4 = 0;  // set by gemm(): every pointer 16B-aligned and every pitch % 4 == 0
 };
 
 // out[M,N] = op(A)[M,K] * op(B)[N,K]^T, with the epilogue applied per element.

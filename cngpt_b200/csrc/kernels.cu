@@ -46,76 +46,84 @@ __global__ void layernorm_fwd_kernel(const float *__restrict__ x, long ldx,
     }
 }
 
-// dx += rstd (dn - mean(dn) - xhat mean(dn xhat)) per row (src/ops.c:305-329);
-// dw/db column partials per block in registers, written to `part`
-// [gridDim.x][2][C]; layernorm_bwd_reduce adds them to dw/db in block order.
-template <int CPL>  // columns per lane (ceil(C/32))
+// dx += rstd (dn - mean(dn) - xhat mean(dn xhat)) per row (src/ops.c:305-329),
+// dn = dout * w, xhat = (x - mean) * rstd: one warp per row, two passes.
 __global__ void __launch_bounds__(256)
-layernorm_bwd_kernel(const float *__restrict__ dout, const float *__restrict__ x,
-                     const float *__restrict__ w, const float *__restrict__ mean,
-                     const float *__restrict__ rstd, float *__restrict__ dx,
-                     float *__restrict__ part, int T, int C, int rows_per_block) {
-    __shared__ float red[2][32 * CPL];
-    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float pdw[CPL], pdb[CPL];
-#pragma unroll
-    for (int i = 0; i < CPL; ++i) pdw[i] = pdb[i] = 0.f;
-    const long r0 = (long)blockIdx.x * rows_per_block;
-    const long r1 = std::min<long>(T, r0 + rows_per_block);
-    for (long t = r0 + wid; t < r1; t += 8) {
+layernorm_bwd_dx_kernel(const float *__restrict__ dout, const float *__restrict__ x,
+                        const float *__restrict__ w, const float *__restrict__ mean,
+                        const float *__restrict__ rstd, float *__restrict__ dx, int T, int C) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (long t = (long)blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += (long)gridDim.x * warps) {
         const float *dr = dout + t * C, *xr = x + t * C;
         const float m = mean[t], rs = rstd[t];
-        float xh[CPL], dn[CPL], s1 = 0.f, s2 = 0.f;
-#pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-            const int c = lane + 32 * i;
-            if (c < C) {
-                xh[i] = (xr[c] - m) * rs;
-                dn[i] = dr[c] * w[c];
-                s1 += dn[i];
-                s2 += dn[i] * xh[i];
-                pdw[i] += dr[c] * xh[i];
-                pdb[i] += dr[c];
-            }
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll 4
+        for (int c = lane; c < C; c += 32) {
+            const float dn = dr[c] * w[c];
+            s1 += dn;
+            s2 += dn * ((xr[c] - m) * rs);
         }
         s1 = warp_sum(s1) / (float)C;
         s2 = warp_sum(s2) / (float)C;
         float *dxr = dx + t * C;
-#pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-            const int c = lane + 32 * i;
-            if (c < C) dxr[c] += rs * (dn[i] - s1 - xh[i] * s2);
+#pragma unroll 4
+        for (int c = lane; c < C; c += 32) {
+            const float xh = (xr[c] - m) * rs, dn = dr[c] * w[c];
+            dxr[c] += rs * (dn - s1 - xh * s2);
         }
-    }
-    // warps add their column partials into shared memory one after another
-    // (fixed order), then the block's partial goes to `part`
-    for (int k = 0; k < 8; ++k) {
-        if (wid == k) {
-#pragma unroll
-            for (int i = 0; i < CPL; ++i) {
-                red[0][lane + 32 * i] = k == 0 ? pdw[i] : red[0][lane + 32 * i] + pdw[i];
-                red[1][lane + 32 * i] = k == 0 ? pdb[i] : red[1][lane + 32 * i] + pdb[i];
-            }
-        }
-        __syncthreads();
-    }
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        part[((long)blockIdx.x * 2 + 0) * C + c] = red[0][c];
-        part[((long)blockIdx.x * 2 + 1) * C + c] = red[1][c];
     }
 }
 
-__global__ void layernorm_bwd_reduce(const float *__restrict__ part, int nblocks, int C,
-                                     float *__restrict__ dw, float *__restrict__ db) {
+// Column partials of dw = sum_t dout * xhat and db = sum_t dout over a chunk
+// of rows: thread = column (coalesced across the warp), rows in order.
+// part layout [chunk][2][C]; layernorm_bwd_reduce adds them in chunk order.
+__global__ void __launch_bounds__(256)
+layernorm_bwd_dwdb_kernel(const float *__restrict__ dout, const float *__restrict__ x,
+                          const float *__restrict__ mean, const float *__restrict__ rstd,
+                          float *__restrict__ part, int T, int C, int rows_per_chunk) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= C) return;
+    const long r0 = (long)blockIdx.y * rows_per_chunk;
+    const long r1 = std::min<long>(T, r0 + rows_per_chunk);
     float a = 0.f, b = 0.f;
-    for (int k = 0; k < nblocks; ++k) {
-        a += part[((long)k * 2 + 0) * C + c];
-        b += part[((long)k * 2 + 1) * C + c];
+#pragma unroll 8
+    for (long t = r0; t < r1; ++t) {
+        const float d = dout[t * C + c];
+        a += d * ((x[t * C + c] - mean[t]) * rstd[t]);
+        b += d;
     }
-    dw[c] += a;
-    db[c] += b;
+    part[((long)blockIdx.y * 2 + 0) * C + c] = a;
+    part[((long)blockIdx.y * 2 + 1) * C + c] = b;
+}
+
+// dw/db += sum of the per-block partials, in block order. One block per 32
+// columns; warp w sums blocks k = w, w+8, ... and the 8 warp sums are added
+// in warp order, so the result is independent of scheduling.
+__global__ void __launch_bounds__(256)
+layernorm_bwd_reduce(const float *__restrict__ part, int nblocks, int C, float *__restrict__ dw,
+                     float *__restrict__ db) {
+    __shared__ float red[8][2][32];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x * 32 + lane;
+    float a = 0.f, b = 0.f;
+    if (c < C)
+        for (int k = wid; k < nblocks; k += 8) {
+            a += part[((long)k * 2 + 0) * C + c];
+            b += part[((long)k * 2 + 1) * C + c];
+        }
+    red[wid][0][lane] = a;
+    red[wid][1][lane] = b;
+    __syncthreads();
+    if (wid == 0 && c < C) {
+        float sa = 0.f, sb = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            sa += red[k][0][lane];
+            sb += red[k][1][lane];
+        }
+        dw[c] += sa;
+        db[c] += sb;
+    }
 }
 
 // ---------------------------------------------------------------- GELU
@@ -169,46 +177,75 @@ __global__ void causal_mask_kernel(float *__restrict__ s, int T) {
 }
 
 // ---------------------------------------------------------------- cross-entropy
-// One block per row of logits [rows, V] (pitch ldl). Writes probs (optional,
-// pitch ldp), dlogits = scale * (probs - onehot) (optional, pitch ldd; the
-// pad columns [V, ldd) are zeroed) and the row's NLL term
-// (l[tgt] - max) - log(sum) to rowterm[row] (src/ops.c:551-570).
+// (max, sum exp(x - max)) pairs, merged with rescaling (online softmax)
+__device__ __forceinline__ void ms_merge(float &m, float &sum, float m2, float s2) {
+    if (m2 == -INFINITY) return;
+    if (m == -INFINITY) { m = m2; sum = s2; return; }
+    if (m2 > m) { sum = sum * expf(m - m2) + s2; m = m2; }
+    else sum += s2 * expf(m2 - m);
+}
+
+// One block per row of logits [rows, V] (pitch ldl). One pass computes the
+// row max and sum of exp(x - max) together; a second writes probs (optional,
+// pitch ldp) and dlogits = scale * (probs - onehot) (optional, pitch ldd, pad
+// columns [V, ldd) zeroed), and the row's NLL term (l[tgt] - max) - log(sum)
+// goes to rowterm[row] (src/ops.c:551-570). The block reduction has a fixed
+// shape, so the result is deterministic.
 __global__ void __launch_bounds__(512)
 ce_fwd_kernel(const float *__restrict__ logits, long ldl, const int *__restrict__ targets,
               float *__restrict__ probs, long ldp, float *__restrict__ dlogits, long ldd,
               float scale, float *__restrict__ rowterm, int V) {
-    __shared__ float sh[32];
+    __shared__ float shm[16], shs[16];
     const long r = blockIdx.x;
     const float *lg = logits + r * ldl;
-    float mx = -INFINITY;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) mx = fmaxf(mx, lg[v]);
-    mx = block_reduce(mx, true, sh);
-    float s = 0.f;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) s += expf(lg[v] - mx);
-    s = block_reduce(s, false, sh);
-    const float inv = 1.0f / s;
+    float m = -INFINITY, sum = 0.f;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float x = lg[v];
+        if (x > m) { sum = (m == -INFINITY ? 0.f : sum * expf(m - x)) + 1.0f; m = x; }
+        else sum += expf(x - m);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, sum, o);
+        ms_merge(m, sum, m2, s2);
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) { shm[wid] = m; shs[wid] = sum; }
+    __syncthreads();
+    m = shm[0];
+    sum = shs[0];
+    for (int k = 1; k < nw; ++k) ms_merge(m, sum, shm[k], shs[k]);
+    const float inv = 1.0f / sum;
     const int tgt = targets ? targets[r] : -1;
     if (probs || dlogits) {
         float *pr = probs ? probs + r * ldp : nullptr;
         float *dl = dlogits ? dlogits + r * ldd : nullptr;
         for (int v = threadIdx.x; v < V; v += blockDim.x) {
-            const float p = expf(lg[v] - mx) * inv;
+            const float p = expf(lg[v] - m) * inv;
             if (pr) pr[v] = p;
             if (dl) dl[v] = scale * (p - (v == tgt ? 1.0f : 0.0f));
         }
         if (dl)
             for (long v = V + threadIdx.x; v < ldd; v += blockDim.x) dl[v] = 0.f;
     }
-    if (threadIdx.x == 0 && rowterm) rowterm[r] = tgt >= 0 ? (lg[tgt] - mx) - logf(s) : 0.f;
+    if (threadIdx.x == 0 && rowterm) rowterm[r] = tgt >= 0 ? (lg[tgt] - m) - logf(sum) : 0.f;
 }
 
-// loss = -(sum of row terms, in row order) / rows, as one float accumulator
-// like src/ops.c:503,548,573. Single thread: rows <= a few 10^4.
-__global__ void ce_loss_kernel(const float *__restrict__ rowterm, int rows, float *__restrict__ loss) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+// loss = -(sum of the row terms) / rows: 1024 threads each sum a fixed
+// strided subset, then a fixed-shape tree (deterministic; the reference sums
+// in row order in one float, src/ops.c:503,548,573).
+__global__ void __launch_bounds__(1024) ce_loss_kernel(const float *__restrict__ rowterm, int rows,
+                                                       float *__restrict__ loss) {
+    __shared__ float sh[1024];
     float acc = 0.f;
-    for (int r = 0; r < rows; ++r) acc -= rowterm[r];
-    *loss = acc / (float)rows;
+    for (int r = threadIdx.x; r < rows; r += 1024) acc += rowterm[r];
+    sh[threadIdx.x] = acc;
+    __syncthreads();
+    for (int w = 512; w > 0; w >>= 1) {
+        if ((int)threadIdx.x < w) sh[threadIdx.x] += sh[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *loss = -sh[0] / (float)rows;
 }
 
 __global__ void ce_bwd_kernel(float *__restrict__ dlogits, const float *__restrict__ probs,
@@ -385,25 +422,45 @@ embed_bwd_wte_kernel(const int *__restrict__ tok, const float *__restrict__ dx,
 // ---------------------------------------------------------------- AdamW
 // One fused pass (src/model.c:901-920): grads are first multiplied by the
 // clip factor computed on the device (identity when no clipping applies).
+// Four parameters per thread per iteration (16-byte loads and stores).
+__device__ __forceinline__ void adamw_one(float &p, float &g, float &m, float &v, unsigned char d,
+                                          float cf, bool scale, float lr, float b1, float b2,
+                                          float eps, float wd, float bc1, float bc2) {
+    if (scale) g *= cf;
+    m = b1 * m + (1.0f - b1) * g;
+    v = b2 * v + (1.0f - b2) * g * g;
+    const float mh = m / bc1, vh = v / bc2;
+    const float ewd = d ? wd : 0.0f;
+    p = p * (1.0f - lr * ewd) - lr * mh / (sqrtf(vh) + eps);
+}
+
 __global__ void adamw_kernel(float *__restrict__ p, float *__restrict__ g, float *__restrict__ m,
                              float *__restrict__ v, const unsigned char *__restrict__ decay, long n,
                              const float *__restrict__ clip_factor, float lr, float b1, float b2,
                              float eps, float wd, float bc1, float bc2) {
     const float cf = clip_factor ? *clip_factor : 1.0f;
     const bool scale = cf != 1.0f;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-        float gi = g[i];
-        if (scale) {
-            gi *= cf;
-            g[i] = gi;
-        }
-        const float mi = b1 * m[i] + (1.0f - b1) * gi;
-        const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
-        m[i] = mi;
-        v[i] = vi;
-        const float mh = mi / bc1, vh = vi / bc2;
-        const float ewd = decay[i] ? wd : 0.0f;
-        p[i] = p[i] * (1.0f - lr * ewd) - lr * mh / (sqrtf(vh) + eps);
+    const long n4 = n / 4;
+    const long stride = (long)gridDim.x * blockDim.x;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += stride) {
+        float4 P = ((float4 *)p)[i], G = ((float4 *)g)[i], Mm = ((float4 *)m)[i], Vv = ((float4 *)v)[i];
+        const uchar4 D = ((const uchar4 *)decay)[i];
+        adamw_one(P.x, G.x, Mm.x, Vv.x, D.x, cf, scale, lr, b1, b2, eps, wd, bc1, bc2);
+        adamw_one(P.y, G.y, Mm.y, Vv.y, D.y, cf, scale, lr, b1, b2, eps, wd, bc1, bc2);
+        adamw_one(P.z, G.z, Mm.z, Vv.z, D.z, cf, scale, lr, b1, b2, eps, wd, bc1, bc2);
+        adamw_one(P.w, G.w, Mm.w, Vv.w, D.w, cf, scale, lr, b1, b2, eps, wd, bc1, bc2);
+        ((float4 *)p)[i] = P;
+        if (scale) ((float4 *)g)[i] = G;
+        ((float4 *)m)[i] = Mm;
+        ((float4 *)v)[i] = Vv;
+    }
+    for (long i = n4 * 4 + blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += stride) {
+        float pp = p[i], gg = g[i], mm = m[i], vv = v[i];
+        adamw_one(pp, gg, mm, vv, decay[i], cf, scale, lr, b1, b2, eps, wd, bc1, bc2);
+        p[i] = pp;
+        g[i] = gg;
+        m[i] = mm;
+        v[i] = vv;
     }
 }
 
@@ -476,33 +533,24 @@ int layernorm_fwd(const float *x, long ldx, const float *w, const float *b, floa
     return OK;
 }
 
+constexpr int kLnBwdRowsPerChunk = 128;
+
 size_t layernorm_bwd_scratch_bytes(int T, int C) {
-    const int rpb = 64;
-    const long nb = (T + rpb - 1) / rpb;
-    return (size_t)nb * 2 * C * sizeof(float);
+    const long chunks = (T + kLnBwdRowsPerChunk - 1) / kLnBwdRowsPerChunk;
+    return (size_t)chunks * 2 * C * sizeof(float);
 }
 
 int layernorm_bwd(const float *dout, const float *x, const float *w, const float *mean,
                   const float *rstd, float *dx, float *dw, float *db, int T, int C, float *scratch,
                   cudaStream_t s) {
     if (T <= 0) return OK;
-    if (C > 2048) {
-        set_last_error(ERR_ARG, "layernorm_bwd: C=%d > 2048 unsupported", C);
-        return ERR_ARG;
-    }
-    const int rpb = 64;
-    const int nb = (T + rpb - 1) / rpb;
-    const int cpl = (C + 31) / 32;
-#define LNB(N) layernorm_bwd_kernel<N><<<nb, 256, 0, s>>>(dout, x, w, mean, rstd, dx, scratch, T, C, rpb)
-    if (cpl <= 4) LNB(4);
-    else if (cpl <= 8) LNB(8);
-    else if (cpl <= 16) LNB(16);
-    else if (cpl <= 32) LNB(32);
-    else if (cpl <= 50) LNB(50);
-    else LNB(64);
-#undef LNB
+    layernorm_bwd_dx_kernel<<<grid_for(T, 8, 148 * 16), 256, 0, s>>>(dout, x, w, mean, rstd, dx, T, C);
     LAUNCH_CHECK();
-    layernorm_bwd_reduce<<<(C + 255) / 256, 256, 0, s>>>(scratch, nb, C, dw, db);
+    const int chunks = (T + kLnBwdRowsPerChunk - 1) / kLnBwdRowsPerChunk;
+    dim3 g((C + 255) / 256, chunks);
+    layernorm_bwd_dwdb_kernel<<<g, 256, 0, s>>>(dout, x, mean, rstd, scratch, T, C, kLnBwdRowsPerChunk);
+    LAUNCH_CHECK();
+    layernorm_bwd_reduce<<<(C + 31) / 32, 256, 0, s>>>(scratch, chunks, C, dw, db);
     LAUNCH_CHECK();
     return OK;
 }
@@ -547,7 +595,7 @@ int cross_entropy_rows(const float *logits, long ldl, const int *targets, float 
 }
 
 int cross_entropy_loss(const float *rowterm, int rows, float *loss, cudaStream_t s) {
-    ce_loss_kernel<<<1, 32, 0, s>>>(rowterm, rows, loss);
+    ce_loss_kernel<<<1, 1024, 0, s>>>(rowterm, rows, loss);
     LAUNCH_CHECK();
     return OK;
 }
@@ -649,7 +697,11 @@ int adamw(float *p, float *g, float *m, float *v, const unsigned char *decay, lo
           const float *clip_factor, float lr, float b1, float b2, float eps, float wd, float bc1,
           float bc2, cudaStream_t s) {
     if (n <= 0) return OK;
-    adamw_kernel<<<grid_for(n, 256, 148 * 32), 256, 0, s>>>(p, g, m, v, decay, n, clip_factor, lr, b1,
+    if (((uintptr_t)p | (uintptr_t)g | (uintptr_t)m | (uintptr_t)v) % 16 || (uintptr_t)decay % 4) {
+        set_last_error(ERR_ARG, "adamw: arenas must be 16-byte aligned");
+        return ERR_ARG;
+    }
+    adamw_kernel<<<grid_for(n / 4 + 1, 256, 148 * 16), 256, 0, s>>>(p, g, m, v, decay, n, clip_factor, lr, b1,
                                                             b2, eps, wd, bc1, bc2);
     LAUNCH_CHECK();
     return OK;

@@ -10,7 +10,16 @@ namespace cg {
 namespace {
 int g_status = OK;
 char g_msg[512] = "";
-int g_precision = PREC_3XTF32;
+// CNGPT_CUDA_PRECISION = tf32 | 3xtf32 | fp32 selects the starting mode (the
+// reference's own test programs have no other way to choose it)
+int initial_precision() {
+    const char *e = getenv("CNGPT_CUDA_PRECISION");
+    if (!e) return PREC_3XTF32;
+    if (!strcmp(e, "tf32")) return PREC_TF32;
+    if (!strcmp(e, "fp32")) return PREC_FP32;
+    return PREC_3XTF32;
+}
+int g_precision = initial_precision();
 int g_sms = 0;
 }  // namespace
 

@@ -1,0 +1,88 @@
+"""Run a few GPT-2 training steps (or one GEMM shape) through libcngpt_cuda,
+for profilers (ncu) and quick timing.
+
+    python -m cngpt_b200.profile_step [--B 8] [--T 1024] [--layers 12] [--steps 1]
+                                      [--warmup 3] [--prec tf32|3xtf32|fp32]
+    python -m cngpt_b200.profile_step --gemm M N K [--a-mn] [--b-mn] [--reps 3]
+
+Token ids live on the device before the first step; nothing else runs.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+from cngpt_b200 import abi  # noqa: E402
+
+PREC = {"tf32": abi.PREC_TF32, "3xtf32": abi.PREC_3XTF32, "fp32": abi.PREC_FP32}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--B", type=int, default=8)
+    ap.add_argument("--T", type=int, default=1024)
+    ap.add_argument("--layers", type=int, default=12)
+    ap.add_argument("--steps", type=int, default=1)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--prec", choices=list(PREC), default="tf32")
+    ap.add_argument("--gemm", type=int, nargs=3, metavar=("M", "N", "K"))
+    ap.add_argument("--a-mn", action="store_true")
+    ap.add_argument("--b-mn", action="store_true")
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--epi", choices=["store", "gelu", "resid", "accum", "gelu_bwd"], default="store")
+    a = ap.parse_args()
+    import torch
+    torch.cuda.set_device(0)
+    lib = abi.load()
+    lib.cngpt_cuda_set_precision(PREC[a.prec])
+    if a.gemm:
+        M, N, K = a.gemm
+        A = torch.randn((K, M) if a.a_mn else (M, K), device="cuda")
+        B = torch.randn((K, N) if a.b_mn else (N, K), device="cuda")
+        D = torch.zeros(M, N, device="cuda")
+        D2 = torch.empty(M, N, device="cuda") if a.epi in ("gelu", "resid") else D
+        R = torch.randn(M, N, device="cuda") if a.epi in ("resid", "gelu_bwd") else D
+        bias = torch.zeros(N, device="cuda")
+        mode = {"store": abi.EPI_STORE, "gelu": abi.EPI_GELU, "resid": abi.EPI_RESID,
+                "accum": abi.EPI_ACCUM, "gelu_bwd": abi.EPI_GELU_BWD}[a.epi]
+        for _ in range(a.reps):
+            abi.check(lib, lib.cngpt_cuda_gemm(A.data_ptr(), A.shape[1], int(a.a_mn), B.data_ptr(), B.shape[1],
+                                               int(a.b_mn), M, N, K, mode, 1.0, D.data_ptr(), N,
+                                               bias.data_ptr(), D2.data_ptr(), N, R.data_ptr(), N,
+                                               R.data_ptr(), N), "gemm")
+        abi.check(lib, lib.cngpt_cuda_check(), "sync")
+        print(f"gemm {M}x{N}x{K} done")
+        return
+    m = abi.GPT()
+    assert lib.gpt_init(C.byref(m), abi.GPTConfig(a.layers, 12, 768, 50257, 1024, 0.0)) == 0
+    C.CDLL(None).srand(1)
+    lib.gpt_init_weights(C.byref(m))
+    rng = np.random.default_rng(0)
+    ids = torch.from_numpy(rng.integers(0, 50257, a.B * a.T + 1).astype(np.int32)).cuda()
+    tok, tgt = ids[:-1].contiguous(), ids[1:].contiguous()
+    loss = C.c_float()
+    for i in range(a.warmup + a.steps):
+        if i == a.warmup:
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+        abi.check(lib, lib.cngpt_cuda_train_step(C.byref(m), tok.data_ptr(), tgt.data_ptr(), a.B, a.T, 1e-4,
+                                                 0.9, 0.95, 1e-8, 0.1, 1.0, None), "step")
+    abi.check(lib, lib.cngpt_cuda_check(), "sync")
+    dt = (time.perf_counter() - t0) / max(a.steps, 1)
+    abi.check(lib, lib.cngpt_cuda_last_loss(C.byref(m), C.byref(loss)), "loss")
+    print(f"{a.steps} step(s) B={a.B} T={a.T} L={a.layers} prec={a.prec}: {dt * 1e3:.2f} ms/step "
+          f"(host wall), loss {loss.value:.4f}")
+    lib.gpt_free(C.byref(m))
+
+
+if __name__ == "__main__":
+    main()

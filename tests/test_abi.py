@@ -1,0 +1,117 @@
+"""The C-ABI boundary, checked without a GPU.
+
+- libcngpt_cuda.so loads and exports every function that include/*.h declares;
+- the drop-in headers declare every function of the reference's ops.h,
+  model.h and fast.h with the same signature;
+- GPT, GPTConfig, GPTWeights, GPTActivations, FastCtx and GPTHeader are
+  byte-identical to the reference's (offset of every field, compiled by gcc
+  against both headers), so code compiled against either header links here;
+- the ctypes mirror in cngpt_b200/abi.py matches the C layout.
+"""
+import ctypes as C
+import re
+import subprocess
+import tempfile
+from pathlib import Path
+
+import pytest
+
+from cngpt_b200 import abi
+
+ROOT = Path(__file__).resolve().parents[1]
+INC = ROOT / "include"
+REF_SRC = Path("/root/reference/src")
+
+
+def declared_functions(path: Path) -> set[str]:
+    txt = re.sub(r"/\*.*?\*/", "", path.read_text(), flags=re.S)
+    txt = re.sub(r"//[^\n]*", "", txt)
+    names = set()
+    for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b([a-z_][a-z0-9_]*)\s*\(", txt, re.M):
+        name = m.group(1)
+        if name not in {"if", "for", "while", "return", "sizeof"} and not name.startswith("__"):
+            names.add(name)
+    return names
+
+
+def exported_symbols(path: Path) -> set[str]:
+    out = subprocess.run(["nm", "-D", "--defined-only", str(path)], capture_output=True, text=True,
+                         check=True).stdout
+    return {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = abi.load()  # dlopen works without a GPU: no CUDA call happens at load
+    assert lib is not None
+    syms = exported_symbols(abi.LIB_PATH)
+    declared = set()
+    for h in sorted(INC.rglob("*.h")):
+        declared |= declared_functions(h)
+    assert declared, "no declarations parsed"
+    missing = sorted(declared - syms)
+    assert not missing, f"declared but not exported: {missing}"
+    for name in list(abi.DROPIN_SIGNATURES) + list(abi.EXT_SIGNATURES):
+        assert name in syms, name
+
+
+@pytest.mark.skipif(not REF_SRC.exists(), reason="reference tree absent")
+def test_dropin_headers_cover_reference_api():
+    for h in ("ops.h", "model.h", "fast.h"):
+        ref = declared_functions(REF_SRC / h)
+        ours = declared_functions(INC / "cngpt" / h)
+        assert ref <= ours, f"{h}: missing {sorted(ref - ours)}"
+
+
+LAYOUT_C = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "model.h"
+#include "fast.h"
+#define F(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
+int main(void) {
+  printf("GPT %zu\nGPTConfig %zu\nGPTWeights %zu\nGPTActivations %zu\nFastCtx %zu\nGPTHeader %zu\n",
+         sizeof(GPT), sizeof(GPTConfig), sizeof(GPTWeights), sizeof(GPTActivations),
+         sizeof(FastCtx), sizeof(GPTHeader));
+  F(GPT, cfg) F(GPT, params) F(GPT, grads) F(GPT, acts) F(GPT, param_buf) F(GPT, grad_buf)
+  F(GPT, act_buf) F(GPT, mask_buf) F(GPT, m_buf) F(GPT, v_buf) F(GPT, decay_buf)
+  F(GPT, n_params) F(GPT, step)
+  F(GPTActivations, emb) F(GPTActivations, qkv) F(GPTActivations, attn_scores) F(GPTActivations, res2)
+  F(GPTActivations, ln_f_out) F(GPTActivations, logits) F(GPTActivations, probs)
+  F(GPTActivations, emb_mask) F(GPTActivations, res2_mask)
+  F(GPTWeights, wte) F(GPTWeights, c_attn_w) F(GPTWeights, mlp_proj_b) F(GPTWeights, ln_f_b)
+  F(FastCtx, x) F(FastCtx, scores) F(FastCtx, logits)
+  return 0;
+}
+"""
+
+
+def _layout(include_dir: Path) -> str:
+    with tempfile.TemporaryDirectory() as d:
+        src = Path(d) / "l.c"
+        src.write_text(LAYOUT_C)
+        exe = Path(d) / "l"
+        subprocess.run(["/usr/bin/gcc" if Path("/usr/bin/gcc").exists() else "gcc", "-std=c11",
+                        f"-I{include_dir}", str(src), "-o", str(exe)], check=True)
+        return subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+
+
+def test_struct_layout_matches_ctypes_mirror():
+    lines = dict(ln.rsplit(" ", 1) for ln in _layout(INC / "cngpt").splitlines())
+    assert int(lines["GPT"]) == C.sizeof(abi.GPT)
+    assert int(lines["FastCtx"]) == C.sizeof(abi.FastCtx)
+    assert int(lines["GPTActivations"]) == C.sizeof(abi.GPTActivations)
+    assert int(lines["GPT.n_params"]) == abi.GPT.n_params.offset
+    assert int(lines["GPT.param_buf"]) == abi.GPT.param_buf.offset
+
+
+@pytest.mark.skipif(not REF_SRC.exists(), reason="reference tree absent")
+def test_struct_layout_identical_to_reference():
+    assert _layout(INC / "cngpt") == _layout(REF_SRC)
+
+
+def test_num_params_formula():
+    lib = abi.load()
+    for cfg, n in [((12, 12, 768, 50257, 1024), 124439808), ((24, 16, 1024, 50257, 1024), 354823168),
+                   ((48, 25, 1600, 50257, 1024), 1557611200), ((6, 6, 384, 65, 256), 10770816)]:
+        c = abi.GPTConfig(*cfg, 0.0)
+        assert lib.gpt_num_params(C.byref(c)) == n
