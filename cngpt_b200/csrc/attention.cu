@@ -42,15 +42,24 @@ __device__ __forceinline__ void mma8(float (&d)[4], const uint32_t (&a)[4], cons
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-// d += a * b with fp32 operands, TF32 or 3xTF32 depending on SPLIT.
+// d += a * b with fp32 operands. TF32 mode passes the fp32 bit patterns
+// straight to the tensor core, which reads them as tf32 (dropping the low 13
+// mantissa bits); 3xTF32 mode splits each operand into rna-rounded hi/lo
+// parts and issues lo*hi + hi*lo + hi*hi.
 template <bool SPLIT>
 __device__ __forceinline__ void mma_f32(float (&d)[4], const float (&a)[4], const float (&b)[2]) {
     uint32_t ah[4], bh[2];
+    if constexpr (!SPLIT) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) ah[i] = to_tf32(a[i]);
+        for (int i = 0; i < 4; ++i) ah[i] = __float_as_uint(a[i]);
 #pragma unroll
-    for (int i = 0; i < 2; ++i) bh[i] = to_tf32(b[i]);
-    if (SPLIT) {
+        for (int i = 0; i < 2; ++i) bh[i] = __float_as_uint(b[i]);
+        mma8(d, ah, bh);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ah[i] = to_tf32(a[i]);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) bh[i] = to_tf32(b[i]);
         uint32_t al[4], bl[2];
 #pragma unroll
         for (int i = 0; i < 4; ++i) al[i] = to_tf32(a[i] - __uint_as_float(ah[i]));
@@ -58,8 +67,8 @@ __device__ __forceinline__ void mma_f32(float (&d)[4], const float (&a)[4], cons
         for (int i = 0; i < 2; ++i) bl[i] = to_tf32(b[i] - __uint_as_float(bh[i]));
         mma8(d, al, bh);
         mma8(d, ah, bl);
+        mma8(d, ah, bh);
     }
-    mma8(d, ah, bh);
 }
 
 // Key order inside an 8-wide n-tile: accumulator column n holds key sig(n), so
@@ -67,33 +76,62 @@ __device__ __forceinline__ void mma_f32(float (&d)[4], const float (&a)[4], cons
 // A-fragment columns it needs when the result feeds the next product.
 __device__ __forceinline__ int sig(int n) { return (n >> 1) + 4 * (n & 1); }
 
-// Load a [rows x 64] tile with row pitch `ld` (floats) into smem [rows][LDS];
-// rows >= valid are zero-filled.
-__device__ __forceinline__ void load_tile(float *dst, const float *src, long ld, int rows,
-                                          int valid) {
+// Load a [rows x 64] tile with row pitch `ld` (floats) into smem [rows][LDS]
+// with cp.async (16 bytes per copy; rows >= valid are zero-filled), so the
+// copy of the next tile overlaps the math on the current one.
+__device__ __forceinline__ void load_tile_async(float *dst, const float *src, long ld, int rows,
+                                                int valid) {
     for (int i = threadIdx.x; i < rows * (HS / 4); i += blockDim.x) {
         const int r = i / (HS / 4), c4 = i % (HS / 4);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (r < valid) v = *(const float4 *)(src + (long)r * ld + c4 * 4);
-        *(float4 *)(dst + r * LDS + c4 * 4) = v;
+        const bool ok = r < valid;
+        const float *g = src + (long)(ok ? r : 0) * ld + c4 * 4;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
+                     ::"r"(smem_u32(dst + r * LDS + c4 * 4)), "l"(g), "r"(ok ? 16 : 0) : "memory");
     }
 }
 
-// A fragment (16 rows x 8 cols starting at row r0, col k0) from smem [.][LDS]
-__device__ __forceinline__ void frag_a(float (&a)[4], const float *s, int r0, int k0, int g, int t) {
-    a[0] = s[(r0 + g) * LDS + k0 + t];
-    a[1] = s[(r0 + g + 8) * LDS + k0 + t];
-    a[2] = s[(r0 + g) * LDS + k0 + t + 4];
-    a[3] = s[(r0 + g + 8) * LDS + k0 + t + 4];
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// ldmatrix.x4: four 8x(16-byte) matrices; lane l gives the address of row
+// l % 8 of matrix l / 8 and receives, from each matrix, the 32-bit word at
+// (row l / 4, word l % 4) - which for 32-bit data is a tf32 mma fragment
+// element. Rows are 272 bytes apart (LDS = 68 floats): conflict-free.
+__device__ __forceinline__ void ldsm4(float (&r)[4], const float *p) {
+    uint32_t x0, x1, x2, x3;
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3) : "r"(smem_u32(p)));
+    r[0] = __uint_as_float(x0);
+    r[1] = __uint_as_float(x1);
+    r[2] = __uint_as_float(x2);
+    r[3] = __uint_as_float(x3);
 }
 
-// B fragment where the operand's n index runs over smem rows (permuted by
-// sig) and k over smem columns: element (k, n) = s[(n0 + sig(n))][k0 + k].
-__device__ __forceinline__ void frag_b_rows(float (&b)[2], const float *s, int n0, int k0, int g,
-                                            int t) {
-    b[0] = s[(n0 + sig(g)) * LDS + k0 + t];
-    b[1] = s[(n0 + sig(g)) * LDS + k0 + t + 4];
+// A fragment (16 rows x 8 cols starting at row r0, col k0) from smem [.][LDS]:
+// matrices (rows 0-7, cols 0-3), (rows 8-15, cols 0-3), (0-7, 4-7), (8-15, 4-7)
+__device__ __forceinline__ void frag_a(float (&a)[4], const float *s, int r0, int k0, int lane) {
+    const int mat = lane >> 3, rr = lane & 7;
+    ldsm4(a, s + (r0 + rr + (mat & 1) * 8) * LDS + k0 + (mat >> 1) * 4);
 }
+
+// B fragments of two consecutive k-steps (k0 and k0+8) where the operand's n
+// index runs over smem rows, permuted by sig, and k over smem columns:
+// element (k, n) = s[n0 + sig(n)][k]. b[0..1] is the k0 step, b[2..3] k0+8.
+__device__ __forceinline__ void frag_b_rows2(float (&b)[4], const float *s, int n0, int k0, int lane) {
+    const int mat = lane >> 3, rr = lane & 7;
+    ldsm4(b, s + (n0 + sig(rr)) * LDS + k0 + mat * 4);
+}
+
+// 2^x on the special-function unit (ex2.approx; |rel. err| ~ 2^-22)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
 
 // B fragment where k runs over smem rows and n over smem columns:
 // element (k, n) = s[(k0 + k)][n0 + n].
@@ -104,102 +142,128 @@ __device__ __forceinline__ void frag_b_cols(float (&b)[2], const float *s, int k
 }
 
 // ------------------------------------------------------------- forward
+// One block per (batch*head, 128-query tile), 8 warps of 16 query rows; key
+// tiles of 64 stream through a double-buffered shared-memory ring.
+constexpr int FQ = 128;
+
 template <bool SPLIT>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 attn_fwd_mma_kernel(const float *__restrict__ qkv, float *__restrict__ out, float *__restrict__ lse,
                     int T, int C, int H, float scale) {
     extern __shared__ float sm[];
-    float *sQ = sm, *sK = sm + TQ * LDS, *sV = sm + 2 * TQ * LDS;
-    const int nqt = (T + TQ - 1) / TQ;
+    float *sQ = sm;
+    float *sK[2] = {sm + FQ * LDS, sm + (FQ + TK) * LDS};
+    float *sV[2] = {sm + (FQ + 2 * TK) * LDS, sm + (FQ + 3 * TK) * LDS};
+    const int nqt = (T + FQ - 1) / FQ;
     const int qt = nqt - 1 - blockIdx.x;  // heaviest tiles first
     const int bh = blockIdx.y, b = bh / H, h = bh % H;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const long ld = 3L * C;
     const float *base = qkv + (long)b * T * ld;
-    const int q0 = qt * TQ;
-    load_tile(sQ, base + (long)q0 * ld + h * HS, ld, TQ, min(TQ, T - q0));
+    const int q0 = qt * FQ;
+    const int nkt = (min(T, q0 + FQ) + TK - 1) / TK;
+    load_tile_async(sQ, base + (long)q0 * ld + h * HS, ld, FQ, min(FQ, T - q0));
+    load_tile_async(sK[0], base + C + h * HS, ld, TK, min(TK, T));
+    load_tile_async(sV[0], base + 2 * C + h * HS, ld, TK, min(TK, T));
+    cp_async_commit();
 
     float o[8][4] = {};
     float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
     const int row0 = q0 + warp * 16 + g, row1 = row0 + 8;
 
-    for (int kt = 0; kt <= qt; ++kt) {
-        const int k0 = kt * TK;
+    for (int kt = 0; kt < nkt; ++kt) {
+        const int k0 = kt * TK, buf = kt & 1;
+        if (kt + 1 < nkt) {
+            const int k1 = k0 + TK;
+            load_tile_async(sK[buf ^ 1], base + (long)k1 * ld + C + h * HS, ld, TK, min(TK, T - k1));
+            load_tile_async(sV[buf ^ 1], base + (long)k1 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k1));
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
         __syncthreads();
-        load_tile(sK, base + (long)k0 * ld + C + h * HS, ld, TK, min(TK, T - k0));
-        load_tile(sV, base + (long)k0 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k0));
-        __syncthreads();
-        float s[8][4] = {};
+        if (k0 <= q0 + warp * 16 + 15) {  // else every key of the tile is in this warp's future
+            const float *cK = sK[buf], *cV = sV[buf];
+            float s[8][4] = {};
 #pragma unroll
-        for (int kk = 0; kk < HS / 8; ++kk) {
-            float a[4];
-            frag_a(a, sQ, warp * 16, kk * 8, g, t);
+            for (int kk = 0; kk < HS / 8; kk += 2) {
+                float a0[4], a1[4];
+                frag_a(a0, sQ, warp * 16, kk * 8, lane);
+                frag_a(a1, sQ, warp * 16, kk * 8 + 8, lane);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float bb[4];
+                    frag_b_rows2(bb, cK, j * 8, kk * 8, lane);
+                    const float b0[2] = {bb[0], bb[1]}, b1[2] = {bb[2], bb[3]};
+                    mma_f32<SPLIT>(s[j], a0, b0);
+                    mma_f32<SPLIT>(s[j], a1, b1);
+                }
+            }
+            // scores in log2 units: s * scale * log2(e); the row max and the
+            // probabilities use ex2 (the first processed tile, k0 = 0, always
+            // holds key 0 <= row, so the running max is finite from then on)
+            const float sl2 = scale * LOG2E;
+            float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float bb[2];
-                frag_b_rows(bb, sK, j * 8, kk * 8, g, t);
-                mma_f32<SPLIT>(s[j], a, bb);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int key = k0 + j * 8 + t + ((e & 1) ? 4 : 0);
+                    const int row = (e < 2) ? row0 : row1;
+                    float v = s[j][e] * sl2;
+                    if (key > row || key >= T) v = -INFINITY;
+                    s[j][e] = v;
+                    mx[e >> 1] = fmaxf(mx[e >> 1], v);
+                }
             }
-        }
-        // scale, mask (future keys and keys past T), row max
-        float mx[2] = {-INFINITY, -INFINITY};
+            float corr[2];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = k0 + j * 8 + t + ((e & 1) ? 4 : 0);
-                const int row = (e < 2) ? row0 : row1;
-                float v = s[j][e] * scale;
-                if (key > row || key >= T) v = -INFINITY;
-                s[j][e] = v;
-                mx[e >> 1] = fmaxf(mx[e >> 1], v);
+            for (int r = 0; r < 2; ++r) {
+                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+                const float mnew = fmaxf(m_r[r], mx[r]);
+                corr[r] = ex2(m_r[r] - mnew);
+                m_r[r] = mnew;
             }
-        }
-        float corr[2];
+            float ls[2] = {0.f, 0.f};
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-            const float mnew = fmaxf(m_r[r], mx[r]);
-            corr[r] = (m_r[r] == -INFINITY) ? 0.f : expf(m_r[r] - mnew);
-            m_r[r] = mnew;
-        }
-        float ls[2] = {0.f, 0.f};
+            for (int j = 0; j < 8; ++j) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float mrow = m_r[e >> 1];
-                const float p = (s[j][e] == -INFINITY) ? 0.f : expf(s[j][e] - mrow);
-                s[j][e] = p;
-                ls[e >> 1] += p;
+                for (int e = 0; e < 4; ++e) {
+                    const float p = ex2(s[j][e] - m_r[e >> 1]);
+                    s[j][e] = p;
+                    ls[e >> 1] += p;
+                }
             }
-        }
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
-            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
-            l_r[r] = l_r[r] * corr[r] + ls[r];
-        }
-#pragma unroll
-        for (int dn = 0; dn < 8; ++dn) {
-            o[dn][0] *= corr[0];
-            o[dn][1] *= corr[0];
-            o[dn][2] *= corr[1];
-            o[dn][3] *= corr[1];
-        }
-        // O += P V ; P's C fragment of key tile j is the A fragment {c0, c2, c1, c3}
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float a[4] = {s[j][0], s[j][2], s[j][1], s[j][3]};
+            for (int r = 0; r < 2; ++r) {
+                ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
+                ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
+                l_r[r] = l_r[r] * corr[r] + ls[r];
+            }
 #pragma unroll
             for (int dn = 0; dn < 8; ++dn) {
-                float bb[2];
-                frag_b_cols(bb, sV, j * 8, dn * 8, g, t);
-                mma_f32<SPLIT>(o[dn], a, bb);
+                o[dn][0] *= corr[0];
+                o[dn][1] *= corr[0];
+                o[dn][2] *= corr[1];
+                o[dn][3] *= corr[1];
+            }
+            // O += P V ; P's C fragment of key tile j is the A fragment {c0, c2, c1, c3}
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float a[4] = {s[j][0], s[j][2], s[j][1], s[j][3]};
+#pragma unroll
+                for (int dn = 0; dn < 8; ++dn) {
+                    float bb[2];
+                    frag_b_cols(bb, cV, j * 8, dn * 8, g, t);
+                    mma_f32<SPLIT>(o[dn], a, bb);
+                }
             }
         }
+        __syncthreads();  // the next iteration's prefetch overwrites this buffer
     }
+    if (row0 >= T && row1 >= T) return;
     const float inv0 = 1.0f / l_r[0], inv1 = 1.0f / l_r[1];
 #pragma unroll
     for (int dn = 0; dn < 8; ++dn) {
@@ -209,9 +273,9 @@ attn_fwd_mma_kernel(const float *__restrict__ qkv, float *__restrict__ out, floa
         if (row1 < T)
             *(float2 *)(out + ((long)b * T + row1) * C + col) = make_float2(o[dn][2] * inv1, o[dn][3] * inv1);
     }
-    if (lse && t == 0) {
-        if (row0 < T) lse[(long)bh * T + row0] = m_r[0] + logf(l_r[0]);
-        if (row1 < T) lse[(long)bh * T + row1] = m_r[1] + logf(l_r[1]);
+    if (lse && t == 0) {  // natural-log units: (m2 + log2 l) * ln 2
+        if (row0 < T) lse[(long)bh * T + row0] = m_r[0] * LN2 + logf(l_r[0]);
+        if (row1 < T) lse[(long)bh * T + row1] = m_r[1] * LN2 + logf(l_r[1]);
     }
 }
 
@@ -234,15 +298,18 @@ __global__ void attn_bwd_dot_kernel(const float *__restrict__ out, const float *
     }
 }
 
-// dK, dV for one 64-key tile; loops over query tiles qt >= kt.
+// dK, dV for one 64-key tile; loops over query tiles qt >= kt with the next
+// Q / dO tile prefetched while the current one is used.
 template <bool SPLIT>
 __global__ void __launch_bounds__(128)
 attn_bwd_dkdv_kernel(const float *__restrict__ qkv, const float *__restrict__ dout,
                      const float *__restrict__ lse, const float *__restrict__ Dd,
                      float *__restrict__ dqkv, int T, int C, int H, float scale) {
     extern __shared__ float sm[];
-    float *sK = sm, *sV = sm + TK * LDS, *sQ = sm + 2 * TK * LDS, *sO = sm + 3 * TK * LDS;
-    float *sL = sm + 4 * TK * LDS, *sD = sL + TQ;
+    float *sK = sm, *sV = sm + TK * LDS;
+    float *sQ[2] = {sm + 2 * TK * LDS, sm + (2 * TK + TQ) * LDS};
+    float *sO[2] = {sm + (2 * TK + 2 * TQ) * LDS, sm + (2 * TK + 3 * TQ) * LDS};
+    float *sLD = sm + (2 * TK + 4 * TQ) * LDS;  // [2][2][TQ]: lse, D per buffer
     const int nkt = (T + TK - 1) / TK;
     const int kt = blockIdx.x;  // tile 0 has the most work: launched first
     const int bh = blockIdx.y, b = bh / H, h = bh % H;
@@ -251,35 +318,53 @@ attn_bwd_dkdv_kernel(const float *__restrict__ qkv, const float *__restrict__ do
     const float *base = qkv + (long)b * T * ld;
     const float *dob = dout + (long)b * T * C;
     const int k0 = kt * TK;
-    load_tile(sK, base + (long)k0 * ld + C + h * HS, ld, TK, min(TK, T - k0));
-    load_tile(sV, base + (long)k0 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k0));
+    auto load_q = [&](int qt, int buf) {
+        const int q0 = qt * TQ;
+        load_tile_async(sQ[buf], base + (long)q0 * ld + h * HS, ld, TQ, min(TQ, T - q0));
+        load_tile_async(sO[buf], dob + (long)q0 * C + h * HS, C, TQ, min(TQ, T - q0));
+        for (int i = threadIdx.x; i < TQ; i += blockDim.x) {
+            const int q = q0 + i;
+            sLD[buf * 2 * TQ + i] = q < T ? lse[(long)bh * T + q] : 0.f;
+            sLD[buf * 2 * TQ + TQ + i] = q < T ? Dd[(long)bh * T + q] : 0.f;
+        }
+    };
+    load_tile_async(sK, base + (long)k0 * ld + C + h * HS, ld, TK, min(TK, T - k0));
+    load_tile_async(sV, base + (long)k0 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k0));
+    load_q(kt, 0);
+    cp_async_commit();
     float dk[8][4] = {}, dv[8][4] = {};
     const int key0 = k0 + warp * 16 + g, key1 = key0 + 8;
     for (int qt = kt; qt < nkt; ++qt) {
-        const int q0 = qt * TQ;
-        __syncthreads();
-        load_tile(sQ, base + (long)q0 * ld + h * HS, ld, TQ, min(TQ, T - q0));
-        load_tile(sO, dob + (long)q0 * C + h * HS, C, TQ, min(TQ, T - q0));
-        for (int i = threadIdx.x; i < TQ; i += blockDim.x) {
-            const int q = q0 + i;
-            sL[i] = q < T ? lse[(long)bh * T + q] : 0.f;
-            sD[i] = q < T ? Dd[(long)bh * T + q] : 0.f;
+        const int q0 = qt * TQ, buf = (qt - kt) & 1;
+        if (qt + 1 < nkt) {
+            load_q(qt + 1, buf ^ 1);
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
+        const float *cQ = sQ[buf], *cO = sO[buf], *cL = sLD + buf * 2 * TQ, *cD = cL + TQ;
         // S^T = K Q^T and dP^T = V dO^T  (rows: this warp's 16 keys, cols: 64 queries)
         float st[8][4] = {}, dpt[8][4] = {};
 #pragma unroll
-        for (int kk = 0; kk < HS / 8; ++kk) {
-            float ak[4], av[4];
-            frag_a(ak, sK, warp * 16, kk * 8, g, t);
-            frag_a(av, sV, warp * 16, kk * 8, g, t);
+        for (int kk = 0; kk < HS / 8; kk += 2) {
+            float ak0[4], ak1[4], av0[4], av1[4];
+            frag_a(ak0, sK, warp * 16, kk * 8, lane);
+            frag_a(ak1, sK, warp * 16, kk * 8 + 8, lane);
+            frag_a(av0, sV, warp * 16, kk * 8, lane);
+            frag_a(av1, sV, warp * 16, kk * 8 + 8, lane);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float bq[2], bo[2];
-                frag_b_rows(bq, sQ, j * 8, kk * 8, g, t);
-                frag_b_rows(bo, sO, j * 8, kk * 8, g, t);
-                mma_f32<SPLIT>(st[j], ak, bq);
-                mma_f32<SPLIT>(dpt[j], av, bo);
+                float bq[4], bo[4];
+                frag_b_rows2(bq, cQ, j * 8, kk * 8, lane);
+                frag_b_rows2(bo, cO, j * 8, kk * 8, lane);
+                const float q0b[2] = {bq[0], bq[1]}, q1b[2] = {bq[2], bq[3]};
+                const float o0b[2] = {bo[0], bo[1]}, o1b[2] = {bo[2], bo[3]};
+                mma_f32<SPLIT>(st[j], ak0, q0b);
+                mma_f32<SPLIT>(st[j], ak1, q1b);
+                mma_f32<SPLIT>(dpt[j], av0, o0b);
+                mma_f32<SPLIT>(dpt[j], av1, o1b);
             }
         }
         // P^T = exp(S^T*scale - lse[q]) (0 where q < key), dS^T = P^T (dP^T - D[q])
@@ -291,9 +376,9 @@ attn_bwd_dkdv_kernel(const float *__restrict__ qkv, const float *__restrict__ do
                 const int q = q0 + qi;
                 const int key = (e < 2) ? key0 : key1;
                 float p = 0.f;
-                if (q >= key && q < T && key < T) p = expf(st[j][e] * scale - sL[qi]);
+                if (q >= key && q < T && key < T) p = ex2((st[j][e] * scale - cL[qi]) * LOG2E);
                 st[j][e] = p;
-                dpt[j][e] = p * (dpt[j][e] - sD[qi]);
+                dpt[j][e] = p * (dpt[j][e] - cD[qi]);
             }
         }
         // dV += P^T dO ; dK += dS^T Q
@@ -304,12 +389,13 @@ attn_bwd_dkdv_kernel(const float *__restrict__ qkv, const float *__restrict__ do
 #pragma unroll
             for (int dn = 0; dn < 8; ++dn) {
                 float bo[2], bq[2];
-                frag_b_cols(bo, sO, j * 8, dn * 8, g, t);
-                frag_b_cols(bq, sQ, j * 8, dn * 8, g, t);
+                frag_b_cols(bo, cO, j * 8, dn * 8, g, t);
+                frag_b_cols(bq, cQ, j * 8, dn * 8, g, t);
                 mma_f32<SPLIT>(dv[dn], ap, bo);
                 mma_f32<SPLIT>(dk[dn], as, bq);
             }
         }
+        __syncthreads();  // the next iteration's prefetch overwrites this buffer
     }
     float *dkb = dqkv + (long)b * T * ld + C + h * HS;
     float *dvb = dqkv + (long)b * T * ld + 2 * C + h * HS;
@@ -327,14 +413,17 @@ attn_bwd_dkdv_kernel(const float *__restrict__ qkv, const float *__restrict__ do
     }
 }
 
-// dQ for one 64-query tile; loops over key tiles kt <= qt.
+// dQ for one 64-query tile; loops over key tiles kt <= qt with the next K / V
+// tile prefetched while the current one is used.
 template <bool SPLIT>
 __global__ void __launch_bounds__(128)
 attn_bwd_dq_kernel(const float *__restrict__ qkv, const float *__restrict__ dout,
                    const float *__restrict__ lse, const float *__restrict__ Dd,
                    float *__restrict__ dqkv, int T, int C, int H, float scale) {
     extern __shared__ float sm[];
-    float *sQ = sm, *sO = sm + TQ * LDS, *sK = sm + 2 * TQ * LDS, *sV = sm + 3 * TQ * LDS;
+    float *sQ = sm, *sO = sm + TQ * LDS;
+    float *sK[2] = {sm + 2 * TQ * LDS, sm + (2 * TQ + TK) * LDS};
+    float *sV[2] = {sm + (2 * TQ + 2 * TK) * LDS, sm + (2 * TQ + 3 * TK) * LDS};
     const int nqt = (T + TQ - 1) / TQ;
     const int qt = nqt - 1 - blockIdx.x;
     const int bh = blockIdx.y, b = bh / H, h = bh % H;
@@ -342,8 +431,11 @@ attn_bwd_dq_kernel(const float *__restrict__ qkv, const float *__restrict__ dout
     const long ld = 3L * C;
     const float *base = qkv + (long)b * T * ld;
     const int q0 = qt * TQ;
-    load_tile(sQ, base + (long)q0 * ld + h * HS, ld, TQ, min(TQ, T - q0));
-    load_tile(sO, dout + ((long)b * T + q0) * C + h * HS, C, TQ, min(TQ, T - q0));
+    load_tile_async(sQ, base + (long)q0 * ld + h * HS, ld, TQ, min(TQ, T - q0));
+    load_tile_async(sO, dout + ((long)b * T + q0) * C + h * HS, C, TQ, min(TQ, T - q0));
+    load_tile_async(sK[0], base + C + h * HS, ld, TK, min(TK, T));
+    load_tile_async(sV[0], base + 2 * C + h * HS, ld, TK, min(TK, T));
+    cp_async_commit();
     const int row0 = q0 + warp * 16 + g, row1 = row0 + 8;
     const float L0 = row0 < T ? lse[(long)bh * T + row0] : 0.f;
     const float L1 = row1 < T ? lse[(long)bh * T + row1] : 0.f;
@@ -351,24 +443,37 @@ attn_bwd_dq_kernel(const float *__restrict__ qkv, const float *__restrict__ dout
     const float D1 = row1 < T ? Dd[(long)bh * T + row1] : 0.f;
     float dq[8][4] = {};
     for (int kt = 0; kt <= qt; ++kt) {
-        const int k0 = kt * TK;
+        const int k0 = kt * TK, buf = kt & 1;
+        if (kt + 1 <= qt) {
+            const int k1 = k0 + TK;
+            load_tile_async(sK[buf ^ 1], base + (long)k1 * ld + C + h * HS, ld, TK, min(TK, T - k1));
+            load_tile_async(sV[buf ^ 1], base + (long)k1 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k1));
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
         __syncthreads();
-        load_tile(sK, base + (long)k0 * ld + C + h * HS, ld, TK, min(TK, T - k0));
-        load_tile(sV, base + (long)k0 * ld + 2 * C + h * HS, ld, TK, min(TK, T - k0));
-        __syncthreads();
+        const float *cK = sK[buf], *cV = sV[buf];
         float s[8][4] = {}, dp[8][4] = {};
 #pragma unroll
-        for (int kk = 0; kk < HS / 8; ++kk) {
-            float aq[4], ao[4];
-            frag_a(aq, sQ, warp * 16, kk * 8, g, t);
-            frag_a(ao, sO, warp * 16, kk * 8, g, t);
+        for (int kk = 0; kk < HS / 8; kk += 2) {
+            float aq0[4], aq1[4], ao0[4], ao1[4];
+            frag_a(aq0, sQ, warp * 16, kk * 8, lane);
+            frag_a(aq1, sQ, warp * 16, kk * 8 + 8, lane);
+            frag_a(ao0, sO, warp * 16, kk * 8, lane);
+            frag_a(ao1, sO, warp * 16, kk * 8 + 8, lane);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                float bk[2], bv[2];
-                frag_b_rows(bk, sK, j * 8, kk * 8, g, t);
-                frag_b_rows(bv, sV, j * 8, kk * 8, g, t);
-                mma_f32<SPLIT>(s[j], aq, bk);
-                mma_f32<SPLIT>(dp[j], ao, bv);
+                float bk[4], bv[4];
+                frag_b_rows2(bk, cK, j * 8, kk * 8, lane);
+                frag_b_rows2(bv, cV, j * 8, kk * 8, lane);
+                const float k0b[2] = {bk[0], bk[1]}, k1b[2] = {bk[2], bk[3]};
+                const float v0b[2] = {bv[0], bv[1]}, v1b[2] = {bv[2], bv[3]};
+                mma_f32<SPLIT>(s[j], aq0, k0b);
+                mma_f32<SPLIT>(s[j], aq1, k1b);
+                mma_f32<SPLIT>(dp[j], ao0, v0b);
+                mma_f32<SPLIT>(dp[j], ao1, v1b);
             }
         }
 #pragma unroll
@@ -379,7 +484,7 @@ attn_bwd_dq_kernel(const float *__restrict__ qkv, const float *__restrict__ dout
                 const int row = (e < 2) ? row0 : row1;
                 float p = 0.f;
                 if (key <= row && key < T && row < T)
-                    p = expf(s[j][e] * scale - ((e < 2) ? L0 : L1));
+                    p = ex2((s[j][e] * scale - ((e < 2) ? L0 : L1)) * LOG2E);
                 s[j][e] = p * (dp[j][e] - ((e < 2) ? D0 : D1));  // dS
             }
         }
@@ -389,10 +494,11 @@ attn_bwd_dq_kernel(const float *__restrict__ qkv, const float *__restrict__ dout
 #pragma unroll
             for (int dn = 0; dn < 8; ++dn) {
                 float bk[2];
-                frag_b_cols(bk, sK, j * 8, dn * 8, g, t);
+                frag_b_cols(bk, cK, j * 8, dn * 8, g, t);
                 mma_f32<SPLIT>(dq[dn], a, bk);
             }
         }
+        __syncthreads();
     }
     float *dqb = dqkv + (long)b * T * ld + h * HS;
 #pragma unroll
@@ -598,16 +704,16 @@ int attention_fwd(const float *qkv, float *out, float *lse, int B, int T, int C,
     const int hs = C / H;
     const float scale = 1.0f / sqrtf((float)hs);
     if (hs == HS && precision() != PREC_FP32) {
-        const int smem = 3 * TQ * LDS * sizeof(float);
-        dim3 grid((T + TQ - 1) / TQ, B * H);
+        const int smem = (FQ + 4 * TK) * LDS * sizeof(float);
+        dim3 grid((T + FQ - 1) / FQ, B * H);
         if (precision() == PREC_3XTF32) {
             static bool a = false;
             if (!a) { CG_TRY(set_smem(attn_fwd_mma_kernel<true>, smem)); a = true; }
-            attn_fwd_mma_kernel<true><<<grid, 128, smem, s>>>(qkv, out, lse, T, C, H, scale);
+            attn_fwd_mma_kernel<true><<<grid, 256, smem, s>>>(qkv, out, lse, T, C, H, scale);
         } else {
             static bool a = false;
             if (!a) { CG_TRY(set_smem(attn_fwd_mma_kernel<false>, smem)); a = true; }
-            attn_fwd_mma_kernel<false><<<grid, 128, smem, s>>>(qkv, out, lse, T, C, H, scale);
+            attn_fwd_mma_kernel<false><<<grid, 256, smem, s>>>(qkv, out, lse, T, C, H, scale);
         }
         LAUNCH_CHECK();
         return OK;
@@ -652,8 +758,8 @@ int attention_bwd(const float *qkv, const float *out, const float *dout, const f
     LAUNCH_CHECK();
     if (hs == HS && precision() != PREC_FP32) {
         const int nt = (T + 63) / 64;
-        const int smem_kv = (4 * TK * LDS + 2 * TQ) * sizeof(float);
-        const int smem_q = 4 * TQ * LDS * sizeof(float);
+        const int smem_kv = ((2 * TK + 4 * TQ) * LDS + 4 * TQ) * sizeof(float);
+        const int smem_q = (2 * TQ + 4 * TK) * LDS * sizeof(float);
         dim3 grid(nt, B * H);
         if (precision() == PREC_3XTF32) {
             static bool a = false;

@@ -585,9 +585,12 @@ template <bool A_MN, bool B_MN>
 int dispatch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, int K,
                 const GemmEpi &epi, cudaStream_t s, bool split) {
     if (split) return launch_tc<128, A_MN, B_MN, true>(A, lda, B, ldb, M, N, K, epi, s);
-    // wide tiles when there are enough of them to fill the machine
-    const long tiles256 = (long)((M + BM - 1) / BM) * ((N + 255) / 256);
-    if (N > 128 && tiles256 >= num_sms())
+    // 128 x 256 tiles halve the A traffic per FLOP; take them unless their
+    // last wave leaves the machine much emptier than 128 x 128 tiles would
+    const long sms = num_sms(), tm = (M + BM - 1) / BM;
+    const long t256 = tm * ((N + 255) / 256);
+    auto eff = [&](long t) { return (double)t / (double)(((t + sms - 1) / sms) * sms); };
+    if (N > 128 && t256 >= sms && eff(t256) >= 0.8)
         return launch_tc<256, A_MN, B_MN, false>(A, lda, B, ldb, M, N, K, epi, s);
     return launch_tc<128, A_MN, B_MN, false>(A, lda, B, ldb, M, N, K, epi, s);
 }
