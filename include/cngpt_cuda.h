@@ -78,6 +78,24 @@ int cngpt_cuda_attention_fwd(const float *qkv, float *out, float *lse,
 int cngpt_cuda_attention_bwd(const float *qkv, const float *out, const float *dout,
                              const float *lse, float *dqkv, int B, int T, int C, int H);
 
+/* ---- LayerNorm backward without device allocation ---------------------------
+ * No counterpart in the reference. Same result as layernorm_bwd (cngpt/ops.h)
+ * on device or managed pointers, but it allocates nothing: the dw/db partial
+ * sums go to a fixed 2 MiB array inside the library (every GPU that loads the
+ * library holds it until the process exits), for callers that cannot let a
+ * library call cudaMalloc - it synchronises the device, and it fails when the
+ * caller has already reserved the GPU's memory for its own pool.
+ *  - T * C up to about 33.5 million (ceil(T/128) * 2 * C <= 524288 floats);
+ *    larger shapes return CNGPT_ERR_ARG with a message, as do host pointers.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress); make that first call before any stream capture.
+ *  - All calls share the one array: calls that overlap on the GPU (different
+ *    streams, or several host threads) race on it and must be serialised.
+ *    Nothing in it needs clearing - each call writes every element it reads. */
+int cngpt_cuda_layernorm_bwd_noalloc(const float *dout, const float *x, const float *w,
+                                     const float *mean, const float *rstd,
+                                     float *dx, float *dw, float *db, int T, int C);
+
 /* ---- training ------------------------------------------------------------
  * One full step of the reference's train loop (src/cngpt.c:154-163):
  * zero_grad, forward, backward, [DP allreduce], AdamW with clipping.
