@@ -246,6 +246,39 @@ def gemm_replay(lib, torch, dev, prec: int, iters: int) -> dict:
             "tflops": flops / (ms * 1e-3) / 1e12, "flops_per_launch": flops / n, "ms_per_launch": ms / n}
 
 
+def fc_gemm_roofline(lib, torch, dev, reps: int = 20) -> dict:
+    """The dominant GEMM launch alone: the MLP fc projection of GPT-2 small
+    (8192 x 3072 x 768, bias + GELU epilogue writing both outputs), the shape
+    profiles/gemm_tc_fc_gelu_8192x3072x768.md captures. CUDA events on the
+    stream the kernel runs on (the legacy default stream)."""
+    from cngpt_b200 import abi
+    M, N, K = B_ * T_, 4 * C_, C_
+    A = torch.randn(M, K, device=dev) * 0.02
+    W = torch.randn(N, K, device=dev) * 0.02
+    bias = torch.zeros(N, device=dev)
+    D, D2 = torch.empty(M, N, device=dev), torch.empty(M, N, device=dev)
+    lib.cngpt_cuda_set_precision(abi.PREC_TF32)
+
+    def one():
+        st = lib.cngpt_cuda_gemm(A.data_ptr(), K, 0, W.data_ptr(), K, 0, M, N, K, abi.EPI_GELU, 1.0,
+                                 D.data_ptr(), N, bias.data_ptr(), D2.data_ptr(), N, None, 0, None, 0)
+        if st:
+            raise RuntimeError(lib.cngpt_cuda_last_message().decode())
+    for _ in range(3):
+        one()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 2.0 * M * N * K
+    return {"ms_per_launch": ms, "flops_per_launch": flops, "tflops": flops / (ms * 1e-3) / 1e12,
+            "algorithmic_bytes": 4.0 * (M * K + N * K + 2 * M * N)}
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -345,6 +378,7 @@ def run_ours(args) -> None:
     peak_src = ("of measured (bf16 cuBLAS burst / 2: the tf32 tensor rate is half the bf16 rate)"
                 if "bf16_tflops" in peaks else "of fallback (1.59 PF bf16 / 2)")
     replay = gemm_replay(lib, torch, dev, abi.PREC_TF32, 3)
+    fc = fc_gemm_roofline(lib, torch, dev)
     traffic = None
     prof = ROOT / "profiles" / "gemm_tc_traffic.json"
     if prof.exists():
@@ -359,10 +393,15 @@ def run_ours(args) -> None:
                 "h2d_bytes_per_step": 3 * B_ * T_ * 4, "d2h_bytes_per_step": 4,
                 "api": "cngpt_cuda_train_step with pinned host token buffers and the loss read back"},
         "gpu_launches": launches,
-        "roofline": {"bound": "tensor", "achieved": replay["tflops"], "peak": tf32_peak,
-                     "unit": "TFLOP/s", "frac": replay["tflops"] / tf32_peak, "traffic": traffic,
-                     "kernel": "gemm_tc_kernel (tcgen05 kind::tf32)", "peak_source": peak_src,
-                     "flops_per_launch": replay["flops_per_launch"], "ms_per_launch": replay["ms_per_launch"]},
+        "roofline": {"bound": "tensor", "achieved": fc["tflops"], "peak": tf32_peak,
+                     "unit": "TFLOP/s", "frac": fc["tflops"] / tf32_peak, "traffic": traffic,
+                     "kernel": "gemm_tc_kernel<256,K,K,tf32>: GPT-2 small fc GEMM 8192x3072x768, bias+GELU",
+                     "peak_source": peak_src, "flops_per_launch": fc["flops_per_launch"],
+                     "ms_per_launch": fc["ms_per_launch"], "algorithmic_bytes": fc["algorithmic_bytes"]},
+        "gemm_step_replay": {"tflops": replay["tflops"], "frac": replay["tflops"] / tf32_peak,
+                             "launches": replay["launches"], "ms_per_step": replay["ms_per_step"],
+                             "note": "all 147 GEMM shapes of one training step, same operand "
+                                     "layouts and epilogues, timed alone"},
         "step_tflops": fl["total"] / (ms * 1e-3) / 1e12,
         "step_frac_of_tf32_peak": fl["total"] / (ms * 1e-3) / 1e12 / tf32_peak,
         "loss_after_steps": loss,
@@ -391,7 +430,7 @@ class _Null:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")

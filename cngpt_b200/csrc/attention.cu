@@ -631,7 +631,7 @@ __global__ void attn_bwd_simt_kernel(const float *__restrict__ qkv, const float 
 __global__ void __launch_bounds__(256)
 attn_decode_kernel(const float *__restrict__ q, long ldq, const float *__restrict__ kc,
                    const float *__restrict__ vc, long Tmax, int len, float *__restrict__ out,
-                   int C, int H, int hs, float scale) {
+                   int C, int H, int hs, float scale, int vec4) {
     extern __shared__ float sm[];
     float *sq = sm, *sp = sm + hs, *red = sp + len;  // red: 64 floats
     const int bh = blockIdx.x, b = bh / H, h = bh % H;
@@ -644,9 +644,13 @@ attn_decode_kernel(const float *__restrict__ q, long ldq, const float *__restric
     for (int j = threadIdx.x; j < len; j += blockDim.x) {
         const float *kr = kb + (long)j * C;
         float d = 0.f;
-        for (int i = 0; i < hs; i += 4) {
-            const float4 kv = *(const float4 *)(kr + i);
-            d += sq[i] * kv.x + sq[i + 1] * kv.y + sq[i + 2] * kv.z + sq[i + 3] * kv.w;
+        if (vec4) {
+            for (int i = 0; i < hs; i += 4) {
+                const float4 kv = *(const float4 *)(kr + i);
+                d += sq[i] * kv.x + sq[i + 1] * kv.y + sq[i + 2] * kv.z + sq[i + 3] * kv.w;
+            }
+        } else {
+            for (int i = 0; i < hs; ++i) d += sq[i] * kr[i];
         }
         d *= scale;
         sp[j] = d;
@@ -698,12 +702,26 @@ int set_smem(K kern, int bytes) {
 
 #define LAUNCH_CHECK() do { ++g_launch_count; CG_CUDA(cudaGetLastError()); } while (0)
 
+namespace {
+// The tensor-core kernels move rows with 16-byte cp.async / ldmatrix and store
+// 8-byte pairs: every base must be 16-byte aligned and every row pitch (3C and
+// C floats) a multiple of 16 bytes. Activation-arena slots are not aligned
+// when B*T is odd (the mean/rstd slots before them hold B*T floats each), so
+// this is checked per call and such calls take the CUDA-core kernels.
+bool mma_ok(int C, std::initializer_list<const void *> ptrs) {
+    if (C % 4 != 0) return false;
+    for (const void *p : ptrs)
+        if (p && ((uintptr_t)p % 16) != 0) return false;
+    return true;
+}
+}  // namespace
+
 int attention_fwd(const float *qkv, float *out, float *lse, int B, int T, int C, int H,
                   cudaStream_t s) {
     if (B <= 0 || T <= 0) return OK;
     const int hs = C / H;
     const float scale = 1.0f / sqrtf((float)hs);
-    if (hs == HS && precision() != PREC_FP32) {
+    if (hs == HS && precision() != PREC_FP32 && mma_ok(C, {qkv, out})) {
         const int smem = (FQ + 4 * TK) * LDS * sizeof(float);
         dim3 grid((T + FQ - 1) / FQ, B * H);
         if (precision() == PREC_3XTF32) {
@@ -756,7 +774,7 @@ int attention_bwd(const float *qkv, const float *out, const float *dout, const f
     attn_bwd_dot_kernel<<<(int)std::min<long>((rows + 7) / 8, 148L * 64), 256, 0, s>>>(out, dout, D, B,
                                                                                       T, C, H, hs);
     LAUNCH_CHECK();
-    if (hs == HS && precision() != PREC_FP32) {
+    if (hs == HS && precision() != PREC_FP32 && mma_ok(C, {qkv, out, dout, dqkv})) {
         const int nt = (T + 63) / 64;
         const int smem_kv = ((2 * TK + 4 * TQ) * LDS + 4 * TQ) * sizeof(float);
         const int smem_q = (2 * TQ + 4 * TK) * LDS * sizeof(float);
@@ -800,7 +818,7 @@ int attention_bwd(const float *qkv, const float *out, const float *dout, const f
 int attention_decode(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
                      int len, float *out, int B, int C, int H, cudaStream_t s) {
     const int hs = C / H;
-    if (hs % 4 != 0 || hs > 256 || len <= 0) {
+    if (hs > 256 || len <= 0) {
         set_last_error(ERR_ARG, "attention_decode: unsupported hs=%d len=%d", hs, len);
         return ERR_ARG;
     }
@@ -812,8 +830,9 @@ int attention_decode(const float *q, long ldq, const float *kcache, const float 
     }
     static bool a = false;
     if (!a) { CG_TRY(set_smem(attn_decode_kernel, 200 * 1024 + 4096)); a = true; }
+    const int vec4 = (C % 4 == 0) && ((uintptr_t)kcache % 16) == 0;
     attn_decode_kernel<<<B * H, 256, smem, s>>>(q, ldq, kcache, vcache, Tmax, len, out, C, H, hs,
-                                                1.0f / sqrtf((float)hs));
+                                                1.0f / sqrtf((float)hs), vec4);
     LAUNCH_CHECK();
     return OK;
 }

@@ -23,8 +23,13 @@ CONFIGS = {
     "grad": dict(L=2, H=4, C=32, V=64, block=8, B=2, T=6, seed=1234),
     # head size 64 (tensor-core attention), tcgen05 GEMMs, T not a tile multiple
     "hs64": dict(L=2, H=2, C=128, V=96, block=128, B=2, T=100, seed=7),
+    # odd B*T: arena slots after the mean/rstd vectors lose 16-byte alignment,
+    # so the vectorised attention kernels must hand over to the CUDA-core ones
+    "odd": dict(L=2, H=2, C=128, V=96, block=64, B=1, T=7, seed=11),
     # GPT-2 small widths, one layer, full vocabulary
     "small1": dict(L=1, H=12, C=768, V=50257, block=1024, B=1, T=128, seed=None),
+    # the whole GPT-2 small stack (12 layers): error growth through depth
+    "small12": dict(L=12, H=12, C=768, V=50257, block=1024, B=1, T=64, seed=None),
 }
 
 TOLS = {abi.PREC_3XTF32: dict(loss=5e-6, logits=1e-5, grad=2e-4),
@@ -72,8 +77,12 @@ def test_forward_backward_parity(lib, cuda, prec, cfgname):
     abi.check(lib, lib.cngpt_cuda_check(), "device")
     oc = oracle.cfg(c["L"], c["H"], c["C"], c["V"], c["block"])
     p0 = ref.params()
-    le, ge = oracle.forward_backward(oc, p0, tok, tgt, B, T)
-    _, lg_e = oracle.forward(oc, p0, tok, None, B, T)
+    # the double-accumulated restatement is the exact reference point; its
+    # backward is too slow on the host for the 12-layer stack, whose gradient
+    # floor is then taken as zero (the plain bound applies)
+    le, lg_e = oracle.forward(oc, p0, tok, tgt, B, T)
+    ge = (oracle.forward_backward(oc, p0, tok, tgt, B, T)[1] if c["L"] * c["C"] * c["C"] * B * T < 2e9
+          else None)
     lg_r, lg_d = ref.logits(B, T), dev.logits(B, T)
     floor_logits = nwerr(lg_r, lg_e)
     rel = abs(ld_ - lr_) / abs(lr_)
@@ -86,7 +95,7 @@ def test_forward_backward_parity(lib, cuda, prec, cfgname):
     worst, worst_floor = 0.0, 0.0
     for name, off, n in param_slices(ref.cfg):
         e = nwerr(gd[off:off + n], gr[off:off + n])
-        fl = nwerr(gr[off:off + n], ge[off:off + n])
+        fl = nwerr(gr[off:off + n], ge[off:off + n]) if ge is not None else 0.0
         worst, worst_floor = max(worst, e), max(worst_floor, fl)
         assert e < max(tol["grad"], 2 * fl), f"grad {name}: normwise {e:.2e} (floor {fl:.2e})"
     print(f"[{cfgname}/{prec}] worst gradient tensor: dev-ref {worst:.2e}, ref-exact {worst_floor:.2e}")
