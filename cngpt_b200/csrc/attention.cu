@@ -631,9 +631,11 @@ __global__ void attn_bwd_simt_kernel(const float *__restrict__ qkv, const float 
 __global__ void __launch_bounds__(256)
 attn_decode_kernel(const float *__restrict__ q, long ldq, const float *__restrict__ kc,
                    const float *__restrict__ vc, long Tmax, int len, float *__restrict__ out,
-                   int C, int H, int hs, float scale, int vec4) {
+                   int C, int H, int hs, float scale, int vec4, const int *__restrict__ pos_dev) {
     extern __shared__ float sm[];
-    float *sq = sm, *sp = sm + hs, *red = sp + len;  // red: 64 floats
+    // with a device position the scores area is sized for the capacity Tmax
+    float *sq = sm, *sp = sm + hs, *red = sp + (pos_dev ? (int)Tmax : len);  // red: 64 floats
+    if (pos_dev) len = *pos_dev + 1;
     const int bh = blockIdx.x, b = bh / H, h = bh % H;
     const float *qr = q + (long)b * ldq + h * hs;
     for (int i = threadIdx.x; i < hs; i += blockDim.x) sq[i] = qr[i];
@@ -815,26 +817,38 @@ int attention_bwd(const float *qkv, const float *out, const float *dout, const f
     return OK;
 }
 
-int attention_decode(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
-                     int len, float *out, int B, int C, int H, cudaStream_t s) {
+int attention_decode_impl(const float *q, long ldq, const float *kcache, const float *vcache,
+                          long Tmax, int len, const int *pos_dev, float *out, int B, int C, int H,
+                          cudaStream_t s) {
     const int hs = C / H;
-    if (hs > 256 || len <= 0) {
-        set_last_error(ERR_ARG, "attention_decode: unsupported hs=%d len=%d", hs, len);
+    const int cap = pos_dev ? (int)Tmax : len;
+    if (hs > 256 || cap <= 0) {
+        set_last_error(ERR_ARG, "attention_decode: unsupported hs=%d len=%d", hs, cap);
         return ERR_ARG;
     }
     const int G = 256 / hs;
-    const size_t smem = (size_t)(hs + len + 64 + G * hs) * sizeof(float);
+    const size_t smem = (size_t)(hs + cap + 64 + G * hs) * sizeof(float);
     if (smem > 200 * 1024) {
-        set_last_error(ERR_ARG, "attention_decode: context %d too long", len);
+        set_last_error(ERR_ARG, "attention_decode: context %d too long", cap);
         return ERR_ARG;
     }
     static bool a = false;
     if (!a) { CG_TRY(set_smem(attn_decode_kernel, 200 * 1024 + 4096)); a = true; }
     const int vec4 = (C % 4 == 0) && ((uintptr_t)kcache % 16) == 0;
     attn_decode_kernel<<<B * H, 256, smem, s>>>(q, ldq, kcache, vcache, Tmax, len, out, C, H, hs,
-                                                1.0f / sqrtf((float)hs), vec4);
+                                                1.0f / sqrtf((float)hs), vec4, pos_dev);
     LAUNCH_CHECK();
     return OK;
+}
+
+int attention_decode(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
+                     int len, float *out, int B, int C, int H, cudaStream_t s) {
+    return attention_decode_impl(q, ldq, kcache, vcache, Tmax, len, nullptr, out, B, C, H, s);
+}
+
+int attention_decode_at(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
+                        const int *pos_dev, float *out, int B, int C, int H, cudaStream_t s) {
+    return attention_decode_impl(q, ldq, kcache, vcache, Tmax, 0, pos_dev, out, B, C, H, s);
 }
 
 }  // namespace cg

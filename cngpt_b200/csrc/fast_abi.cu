@@ -30,9 +30,17 @@ void fast_forget(const FastCtx *f);
 
 namespace {
 
+void drop_graph(FastDev *d) {
+    if (d->step_graph) cudaGraphExecDestroy(d->step_graph);
+    d->step_graph = nullptr;
+    d->graph_params = nullptr;
+}
+
 int fast_resize(FastCtx *f, FastDev *d, const GPT *m, int B, int T, bool managed) {
     if (f->x && f->B == B && f->T == T) return OK;
     cudaStreamSynchronize(g_stream);
+    if (d->cap_stream) cudaStreamSynchronize(d->cap_stream);
+    drop_graph(d);  // the captured step holds the scratch addresses
     float **bufs[] = {&f->x, &f->ln, &f->qkv, &f->aout, &f->hid, &f->mean, &f->rstd, &f->logits,
                       &d->xl, &d->al};
     for (auto b : bufs) {
@@ -138,24 +146,62 @@ int fast_forward(const GPT *m, FastCtx *f, FastDev *d, const int *tok, int B, in
     return OK;
 }
 
-// One decode step: tokens tok[B] at position pos; K/V appended at pos.
-int decode_step(const GPT *m, FastCtx *f, FastDev *d, const int *tok, int B, int pos, cudaStream_t s) {
+// One decode step for B sequences: the incoming tokens d->next[B] sit at
+// position ctr[0]; K/V are appended there, the greedy token of the step is
+// written to d->next and to d->gen[ctr[1]], then both counters advance. All
+// positions are read on the device, so one captured graph replays every step.
+int decode_step(const GPT *m, FastCtx *f, FastDev *d, int B, cudaStream_t s) {
     const int C = m->cfg.n_embd, V = m->cfg.vocab_size, L = m->cfg.n_layer, H = m->cfg.n_head;
     const GPTWeights *w = &m->params;
     float *x = d->xl;
-    CG_TRY(embed_fwd(tok, w->wte, w->wpe, x, B, 1, C, pos, s));
+    CG_TRY(embed_fwd_at(d->next, w->wte, w->wpe, x, B, C, d->ctr, s));
     const size_t per = (size_t)d->kv_B * d->kv_T * C;
     for (int l = 0; l < L; l++) {
         CG_TRY(layernorm_fwd(x, C, w->ln1_w[l], w->ln1_b[l], f->ln, C, f->mean, f->rstd, B, C, s));
         CG_TRY(gemm(f->ln, C, false, w->c_attn_w[l], C, false, B, 3 * C, C,
                     epi_store(f->qkv, 3 * C, w->c_attn_b[l]), s));
-        CG_TRY(kv_append(f->qkv, d->kc + l * per, d->vc + l * per, B, 1, d->kv_T, pos, C, s));
-        CG_TRY(attention_decode(f->qkv, 3L * C, d->kc + l * per, d->vc + l * per, d->kv_T, pos + 1,
-                                d->al, B, C, H, s));
+        CG_TRY(kv_append_at(f->qkv, d->kc + l * per, d->vc + l * per, B, d->kv_T, C, d->ctr, s));
+        CG_TRY(attention_decode_at(f->qkv, 3L * C, d->kc + l * per, d->vc + l * per, d->kv_T, d->ctr,
+                                   d->al, B, C, H, s));
         CG_TRY(block_tail(m, l, f, x, d->al, B, s));
     }
     CG_TRY(layernorm_fwd(x, C, w->ln_f_w, w->ln_f_b, f->ln, C, f->mean, f->rstd, B, C, s));
     CG_TRY(gemm(f->ln, C, false, w->wte, C, false, B, V, C, epi_store(f->logits, V, nullptr), s));
+    CG_TRY(argmax_log(f->logits, V, B, V, d->next, d->gen, d->ctr + 1, s));
+    return decode_advance(d->ctr, s);
+}
+
+// Capture one decode step on the FastDev's own stream (reused while the model,
+// batch, cache capacity, precision and output buffer are unchanged).
+int capture_step(const GPT *m, FastCtx *f, FastDev *d, int B) {
+    if (d->step_graph && d->graph_params == m->param_buf && d->graph_B == B && d->graph_T == d->kv_T &&
+        d->graph_prec == precision() && d->graph_logits == f->logits)
+        return OK;
+    drop_graph(d);
+    cudaGraph_t g = nullptr;
+    CG_CUDA(cudaStreamBeginCapture(d->cap_stream, cudaStreamCaptureModeThreadLocal));
+    const int st = decode_step(m, f, d, B, d->cap_stream);
+    const cudaError_t e = cudaStreamEndCapture(d->cap_stream, &g);
+    if (st != OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (e != cudaSuccess) {
+        set_last_error(ERR_CUDA, "decode graph capture: %s", cudaGetErrorString(e));
+        return ERR_CUDA;
+    }
+    const cudaError_t ei = cudaGraphInstantiate(&d->step_graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) {
+        d->step_graph = nullptr;
+        set_last_error(ERR_CUDA, "decode graph instantiate: %s", cudaGetErrorString(ei));
+        return ERR_CUDA;
+    }
+    d->graph_params = m->param_buf;
+    d->graph_B = B;
+    d->graph_T = d->kv_T;
+    d->graph_prec = precision();
+    d->graph_logits = f->logits;
     return OK;
 }
 
@@ -182,6 +228,11 @@ extern "C" void fast_free(FastCtx *f) {
         dev_free(d->vc);
         dev_free(d->next);
         dev_free(d->gen);
+        dev_free(d->ctr);
+        drop_graph(d);
+        if (d->ev_a) cudaEventDestroy(d->ev_a);
+        if (d->ev_b) cudaEventDestroy(d->ev_b);
+        if (d->cap_stream) cudaStreamDestroy(d->cap_stream);
         fast_forget(f);
     }
     memset(f, 0, sizeof(*f));
@@ -222,8 +273,15 @@ extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B,
     CG_TRY(fast_resize(f, d, m, B, T, c->managed));
     const int Tmax = T + n_new;
     const size_t C = m->cfg.n_embd, L = m->cfg.n_layer, V = m->cfg.vocab_size;
+    if (!d->cap_stream) {
+        CG_CUDA(cudaStreamCreateWithFlags(&d->cap_stream, cudaStreamNonBlocking));
+        CG_CUDA(cudaEventCreateWithFlags(&d->ev_a, cudaEventDisableTiming));
+        CG_CUDA(cudaEventCreateWithFlags(&d->ev_b, cudaEventDisableTiming));
+        CG_TRY(dev_alloc((void **)&d->ctr, 2 * sizeof(int), false));
+    }
     if (d->kv_B != B || d->kv_T < Tmax) {
         CG_CUDA(cudaStreamSynchronize(s));
+        drop_graph(d);
         dev_free(d->kc);
         dev_free(d->vc);
         dev_free(d->next);
@@ -236,6 +294,8 @@ extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B,
         d->kv_T = Tmax;
     }
     if ((size_t)B * n_new > d->gen_cap) {
+        CG_CUDA(cudaStreamSynchronize(s));
+        drop_graph(d);
         dev_free(d->gen);
         d->gen = nullptr;
         CG_TRY(dev_alloc((void **)&d->gen, (size_t)B * n_new * 4, false));
@@ -243,12 +303,24 @@ extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B,
     }
     const int *tok = nullptr;
     CG_TRY(stage_tokens(prompt, (size_t)B * T, &d->tok, &d->tok_cap, &tok, s));
+    // counters {T-1, 0}: the prefill's greedy token is logged at step 0, then
+    // decode_advance moves to {T, 1} - position T for the first decode input
+    const int ctr0[2] = {T - 1, 0};
+    CG_CUDA(cudaMemcpyAsync(d->ctr, ctr0, sizeof(ctr0), cudaMemcpyHostToDevice, s));
     CG_TRY(fast_forward(m, f, d, tok, B, T, true, s));
-    // gen is laid out [step][B]; transposed to [B][step] on the host
-    CG_TRY(argmax_rows(f->logits, V, B, (int)V, d->gen, nullptr, s));
-    for (int i = 1; i < n_new; ++i) {
-        CG_TRY(decode_step(m, f, d, d->gen + (size_t)(i - 1) * B, B, T + i - 1, s));
-        CG_TRY(argmax_rows(f->logits, V, B, (int)V, d->gen + (size_t)i * B, nullptr, s));
+    CG_TRY(argmax_log(f->logits, V, B, (int)V, d->next, d->gen, d->ctr + 1, s));
+    CG_TRY(decode_advance(d->ctr, s));
+    if (n_new > 1) {
+        // the decode steps run on the FastDev's stream, ordered after the prefill
+        CG_CUDA(cudaEventRecord(d->ev_a, s));
+        CG_CUDA(cudaStreamWaitEvent(d->cap_stream, d->ev_a, 0));
+        CG_TRY(decode_step(m, f, d, B, d->cap_stream));  // eager first step (warms the kernels)
+        if (n_new > 2) {
+            CG_TRY(capture_step(m, f, d, B));
+            for (int i = 2; i < n_new; ++i) CG_CUDA(cudaGraphLaunch(d->step_graph, d->cap_stream));
+        }
+        CG_CUDA(cudaEventRecord(d->ev_b, d->cap_stream));
+        CG_CUDA(cudaStreamWaitEvent(s, d->ev_b, 0));
     }
     std::vector<int> h((size_t)B * n_new);
     CG_CUDA(cudaMemcpyAsync(h.data(), d->gen, h.size() * 4, cudaMemcpyDeviceToHost, s));

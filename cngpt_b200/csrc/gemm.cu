@@ -488,6 +488,65 @@ gemm_simt_kernel(const float *__restrict__ A, long lda, int a_mn, const float *_
     }
 }
 
+// ------------------------------------------------- skinny GEMM (GEMV) path
+// out[m, n] = sum_k X[m, k] W[n, k] for M <= 8 rows (batch-1..8 decode and
+// the fast path's last-position rows). HBM-bound on W: every warp streams
+// two rows of W with 16-byte loads (both operands K-major, K % 4 == 0,
+// 16-byte aligned), each X load feeds both rows, fp32 FMA accumulation, a
+// warp-shuffle reduction and the fused epilogue of the tensor-core kernel.
+constexpr int GEMV_ROWS = 2;  // W rows per warp
+
+template <int MT>
+__global__ void __launch_bounds__(256)
+gemv_kernel(const float *__restrict__ X, long ldx, const float *__restrict__ W, long ldw, int M, int N,
+            int K, GemmEpi epi) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = (blockIdx.x * 8 + warp) * GEMV_ROWS;
+    if (n0 >= N) return;
+    const int K4 = K / 4;
+    float acc[GEMV_ROWS][MT];
+#pragma unroll
+    for (int r = 0; r < GEMV_ROWS; ++r)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+    const float4 *w4[GEMV_ROWS];
+#pragma unroll
+    for (int r = 0; r < GEMV_ROWS; ++r) w4[r] = (const float4 *)(W + (long)min(n0 + r, N - 1) * ldw);
+#pragma unroll 2
+    for (int k = lane; k < K4; k += 32) {
+        float4 wv[GEMV_ROWS];
+#pragma unroll
+        for (int r = 0; r < GEMV_ROWS; ++r) wv[r] = __ldcs(w4[r] + k);  // streamed once: do not keep in L1
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m < M) {
+                const float4 xv = __ldg((const float4 *)(X + (long)m * ldx) + k);
+#pragma unroll
+                for (int r = 0; r < GEMV_ROWS; ++r)
+                    acc[r][m] += wv[r].x * xv.x + wv[r].y * xv.y + wv[r].z * xv.z + wv[r].w * xv.w;
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < GEMV_ROWS; ++r)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
+    if (lane < GEMV_ROWS * MT) {
+        const int r = lane / MT, m = lane % MT, n = n0 + r;
+        float v = 0.f;
+#pragma unroll
+        for (int rr = 0; rr < GEMV_ROWS; ++rr)
+#pragma unroll
+            for (int mm = 0; mm < MT; ++mm)
+                if (rr == r && mm == m) v = acc[rr][mm];
+        if (m < M && n < N) {
+            long ld = 0;
+            const float *ax = epi_aux(epi, ld);
+            epi_apply(epi, m, n, v, epi.bias ? epi.bias[n] : 0.0f, ax ? ax[(long)m * ld + n] : 0.0f);
+        }
+    }
+}
+
 // ------------------------------------------------------- tensor maps
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_mu;
@@ -616,6 +675,16 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
                   (!epi.R || epi.ldr % 4 == 0) && (!epi.G || epi.ldg % 4 == 0);
     }
     const int prec = precision();
+    if (M <= 8 && !a_mn && !b_mn && K % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 &&
+        ((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0 && (long)N * K >= (1L << 16)) {
+        const int blocks = (N + 8 * GEMV_ROWS - 1) / (8 * GEMV_ROWS);
+        if (M <= 1) gemv_kernel<1><<<blocks, 256, 0, s>>>(A, lda, B, ldb, M, N, K, epi);
+        else if (M <= 4) gemv_kernel<4><<<blocks, 256, 0, s>>>(A, lda, B, ldb, M, N, K, epi);
+        else gemv_kernel<8><<<blocks, 256, 0, s>>>(A, lda, B, ldb, M, N, K, epi);
+        ++g_launch_count;
+        CG_CUDA(cudaGetLastError());
+        return OK;
+    }
     const bool big = (long)M * N * (long)std::max(K, 1) >= (1L << 18) && K > 0;
     const bool tc = prec != PREC_FP32 && big && tma_ok(A, lda) && tma_ok(B, ldb) &&
                     (a_mn ? lda >= M : lda >= K) && (b_mn ? ldb >= N : ldb >= K);

@@ -270,7 +270,9 @@ __global__ void ce_grad_kernel(const float *__restrict__ probs, long ldp, const 
 
 // kc[b, pos0 + t, :] = qkv[b*T + t, C:2C], vc likewise from [2C:3C]
 __global__ void kv_append_kernel(const float *__restrict__ qkv, float *__restrict__ kc,
-                                 float *__restrict__ vc, int B, int T, long Tmax, int pos0, int C) {
+                                 float *__restrict__ vc, int B, int T, long Tmax, int pos0, int C,
+                                 const int *__restrict__ pos_dev) {
+    if (pos_dev) pos0 += *pos_dev;
     const long n = (long)B * T * C;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
         const long r = i / C;
@@ -350,7 +352,8 @@ __global__ void norm_final_kernel(const double *__restrict__ part, int nparts, f
 // emb[i] = wte[tok[i]] + wpe[i % T] (src/model.c:460-470)
 __global__ void embed_fwd_kernel(const int *__restrict__ tok, const float *__restrict__ wte,
                                  const float *__restrict__ wpe, float *__restrict__ out, int BT,
-                                 int T, int C, int pos0) {
+                                 int T, int C, int pos0, const int *__restrict__ pos_dev) {
+    if (pos_dev) pos0 += *pos_dev;
     const long n = (long)BT * C;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
         const long r = i / C;
@@ -490,7 +493,8 @@ __global__ void colsum_final_kernel(const float *__restrict__ part, int chunks, 
 // Greedy token per row: largest logit, lowest index on ties (the first index
 // whose CDF exceeds r in src/model.c:982-985 with top_k = 1).
 __global__ void argmax_kernel(const float *__restrict__ x, long ldx, int V, int *__restrict__ out,
-                              float *__restrict__ outval) {
+                              float *__restrict__ outval, int *__restrict__ log,
+                              const int *__restrict__ step_dev) {
     __shared__ float sv[32];
     __shared__ int si[32];
     const float *row = x + (long)blockIdx.x * ldx;
@@ -514,6 +518,7 @@ __global__ void argmax_kernel(const float *__restrict__ x, long ldx, int V, int 
             if (sv[k] > best || (sv[k] == best && si[k] < bi)) { best = sv[k]; bi = si[k]; }
         out[blockIdx.x] = bi;
         if (outval) outval[blockIdx.x] = best;
+        if (log) log[(long)(*step_dev) * gridDim.x + blockIdx.x] = bi;
     }
 }
 
@@ -651,7 +656,8 @@ int grad_norm(const float *g, long n, double *scratch, float *norm, float *clip_
 int embed_fwd(const int *tok, const float *wte, const float *wpe, float *out, int BT, int T, int C,
               int pos0, cudaStream_t s) {
     if (BT <= 0) return OK;
-    embed_fwd_kernel<<<grid_for((long)BT * C, 256), 256, 0, s>>>(tok, wte, wpe, out, BT, T, C, pos0);
+    embed_fwd_kernel<<<grid_for((long)BT * C, 256), 256, 0, s>>>(tok, wte, wpe, out, BT, T, C, pos0,
+                                                                 nullptr);
     LAUNCH_CHECK();
     return OK;
 }
@@ -735,7 +741,8 @@ int ce_grad(const float *probs, long ldp, const int *targets, float sc, float *d
 int kv_append(const float *qkv, float *kc, float *vc, int B, int T, long Tmax, int pos0, int C,
               cudaStream_t s) {
     if (B * T <= 0) return OK;
-    kv_append_kernel<<<grid_for((long)B * T * C, 256), 256, 0, s>>>(qkv, kc, vc, B, T, Tmax, pos0, C);
+    kv_append_kernel<<<grid_for((long)B * T * C, 256), 256, 0, s>>>(qkv, kc, vc, B, T, Tmax, pos0, C,
+                                                                    nullptr);
     LAUNCH_CHECK();
     return OK;
 }
@@ -747,9 +754,46 @@ int gather_last(const float *src, float *dst, int B, int T, int C, cudaStream_t 
     return OK;
 }
 
+// Decode-step variants: positions and the step index come from device
+// counters ctr[0] (position of the incoming token) and ctr[1] (step), so one
+// captured CUDA graph serves every step.
+__global__ void decode_advance_kernel(int *ctr) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        ctr[0] += 1;
+        ctr[1] += 1;
+    }
+}
+
+int embed_fwd_at(const int *tok, const float *wte, const float *wpe, float *out, int B, int C,
+                 const int *pos_dev, cudaStream_t s) {
+    embed_fwd_kernel<<<grid_for((long)B * C, 256), 256, 0, s>>>(tok, wte, wpe, out, B, 1, C, 0, pos_dev);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int kv_append_at(const float *qkv, float *kc, float *vc, int B, long Tmax, int C, const int *pos_dev,
+                 cudaStream_t s) {
+    kv_append_kernel<<<grid_for((long)B * C, 256), 256, 0, s>>>(qkv, kc, vc, B, 1, Tmax, 0, C, pos_dev);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int argmax_log(const float *x, long ldx, int rows, int V, int *cur, int *log, const int *step_dev,
+               cudaStream_t s) {
+    argmax_kernel<<<rows, 512, 0, s>>>(x, ldx, V, cur, nullptr, log, step_dev);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int decode_advance(int *ctr, cudaStream_t s) {
+    decode_advance_kernel<<<1, 32, 0, s>>>(ctr);
+    LAUNCH_CHECK();
+    return OK;
+}
+
 int argmax_rows(const float *x, long ldx, int rows, int V, int *out, float *outval, cudaStream_t s) {
     if (rows <= 0) return OK;
-    argmax_kernel<<<rows, 512, 0, s>>>(x, ldx, V, out, outval);
+    argmax_kernel<<<rows, 512, 0, s>>>(x, ldx, V, out, outval, nullptr, nullptr);
     LAUNCH_CHECK();
     return OK;
 }

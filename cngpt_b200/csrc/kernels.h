@@ -44,6 +44,15 @@ int kv_append(const float *qkv, float *kc, float *vc, int B, int T, long Tmax, i
               cudaStream_t s);
 int gather_last(const float *src, float *dst, int B, int T, int C, cudaStream_t s);
 int argmax_rows(const float *x, long ldx, int rows, int V, int *out, float *outval, cudaStream_t s);
+// decode-step variants reading positions from device counters (ctr[0] =
+// position of the incoming token, ctr[1] = step index)
+int embed_fwd_at(const int *tok, const float *wte, const float *wpe, float *out, int B, int C,
+                 const int *pos_dev, cudaStream_t s);
+int kv_append_at(const float *qkv, float *kc, float *vc, int B, long Tmax, int C, const int *pos_dev,
+                 cudaStream_t s);
+int argmax_log(const float *x, long ldx, int rows, int V, int *cur, int *log, const int *step_dev,
+               cudaStream_t s);
+int decode_advance(int *ctr, cudaStream_t s);
 
 // ---------------------------------------------------------------- attention
 // Causal self-attention over packed qkv rows [B, T, 3C] (head h: columns
@@ -64,5 +73,9 @@ int attention_fwd_rows(const float *qkv, float *out, int B, int T, int C, int H,
 // kcache/vcache [B, Tmax, C], attends positions [0, len). out [B, C].
 int attention_decode(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
                      int len, float *out, int B, int C, int H, cudaStream_t s);
+// same, with the attended length (position + 1) read from a device counter;
+// shared memory is sized for the cache capacity Tmax
+int attention_decode_at(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
+                        const int *pos_dev, float *out, int B, int C, int H, cudaStream_t s);
 
 }  // namespace cg

@@ -48,9 +48,17 @@ struct FastDev {
     // KV cache for greedy decode: [L][B][Tmax][C] each
     float *kc = nullptr, *vc = nullptr;
     int kv_B = 0, kv_T = 0;
-    int *next = nullptr;   // [B] argmax tokens
-    int *gen = nullptr;    // [B * n_new]
+    int *next = nullptr;   // [B] argmax tokens (the next step's input)
+    int *gen = nullptr;    // [n_new][B] generated tokens
     size_t gen_cap = 0;
+    int *ctr = nullptr;    // [0] position of the incoming token, [1] step index
+    // one decode step captured as a CUDA graph, reused while the key matches
+    cudaStream_t cap_stream = nullptr;
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+    cudaGraphExec_t step_graph = nullptr;
+    const void *graph_params = nullptr;
+    int graph_B = 0, graph_T = 0, graph_prec = -1;
+    const float *graph_logits = nullptr;
 };
 
 ModelCtx *model_ctx(const GPT *m);  // nullptr (and ERR_STATE recorded) if unknown
@@ -60,5 +68,15 @@ void dev_free(void *p);
 // copy token ids to the device unless they already are device-accessible
 int stage_tokens(const int *src, size_t n, int **buf, size_t *cap, const int **out, cudaStream_t s);
 int dp_allreduce(ModelCtx *c, float *buf, size_t n, cudaStream_t s);
+
+// NCCL, opened with dlopen on first use (dist.cu)
+int nccl_open();
+int nccl_comm_init(void **comm, const unsigned char id[128], int world, int rank);
+void nccl_comm_destroy(void *comm);
+int nccl_allreduce_sum(float *buf, size_t n, void *comm, cudaStream_t s);
+int nccl_allgather_words(const void *src, void *dst, size_t words, void *comm, cudaStream_t s);
+
+// tensor-parallel state of a model, released by gpt_free (tp_abi.cu)
+void tp_release(const GPT *m);
 
 }  // namespace cg

@@ -68,6 +68,8 @@ def prec(request, lib):
 # (M, N, K) - GPT-2 small call sites with M reduced, LM-head ragged N, odd K
 SHAPES = [(256, 2304, 768), (256, 768, 3072), (384, 50257, 64), (300, 200, 100), (128, 128, 32),
           (1000, 520, 72), (64, 3072, 768)]
+# decode-shaped rows (M <= 8 takes the GEMV kernel when A and B are K-major)
+SKINNY = [(1, 2304, 768), (5, 768, 3072), (8, 50257, 768), (3, 3072, 768)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -95,6 +97,26 @@ def test_gemm_epilogues(lib, cuda, prec, mode):
     elif mode == abi.EPI_RESID:
         assert nwerr(r["D"], ref) < TOL[prec]
         assert nwerr(r["D2"], r["R"] + ref) < TOL[prec]
+    elif mode == abi.EPI_GELU_BWD:
+        x = r["G"]
+        th = np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3))
+        gp = 0.5 * (1 + th) + 0.5 * x * (1 - th * th) * 0.7978845608028654 * (1 + 3 * 0.044715 * x * x)
+        assert nwerr(r["D"], ref * gp) < max(TOL[prec], 1e-5)
+    else:
+        assert nwerr(r["D"], ref) < TOL[prec]
+
+
+@pytest.mark.parametrize("M,N,K", SKINNY)
+@pytest.mark.parametrize("mode", [abi.EPI_STORE, abi.EPI_ACCUM, abi.EPI_GELU, abi.EPI_RESID,
+                                  abi.EPI_GELU_BWD])
+def test_gemm_skinny_rows(lib, cuda, prec, M, N, K, mode):
+    r = run_gemm(lib, cuda, M, N, K, False, False, mode=mode, bias=mode != abi.EPI_GELU_BWD, seed=M)
+    ref = r["ref"]
+    if mode == abi.EPI_GELU:
+        g = 0.5 * ref * (1 + np.tanh(0.7978845608028654 * (ref + 0.044715 * ref ** 3)))
+        assert nwerr(r["D"], ref) < TOL[prec] and nwerr(r["D2"], g) < max(TOL[prec], 1e-5)
+    elif mode == abi.EPI_RESID:
+        assert nwerr(r["D"], ref) < TOL[prec] and nwerr(r["D2"], r["R"] + ref) < TOL[prec]
     elif mode == abi.EPI_GELU_BWD:
         x = r["G"]
         th = np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3))
