@@ -279,6 +279,108 @@ def fc_gemm_roofline(lib, torch, dev, reps: int = 20) -> dict:
             "algorithmic_bytes": 4.0 * (M * K + N * K + 2 * M * N)}
 
 
+def decode_bytes(n_params: int, L: int, C: int, B: int, ctx0: int, steps: int) -> float:
+    """HBM bytes one greedy decode step must read, averaged over the window:
+    every weight once (fp32) plus the K and V cache of every layer up to the
+    current position."""
+    ctx = ctx0 + steps / 2.0
+    return 4.0 * n_params + 2.0 * 4.0 * L * C * B * ctx
+
+
+def inference_bench(lib, torch, dev, world: int, rank: int, hbm_peak: float, barrier, max_over_ranks) -> dict:
+    """BASELINE configs[2] (GPT-2 small: prefill 128 + 256 greedy steps at
+    B = 1 and 32, one GPU) and configs[4] (GPT-2 XL: prefill 8 x 1024, then
+    128 greedy steps at B = 1 and 8, tensor parallel over all ranks).
+
+    Times are wall-clock around the blocking API calls (prompt upload, the
+    device work and the token read-back included), max over ranks; decode
+    rate = (t(n_new) - t(1)) / (n_new - 1) per step."""
+    from cngpt_b200 import abi
+    out = {}
+
+    def timed(fn, reps=2):
+        fn()  # warm-up (graph capture, workspace allocation)
+        best = float("inf")
+        for _ in range(reps):
+            barrier()
+            t0 = time.perf_counter()
+            fn()
+            best = min(best, time.perf_counter() - t0)
+        return max_over_ranks(best)
+
+    if world == 1:
+        m = abi.GPT()
+        lib.gpt_init(C.byref(m), abi.GPTConfig(L_, H_, C_, V_, BLOCK, 0.0))
+        C.CDLL(None).srand(1)
+        lib.gpt_init_weights(C.byref(m))
+        lib.cngpt_cuda_set_precision(abi.PREC_TF32)
+        small = {}
+        for B in (1, 32):
+            T, n = 128, 256
+            prompt = lcg_tokens(B * T, V_, 7)
+            toks = np.zeros(B * n, np.int32)
+            fc = abi.FastCtx()
+            lib.fast_init(C.byref(fc))
+
+            def gen(k):
+                return lambda: abi.check(lib, lib.cngpt_cuda_generate(
+                    C.byref(m), C.byref(fc), prompt.ctypes.data, B, T, k, toks.ctypes.data), "generate")
+            t1, tn = timed(gen(1)), timed(gen(n))
+            per = (tn - t1) / (n - 1)
+            gbs = decode_bytes(m.n_params, L_, C_, B, T, n) / per / 1e9
+            small[f"B{B}"] = {"decode_tokens_per_s": B / per, "ms_per_step": per * 1e3,
+                              "prefill_tokens_per_s": B * T / t1, "hbm_gbs": gbs,
+                              "hbm_frac": gbs / hbm_peak}
+            lib.fast_free(C.byref(fc))
+        lib.gpt_free(C.byref(m))
+        out["gpt2_small"] = {"config": "BASELINE configs[2]: prefill 128 + 256 greedy steps, tf32", **small}
+    # GPT-2 XL, tensor parallel over every rank
+    L, H, Cx = 48, 25, 1600
+    m = abi.GPT()
+    lib.gpt_init(C.byref(m), abi.GPTConfig(L, H, Cx, V_, BLOCK, 0.0))
+    g = torch.Generator(device=dev).manual_seed(1234)  # same weights on every rank
+    w = torch.randn(m.n_params, generator=g, device=dev) * 0.02
+    abi.check(lib, lib.cngpt_cuda_copy(C.cast(m.param_buf, C.c_void_p), C.c_void_p(w.data_ptr()), m.n_params * 4), "copy")
+    del w
+    uid = (C.c_ubyte * 128)()
+    if world > 1:
+        import torch.distributed as dist
+        if rank == 0:
+            abi.check(lib, lib.cngpt_cuda_dp_unique_id(uid), "tp id")
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0)
+        uid = (C.c_ubyte * 128).from_buffer_copy(obj[0])
+    abi.check(lib, lib.cngpt_cuda_tp_init(C.byref(m), uid, world, rank), "tp init")
+    lib.cngpt_cuda_set_precision(abi.PREC_TF32)
+    xl = {"config": "BASELINE configs[4]: prefill 8 x 1024; decode from a 896-token prompt for 128 "
+                    "greedy steps (the cache ends at block_size 1024), tf32", "tp": world}
+    Bp, Tp = 8, 1024
+    ptok = lcg_tokens(Bp * Tp, V_, 11)
+    tpf = timed(lambda: abi.check(lib, lib.cngpt_cuda_tp_forward_last(C.byref(m), ptok.ctypes.data, Bp, Tp, None),
+                                  "tp forward"))
+    flops = 2.0 * m.n_params * Bp * Tp
+    xl["prefill_tokens_per_s"] = Bp * Tp / tpf
+    xl["prefill_tflops"] = flops / tpf / 1e12
+    for B in (1, 8):
+        T, n = 896, 128
+        prompt = lcg_tokens(B * T, V_, 13)
+        toks = np.zeros(B * n, np.int32)
+
+        def gen(k):
+            return lambda: abi.check(lib, lib.cngpt_cuda_tp_generate(C.byref(m), prompt.ctypes.data, B, T, k,
+                                                                     toks.ctypes.data), "tp generate")
+        t1, tn = timed(gen(1), 1), timed(gen(n), 1)
+        per = (tn - t1) / (n - 1)
+        gbs = decode_bytes(m.n_params, L, Cx, B, T, n) / world / per / 1e9
+        xl[f"decode_B{B}"] = {"tokens_per_s": B / per, "ms_per_step": per * 1e3,
+                              "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / hbm_peak}
+    lib.cngpt_cuda_tp_free(C.byref(m))
+    lib.gpt_free(C.byref(m))
+    out["gpt2_xl"] = xl
+    return out
+
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -408,6 +510,9 @@ def run_ours(args) -> None:
         "modes": {"3xtf32": {"value": tokens / (ms_3x * 1e-3), "ms_per_step": ms_3x, "loss": loss_3x}},
         "clocks": clocks.summary(),
     }
+    if not args.no_inference:
+        line["inference"] = inference_bench(lib, torch, dev, world, rank, peaks.get("hbm_gbs", 6650.0),
+                                            barrier, max_over_ranks)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_reference_step_sample(1, 1, os.cpu_count() or 1)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -434,6 +539,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-inference", action="store_true", help="skip the decode / prefill figures")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -133,6 +133,11 @@ EXT_SIGNATURES = {
     "cngpt_cuda_dp_init": (I, [C.POINTER(GPT), VP, I, I]),
     "cngpt_cuda_dp_allreduce_grads": (I, [C.POINTER(GPT)]),
     "cngpt_cuda_dp_free": (I, [C.POINTER(GPT)]),
+    "cngpt_cuda_tp_plan": (I, [I, I, I, I, I, VP]),
+    "cngpt_cuda_tp_init": (I, [C.POINTER(GPT), VP, I, I]),
+    "cngpt_cuda_tp_forward_last": (I, [C.POINTER(GPT), VP, I, I, VP]),
+    "cngpt_cuda_tp_generate": (I, [C.POINTER(GPT), VP, I, I, I, VP]),
+    "cngpt_cuda_tp_free": (I, [C.POINTER(GPT)]),
 }
 
 

@@ -694,6 +694,107 @@ attn_decode_kernel(const float *__restrict__ q, long ldq, const float *__restric
     }
 }
 
+// Split-context decode for head size 64 (flash-decoding): block (b*H + h,
+// split) scores keys [64*split, 64*split + 64) with a half-warp per key
+// (float4 per lane, 4-step shuffle reduction) and forms the chunk's softmax
+// partials (max m, sum l, unnormalised P V). The last block of a head to
+// finish (integer ticket; the partials are made visible with a fence before
+// the ticket is taken) merges every chunk of the head in chunk order, so the
+// result does not depend on which block came last, and resets the ticket.
+// Launched with programmatic dependent launch: nothing is read before
+// griddepcontrol.wait.
+constexpr int DEC_KEYS = 64, DEC_PART = 66;
+
+__global__ void __launch_bounds__(128)
+attn_decode_split_kernel(const float *__restrict__ q, long ldq, const float *__restrict__ kc,
+                         const float *__restrict__ vc, long Tmax, int len, const int *__restrict__ pos_dev,
+                         float *__restrict__ part, int *__restrict__ tickets, float *__restrict__ out,
+                         int C, int H, int S, float scale) {
+    pdl_trigger();
+    pdl_wait();
+    if (pos_dev) len = *pos_dev + 1;
+    const int bh = blockIdx.x, split = blockIdx.y, b = bh / H, h = bh % H;
+    const int j0 = split * DEC_KEYS;
+    if (j0 >= len) return;  // uniform over the block: an empty chunk takes no ticket
+    float *pp = part + ((long)bh * S + split) * DEC_PART;
+    __shared__ float sc[DEC_KEYS], pr[DEC_KEYS], so[64], red[2];
+    __shared__ int last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, half = lane >> 4, l16 = lane & 15;
+    const float4 qv = *(const float4 *)(q + (long)b * ldq + h * 64 + 4 * l16);
+    const float *kb = kc + (long)b * Tmax * C + h * 64 + 4 * l16;
+    float d[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int j = j0 + warp * 16 + 2 * i + half;
+        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < len) kv = *(const float4 *)(kb + (long)j * C);
+        d[i] = qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) d[i] += __shfl_xor_sync(0xffffffffu, d[i], o);
+    if (l16 == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int jl = warp * 16 + 2 * i + half;
+            sc[jl] = (j0 + jl < len) ? d[i] * scale : -INFINITY;
+        }
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    if (threadIdx.x < DEC_KEYS) m = sc[threadIdx.x];
+    m = warp_max(m);
+    if (lane == 0 && warp < 2) red[warp] = m;
+    __syncthreads();
+    m = fmaxf(red[0], red[1]);  // sc[0] is a valid key: m is finite
+    __syncthreads();
+    if (threadIdx.x < DEC_KEYS) {
+        const float p = j0 + (int)threadIdx.x < len ? expf(sc[threadIdx.x] - m) : 0.f;
+        pr[threadIdx.x] = p;
+        const float w = warp_sum(p);
+        if (lane == 0) red[warp] = w;
+    }
+    __syncthreads();
+    // P V: thread (kh, dim) sums keys kh*32 .. kh*32+31 of its dim
+    const int dim = threadIdx.x & 63, kh = threadIdx.x >> 6;
+    const float *vb = vc + (long)b * Tmax * C + h * 64 + dim;
+    const int kend = min(DEC_KEYS, len - j0);
+    float acc = 0.f;
+#pragma unroll 8
+    for (int k = kh * 32; k < kh * 32 + 32; ++k)
+        if (k < kend) acc += pr[k] * vb[(long)(j0 + k) * C];
+    if (kh == 1) so[dim] = acc;
+    __syncthreads();
+    if (kh == 0) {
+        pp[2 + dim] = acc + so[dim];
+        if (dim == 0) {
+            pp[0] = m;
+            pp[1] = red[0] + red[1];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    const int ns = (len + DEC_KEYS - 1) / DEC_KEYS;
+    if (threadIdx.x == 0) last = (atomicAdd(&tickets[bh], 1) == ns - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x < 64) {
+        const float *pb = part + (long)bh * S * DEC_PART;
+        float M = -INFINITY;
+        for (int k = 0; k < ns; ++k) M = fmaxf(M, __ldcg(pb + k * DEC_PART));
+        float L = 0.f, O = 0.f;
+        for (int k = 0; k < ns; ++k) {
+            const float w = expf(__ldcg(pb + k * DEC_PART) - M);
+            L += __ldcg(pb + k * DEC_PART + 1) * w;
+            O += __ldcg(pb + k * DEC_PART + 2 + threadIdx.x) * w;
+        }
+        out[(long)b * C + h * 64 + threadIdx.x] = O / L;
+        if (threadIdx.x == 0) tickets[bh] = 0;
+    }
+}
+
 template <typename K>
 int set_smem(K kern, int bytes) {
     CG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
@@ -819,12 +920,32 @@ int attention_bwd(const float *qkv, const float *out, const float *dout, const f
 
 int attention_decode_impl(const float *q, long ldq, const float *kcache, const float *vcache,
                           long Tmax, int len, const int *pos_dev, float *out, int B, int C, int H,
-                          cudaStream_t s) {
+                          float *part, cudaStream_t s) {
     const int hs = C / H;
     const int cap = pos_dev ? (int)Tmax : len;
     if (hs > 256 || cap <= 0) {
         set_last_error(ERR_ARG, "attention_decode: unsupported hs=%d len=%d", hs, cap);
         return ERR_ARG;
+    }
+    const float scale = 1.0f / sqrtf((float)hs);
+    const bool vec4 = (C % 4 == 0) && (ldq % 4 == 0) && ((uintptr_t)kcache % 16) == 0 &&
+                      ((uintptr_t)vcache % 16) == 0 && ((uintptr_t)q % 16) == 0;
+    if (part && hs == 64 && vec4) {
+        const int S = (cap + DEC_KEYS - 1) / DEC_KEYS;
+        int *tickets = (int *)(part + (size_t)B * H * S * DEC_PART);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(B * H, S);
+        cfg.blockDim = dim3(128);
+        cfg.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        CG_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_split_kernel, q, ldq, kcache, vcache, Tmax, len, pos_dev,
+                                   part, tickets, out, C, H, S, scale));
+        ++g_launch_count;
+        return OK;
     }
     const int G = 256 / hs;
     const size_t smem = (size_t)(hs + cap + 64 + G * hs) * sizeof(float);
@@ -834,21 +955,25 @@ int attention_decode_impl(const float *q, long ldq, const float *kcache, const f
     }
     static bool a = false;
     if (!a) { CG_TRY(set_smem(attn_decode_kernel, 200 * 1024 + 4096)); a = true; }
-    const int vec4 = (C % 4 == 0) && ((uintptr_t)kcache % 16) == 0;
-    attn_decode_kernel<<<B * H, 256, smem, s>>>(q, ldq, kcache, vcache, Tmax, len, out, C, H, hs,
-                                                1.0f / sqrtf((float)hs), vec4, pos_dev);
+    attn_decode_kernel<<<B * H, 256, smem, s>>>(q, ldq, kcache, vcache, Tmax, len, out, C, H, hs, scale,
+                                                (C % 4 == 0) && ((uintptr_t)kcache % 16) == 0, pos_dev);
     LAUNCH_CHECK();
     return OK;
 }
 
+size_t attention_decode_scratch_floats(int B, int H, long Tmax) {
+    // partials, then one int ticket per (sequence, head)
+    return (size_t)B * H * ((Tmax + DEC_KEYS - 1) / DEC_KEYS) * DEC_PART + (size_t)B * H;
+}
+
 int attention_decode(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
-                     int len, float *out, int B, int C, int H, cudaStream_t s) {
-    return attention_decode_impl(q, ldq, kcache, vcache, Tmax, len, nullptr, out, B, C, H, s);
+                     int len, float *out, int B, int C, int H, float *part, cudaStream_t s) {
+    return attention_decode_impl(q, ldq, kcache, vcache, Tmax, len, nullptr, out, B, C, H, part, s);
 }
 
 int attention_decode_at(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
-                        const int *pos_dev, float *out, int B, int C, int H, cudaStream_t s) {
-    return attention_decode_impl(q, ldq, kcache, vcache, Tmax, 0, pos_dev, out, B, C, H, s);
+                        const int *pos_dev, float *out, int B, int C, int H, float *part, cudaStream_t s) {
+    return attention_decode_impl(q, ldq, kcache, vcache, Tmax, 0, pos_dev, out, B, C, H, part, s);
 }
 
 }  // namespace cg

@@ -22,7 +22,7 @@ namespace cg {
 
 // NCCL is opened on first use rather than linked: a process that loads this
 // library before PyTorch must not pin the system libnccl.so.2 ahead of the
-// one PyTorch ships (and a process without data parallelism needs none).
+// one PyTorch ships (and a process without collectives needs none).
 namespace {
 struct Nccl {
     void *h = nullptr;
@@ -30,9 +30,17 @@ struct Nccl {
     ncclResult_t (*commInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*allReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t) = nullptr;
+    ncclResult_t (*allGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
     ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
     const char *(*errorString)(ncclResult_t) = nullptr;
 } g_nccl;
+
+int nccl_fail(const char *what, ncclResult_t r) {
+    set_last_error(ERR_NCCL, "%s: %s", what, g_nccl.errorString(r));
+    return ERR_NCCL;
+}
+}  // namespace
 
 int nccl_open() {
     if (g_nccl.h) return OK;
@@ -44,26 +52,47 @@ int nccl_open() {
     g_nccl.getUniqueId = (decltype(g_nccl.getUniqueId))dlsym(h, "ncclGetUniqueId");
     g_nccl.commInitRank = (decltype(g_nccl.commInitRank))dlsym(h, "ncclCommInitRank");
     g_nccl.allReduce = (decltype(g_nccl.allReduce))dlsym(h, "ncclAllReduce");
+    g_nccl.allGather = (decltype(g_nccl.allGather))dlsym(h, "ncclAllGather");
     g_nccl.commDestroy = (decltype(g_nccl.commDestroy))dlsym(h, "ncclCommDestroy");
     g_nccl.errorString = (decltype(g_nccl.errorString))dlsym(h, "ncclGetErrorString");
-    if (!g_nccl.getUniqueId || !g_nccl.commInitRank || !g_nccl.allReduce || !g_nccl.commDestroy ||
-        !g_nccl.errorString) {
+    if (!g_nccl.getUniqueId || !g_nccl.commInitRank || !g_nccl.allReduce || !g_nccl.allGather ||
+        !g_nccl.commDestroy || !g_nccl.errorString) {
         set_last_error(ERR_NCCL, "libnccl.so.2 lacks an expected entry point");
         return ERR_NCCL;
     }
     g_nccl.h = h;
     return OK;
 }
-}  // namespace
+
+int nccl_comm_init(void **comm, const unsigned char id[128], int world, int rank) {
+    CG_TRY(nccl_open());
+    ncclUniqueId uid;
+    memcpy(&uid, id, 128);
+    ncclComm_t c;
+    const ncclResult_t r = g_nccl.commInitRank(&c, world, uid, rank);
+    if (r != ncclSuccess) return nccl_fail("ncclCommInitRank", r);
+    *comm = c;
+    return OK;
+}
+
+void nccl_comm_destroy(void *comm) {
+    if (comm && g_nccl.h) g_nccl.commDestroy((ncclComm_t)comm);
+}
+
+int nccl_allreduce_sum(float *buf, size_t n, void *comm, cudaStream_t s) {
+    const ncclResult_t r = g_nccl.allReduce(buf, buf, n, ncclFloat, ncclSum, (ncclComm_t)comm, s);
+    return r == ncclSuccess ? OK : nccl_fail("ncclAllReduce", r);
+}
+
+int nccl_allgather_words(const void *src, void *dst, size_t words, void *comm, cudaStream_t s) {
+    const ncclResult_t r = g_nccl.allGather(src, dst, words, ncclInt32, (ncclComm_t)comm, s);
+    return r == ncclSuccess ? OK : nccl_fail("ncclAllGather", r);
+}
 
 int dp_allreduce(ModelCtx *c, float *buf, size_t n, cudaStream_t s) {
     if (c->world <= 1 || !c->nccl_comm) return OK;
     ncclResult_t r = g_nccl.allReduce(buf, buf, n, ncclFloat, ncclAvg, (ncclComm_t)c->nccl_comm, s);
-    if (r != ncclSuccess) {
-        set_last_error(ERR_NCCL, "ncclAllReduce: %s", g_nccl.errorString(r));
-        return ERR_NCCL;
-    }
-    return OK;
+    return r == ncclSuccess ? OK : nccl_fail("ncclAllReduce", r);
 }
 
 }  // namespace cg
@@ -95,15 +124,8 @@ extern "C" int cngpt_cuda_dp_init(GPT *m, const unsigned char id[128], int world
         c->rank = 0;
         return OK;
     }
-    CG_TRY(nccl_open());
-    ncclUniqueId uid;
-    memcpy(&uid, id, 128);
-    ncclComm_t comm;
-    ncclResult_t r = g_nccl.commInitRank(&comm, world, uid, rank);
-    if (r != ncclSuccess) {
-        set_last_error(ERR_NCCL, "ncclCommInitRank: %s", g_nccl.errorString(r));
-        return ERR_NCCL;
-    }
+    void *comm = nullptr;
+    CG_TRY(nccl_comm_init(&comm, id, world, rank));
     c->nccl_comm = comm;
     c->world = world;
     c->rank = rank;
@@ -121,7 +143,7 @@ extern "C" int cngpt_cuda_dp_free(GPT *m) {
     if (!c) return ERR_STATE;
     if (c->nccl_comm) {
         cudaStreamSynchronize(g_stream);
-        g_nccl.commDestroy((ncclComm_t)c->nccl_comm);
+        nccl_comm_destroy(c->nccl_comm);
         c->nccl_comm = nullptr;
     }
     c->world = 1;

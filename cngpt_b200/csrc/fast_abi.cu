@@ -157,16 +157,24 @@ int decode_step(const GPT *m, FastCtx *f, FastDev *d, int B, cudaStream_t s) {
     CG_TRY(embed_fwd_at(d->next, w->wte, w->wpe, x, B, C, d->ctr, s));
     const size_t per = (size_t)d->kv_B * d->kv_T * C;
     for (int l = 0; l < L; l++) {
-        CG_TRY(layernorm_fwd(x, C, w->ln1_w[l], w->ln1_b[l], f->ln, C, f->mean, f->rstd, B, C, s));
-        CG_TRY(gemm(f->ln, C, false, w->c_attn_w[l], C, false, B, 3 * C, C,
-                    epi_store(f->qkv, 3 * C, w->c_attn_b[l]), s));
-        CG_TRY(kv_append_at(f->qkv, d->kc + l * per, d->vc + l * per, B, d->kv_T, C, d->ctr, s));
+        // LN1 fused into the qkv GEMV, whose epilogue also appends K and V
+        GemmEpi eq = epi_store(f->qkv, 3 * C, w->c_attn_b[l]);
+        eq.kc = d->kc + l * per;
+        eq.vc = d->vc + l * per;
+        eq.kv_ld = (long)d->kv_T * C;
+        eq.kv_pos = d->ctr;
+        eq.kv_C = C;
+        CG_TRY(gemm_ln(x, C, w->ln1_w[l], w->ln1_b[l], f->ln, w->c_attn_w[l], C, B, 3 * C, C, eq, s));
         CG_TRY(attention_decode_at(f->qkv, 3L * C, d->kc + l * per, d->vc + l * per, d->kv_T, d->ctr,
-                                   d->al, B, C, H, s));
-        CG_TRY(block_tail(m, l, f, x, d->al, B, s));
+                                   d->al, B, C, H, d->dec_part, s));
+        CG_TRY(gemm(d->al, C, false, w->c_proj_w[l], C, false, B, C, C,
+                    epi_resid_inplace(x, C, w->c_proj_b[l]), s));
+        CG_TRY(gemm_ln(x, C, w->ln2_w[l], w->ln2_b[l], f->ln, w->mlp_fc_w[l], C, B, 4 * C, C,
+                       epi_gelu_only(f->hid, 4 * C, w->mlp_fc_b[l]), s));
+        CG_TRY(gemm(f->hid, 4 * C, false, w->mlp_proj_w[l], 4 * C, false, B, C, 4 * C,
+                    epi_resid_inplace(x, C, w->mlp_proj_b[l]), s));
     }
-    CG_TRY(layernorm_fwd(x, C, w->ln_f_w, w->ln_f_b, f->ln, C, f->mean, f->rstd, B, C, s));
-    CG_TRY(gemm(f->ln, C, false, w->wte, C, false, B, V, C, epi_store(f->logits, V, nullptr), s));
+    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, f->ln, w->wte, C, B, V, C, epi_store(f->logits, V, nullptr), s));
     CG_TRY(argmax_log(f->logits, V, B, V, d->next, d->gen, d->ctr + 1, s));
     return decode_advance(d->ctr, s);
 }
@@ -226,6 +234,7 @@ extern "C" void fast_free(FastCtx *f) {
         dev_free(d->tok);
         dev_free(d->kc);
         dev_free(d->vc);
+        dev_free(d->dec_part);
         dev_free(d->next);
         dev_free(d->gen);
         dev_free(d->ctr);
@@ -285,10 +294,14 @@ extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B,
         dev_free(d->kc);
         dev_free(d->vc);
         dev_free(d->next);
-        d->kc = d->vc = nullptr;
+        dev_free(d->dec_part);
+        d->kc = d->vc = d->dec_part = nullptr;
         d->next = nullptr;
         CG_TRY(dev_alloc((void **)&d->kc, L * B * Tmax * C * 4, false));
         CG_TRY(dev_alloc((void **)&d->vc, L * B * Tmax * C * 4, false));
+        CG_TRY(dev_alloc((void **)&d->dec_part,
+                         attention_decode_scratch_floats(B, m->cfg.n_head, Tmax) * 4, false));
+        CG_CUDA(cudaMemsetAsync(d->dec_part, 0, attention_decode_scratch_floats(B, m->cfg.n_head, Tmax) * 4, s));
         CG_TRY(dev_alloc((void **)&d->next, (size_t)B * 4, false));
         d->kv_B = B;
         d->kv_T = Tmax;

@@ -31,10 +31,13 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
 #include "common.cuh"
+#include "kernels.h"
 
 namespace cg {
 
@@ -109,10 +112,96 @@ __device__ __forceinline__ const float *epi_aux(const GemmEpi &e, long &ld) {
     }
 }
 
+// Epilogue of one 32x32 output block (thread = row on entry, `v` its 32
+// columns): transposed through the warp's padded shared tile `stile`; lane l
+// then handles row (4i + l/8) and columns 4(l%8)..+3 for i = 0..7 -
+// conflict-free shared reads, 16-byte global accesses, and the epilogue mode
+// switch outside the element loop.
+__device__ __forceinline__ void store_block(const GemmEpi &ep, float *stile, int lane, const float (&v)[32],
+                                            int m0, int n0, int M, int N, const float *aux, long ldaux) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stile[lane * 33 + j] = v[j];
+    __syncwarp();
+    const int rsub = lane >> 3, c4 = (lane & 7) * 4;
+    const int n = n0 + c4;
+    if (ep.vec4 && n + 3 < N) {
+        const float4 b4 = ep.bias ? *(const float4 *)(ep.bias + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float al = ep.alpha;
+        auto run = [&](auto op) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = i * 4 + rsub;
+                if (m0 + r < M) {
+                    const float *sp = stile + r * 33 + c4;
+                    float4 a = make_float4(sp[0] * al, sp[1] * al, sp[2] * al, sp[3] * al);
+                    op((long)(m0 + r), a);
+                }
+            }
+        };
+        switch (ep.mode) {
+            case EPI_STORE:
+                run([&](long m, float4 a) {
+                    *(float4 *)(ep.D + m * ep.ldd + n) =
+                        make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
+                });
+                break;
+            case EPI_ACCUM:
+                run([&](long m, float4 a) {
+                    float4 *d = (float4 *)(ep.D + m * ep.ldd + n);
+                    const float4 o = *d;
+                    *d = make_float4((o.x + a.x) + b4.x, (o.y + a.y) + b4.y, (o.z + a.z) + b4.z,
+                                     (o.w + a.w) + b4.w);
+                });
+                break;
+            case EPI_GELU:
+                run([&](long m, float4 a) {
+                    a = make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
+                    if (ep.D) *(float4 *)(ep.D + m * ep.ldd + n) = a;
+                    *(float4 *)(ep.D2 + m * ep.ldd2 + n) =
+                        make_float4(gelu_tanh(a.x), gelu_tanh(a.y), gelu_tanh(a.z), gelu_tanh(a.w));
+                });
+                break;
+            case EPI_RESID:
+                run([&](long m, float4 a) {
+                    a = make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
+                    if (ep.D) *(float4 *)(ep.D + m * ep.ldd + n) = a;
+                    const float4 r = *(const float4 *)(ep.R + m * ep.ldr + n);
+                    *(float4 *)(ep.D2 + m * ep.ldd2 + n) =
+                        make_float4(r.x + a.x, r.y + a.y, r.z + a.z, r.w + a.w);
+                });
+                break;
+            case EPI_GELU_BWD:
+                run([&](long m, float4 a) {
+                    const float4 g = *(const float4 *)(ep.G + m * ep.ldg + n);
+                    *(float4 *)(ep.D + m * ep.ldd + n) =
+                        make_float4(a.x * gelu_tanh_grad(g.x), a.y * gelu_tanh_grad(g.y),
+                                    a.z * gelu_tanh_grad(g.z), a.w * gelu_tanh_grad(g.w));
+                });
+                break;
+        }
+    } else {
+        // ragged edge or unaligned operands: one element at a time
+#pragma unroll 1
+        for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + rsub;
+            if (m0 + r >= M) continue;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int nj = n + j;
+                if (nj >= N) break;
+                const float x = aux ? aux[(long)(m0 + r) * ldaux + nj] : 0.0f;
+                epi_apply(ep, m0 + r, nj, stile[r * 33 + c4 + j], ep.bias ? ep.bias[nj] : 0.0f, x);
+            }
+        }
+    }
+    __syncwarp();
+    }
+
 template <int BN, bool A_MN, bool B_MN, bool SPLIT>
 __global__ void __launch_bounds__(Cfg<BN, SPLIT>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               int M, int N, int K, int tiles_m, int tiles_n, GemmEpi epi) {
+           int M, int N, int K, int tiles_m, int tiles_n, int ksplit, int kb_per,
+           long split_stride, GemmEpi epi) {
     using C = Cfg<BN, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -123,19 +212,314 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     auto sBlo = [&](int s) { return base + s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int num_tiles = tiles_m * tiles_n;
+    // work unit = (output tile, K split); split s covers k-blocks
+    // [s * kb_per, min(kblocks, (s + 1) * kb_per)), never empty (host-checked)
+    const int mn_tiles = tiles_m * tiles_n;
+    const int num_tiles = mn_tiles * ksplit;
     const int kblocks = (K + BK - 1) / BK;
+    auto krange = [&](int tile, int &kb0, int &kb1) {
+    kb0 = (tile / mn_tiles) * kb_per;
+    kb1 = min(kblocks, kb0 + kb_per);
+    };
+    volatile int *abort = &ctl->abort;
+
+    if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+        mbar_init(&ctl->full[s], 1);
+        mbar_init(&ctl->empty[s], 1);
+        mbar_init(&ctl->ready[s], 4);
+    }
+    for (int b = 0; b < 2; ++b) {
+        mbar_init(&ctl->tfull[b], 1);
+        mbar_init(&ctl->tempty[b], C::EPI_WARPS);
+    }
+    ctl->abort = 0;
+    fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = ctl->tmem_base;
+
+    if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int tm = (tile % mn_tiles) % tiles_m, tn = (tile % mn_tiles) / tiles_m;
+            int kb0, kb1;
+            krange(tile, kb0, kb1);
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, DEV_ERR_GEMM_PRODUCER, abort))
+                    goto done;
+                mbar_arrive_expect_tx(&ctl->full[stage], C::A_BYTES + C::B_BYTES);
+                if (A_MN) {
+#pragma unroll
+                    for (int j = 0; j < BM / 32; ++j)
+                        tma_load_2d(sA(stage) + j * (BK * 128), &tmA, &ctl->full[stage],
+                                    tm * BM + j * 32, kb * BK);
+                } else {
+                    tma_load_2d(sA(stage), &tmA, &ctl->full[stage], kb * BK, tm * BM);
+                }
+                if (B_MN) {
+#pragma unroll
+                    for (int j = 0; j < BN / 32; ++j)
+                        tma_load_2d(sB(stage) + j * (BK * 128), &tmB, &ctl->full[stage],
+                                    tn * BN + j * 32, kb * BK);
+                } else {
+                    tma_load_2d(sB(stage), &tmB, &ctl->full[stage], kb * BK, tn * BN);
+                }
+                if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+            }
+        }
+    }
+    } else if (warp == 1) {
+    // ------------------------------------------------- MMA issuer
+    if (lane == 0) {
+        constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+        // K-major (128B swizzle): rows of 128B, 8-row atoms 1024B apart; a
+        // k-step of 8 elements advances the start address by 32B in the atom.
+        // MN-major (128B swizzle, 32B atoms): 32-element MN atoms 4096B apart
+        // (one TMA box of BK rows each), 4-row K groups 512B apart; a k-step
+        // of 8 rows advances by 1024B.
+        auto descA = [&](uint8_t *p, int kk) -> uint64_t {
+            return A_MN ? smem_desc(smem_u32(p) + kk * 1024, BK * 128, 512, 1)
+                        : smem_desc(smem_u32(p) + kk * 32, 16, 1024, 2);
+        };
+        auto descB = [&](uint8_t *p, int kk) -> uint64_t {
+            return B_MN ? smem_desc(smem_u32(p) + kk * 1024, BK * 128, 512, 1)
+                        : smem_desc(smem_u32(p) + kk * 32, 16, 1024, 2);
+        };
+        int stage = 0, acc = 0;
+        uint32_t phase = 0, acc_phase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            int kb0, kb1;
+            krange(tile, kb0, kb1);
+            if constexpr (SPLIT) {
+                // one fresh TMEM accumulator per k-block: the epilogue adds
+                // the k-block partials in fp32 (round to nearest), which
+                // bounds the tensor core's truncating accumulation to 12
+                // steps per partial
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, DEV_ERR_GEMM_MMA, abort))
+                        goto done;
+                    if (!mbar_wait(&ctl->ready[stage], phase, DEV_ERR_GEMM_MMA, abort)) goto done;
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+#pragma unroll
+                    for (int kk = 0; kk < BK / MMA_K; ++kk) {
+                        const uint64_t a = descA(sA(stage), kk), b = descB(sB(stage), kk);
+                        mma_tf32(d_tmem, descA(sAlo(stage), kk), b, idesc, kk != 0);
+                        mma_tf32(d_tmem, a, descB(sBlo(stage), kk), idesc, 1);
+                        mma_tf32(d_tmem, a, b, idesc, 1);
+                    }
+                    mma_commit(&ctl->empty[stage]);
+                    mma_commit(&ctl->tfull[acc]);
+                    if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+                    if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+                }
+            } else {
+                if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, DEV_ERR_GEMM_MMA, abort))
+                    goto done;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(&ctl->full[stage], phase, DEV_ERR_GEMM_MMA, abort)) goto done;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < BK / MMA_K; ++kk)
+                        mma_tf32(d_tmem, descA(sA(stage), kk), descB(sB(stage), kk), idesc,
+                                 (kb != kb0 || kk != 0));
+                    mma_commit(&ctl->empty[stage]);
+                    if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+                }
+                mma_commit(&ctl->tfull[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+        }
+    }
+    } else if (warp < 2 + C::EPI_WARPS) {
+    // --------------------------------------------------- epilogue
+    // Warp w owns TMEM lanes [32q, 32q+32), q = w % 4, and half of the
+    // tile's columns. A 32x32 block is read with one tcgen05.ld (thread =
+    // row), transposed through padded shared memory, and written back by
+    // rows so every global access of the warp is coalesced; the block's
+    // second operand rows (residual / GELU input / accumulator) are all
+    // loaded before use so 32 loads are in flight per thread.
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    constexpr int CH = BN / 64;  // 32-column chunks per warp
+    float *stile = (float *)(base + C::STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    GemmEpi ep = epi;  // ep.D moves to the split's partial-sum slice
+    long ldaux = 0;
+    const float *aux = epi_aux(epi, ldaux);
+    auto store_block_ = [&](const float (&v)[32], int m0, int n0) {
+        store_block(ep, stile, lane, v, m0, n0, M, N, aux, ldaux);
+    };
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int tm = (tile % mn_tiles) % tiles_m, tn = (tile % mn_tiles) / tiles_m;
+        int kb0, kb1;
+        krange(tile, kb0, kb1);
+        ep.D = epi.D + (tile / mn_tiles) * split_stride;
+        const int m0 = tm * BM + q * 32;
+        const int c0 = half * CH;
+        if constexpr (SPLIT) {
+            float sum[CH * 32];
+#pragma unroll
+            for (int j = 0; j < CH * 32; ++j) sum[j] = 0.0f;
+            bool ok = true;
+            for (int kb = kb0; kb < kb1 && ok; ++kb) {
+                if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < CH; ++c) {
+                    float v[32];
+                    tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) +
+                                           ((uint32_t)(q * 32) << 16), v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[c * 32 + j] += v[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+            if (!ok) break;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = sum[c * 32 + j];
+                store_block_(v, m0, tn * BN + (c0 + c) * 32);
+            }
+        } else {
+            if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < CH; ++c) {
+                float v[32];
+                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) +
+                                       ((uint32_t)(q * 32) << 16), v);
+                store_block_(v, m0, tn * BN + (c0 + c) * 32);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+    }
+    } else if (SPLIT) {
+    // ---------------------------------------- 3xTF32 split transform
+    const int t = threadIdx.x - (2 + C::EPI_WARPS) * 32;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int kb0, kb1;
+        krange(tile, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+            if (!mbar_wait(&ctl->full[stage], phase, DEV_ERR_GEMM_TRANSFORM, abort)) goto done;
+            float4 *hi = (float4 *)sA(stage);
+            float4 *lo = (float4 *)sAlo(stage);
+            constexpr int n4 = (C::A_BYTES + C::B_BYTES) / 16;
+            for (int i = t; i < n4; i += 128) {
+                float4 x = hi[i], h, l;
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.x) : "f"(x.x));
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.y) : "f"(x.y));
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.z) : "f"(x.z));
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.w) : "f"(x.w));
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.x) : "f"(x.x - h.x));
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.y) : "f"(x.y - h.y));
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.z) : "f"(x.z - h.z));
+                asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.w) : "f"(x.w - h.w));
+                hi[i] = h;
+                lo[i] = l;
+            }
+            // generic-proxy smem writes -> visible to the tensor core (async proxy)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->ready[stage]);
+            if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+    }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------- CTA-pair (cta_group::2) GEMM
+// The same persistent warp-specialised GEMM over a 2-CTA cluster: the pair
+// owns a 256 x BN output tile, each CTA loads its own 128 rows of A and half
+// of the BN rows of B into its shared memory, and the leader CTA (rank 0)
+// issues tcgen05.mma.cta_group::2 with M = 256, which reads both CTAs' halves
+// and leaves rows [128r, 128r + 128) of the accumulator in CTA r's TMEM. Per
+// CTA that halves the B bytes per FLOP, so a k-block stage is 24-32 KB
+// instead of 48 KB and 6-8 stages fit. Loads are plain (no multicast); both
+// CTAs' TMA completions count on the leader's `full` barrier, the MMA commits
+// arrive on `empty` / `tfull` in both CTAs, and the epilogue warps of both
+// CTAs release an accumulator on the leader's `tempty`. TF32 mode only.
+template <int BN>
+struct Cfg2 {
+    static constexpr int BNH = BN / 2;  // B rows per CTA
+    static constexpr int A_BYTES = BM * KB_BYTES;
+    static constexpr int B_BYTES = BNH * KB_BYTES;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = BN == 256 ? 6 : 8;
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + EPI_WARPS * 32 * 33 * 4;
+};
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg2<BN>::THREADS, 1)
+gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                int M, int N, int K, int tiles_m, int tiles_n, int ksplit, int kb_per, long split_stride,
+                GemmEpi epi) {
+    using C = Cfg2<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    SmemCtl *ctl = (SmemCtl *)(base + C::STAGES * C::STAGE_BYTES);
+    auto sA = [&](int s) { return base + s * C::STAGE_BYTES; };
+    auto sB = [&](int s) { return base + s * C::STAGE_BYTES + C::A_BYTES; };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int mn_tiles = tiles_m * tiles_n;
+    const int num_tiles = mn_tiles * ksplit;
+    const int kblocks = (K + BK - 1) / BK;
+    auto krange = [&](int tile, int &kb0, int &kb1) {
+        kb0 = (tile / mn_tiles) * kb_per;
+        kb1 = min(kblocks, kb0 + kb_per);
+    };
     volatile int *abort = &ctl->abort;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(&ctl->full[s], 1);
             mbar_init(&ctl->empty[s], 1);
-            mbar_init(&ctl->ready[s], 4);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&ctl->tfull[b], 1);
-            mbar_init(&ctl->tempty[b], C::EPI_WARPS);
+            mbar_init(&ctl->tempty[b], 2 * C::EPI_WARPS);
         }
         ctl->abort = 0;
         fence_mbar_init();
@@ -145,54 +529,52 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(&ctl->tmem_base, C::TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc_pair(&ctl->tmem_base, C::TMEM_COLS);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = ctl->tmem_base;
 
     if (warp == 0) {
-        // ------------------------------------------------ TMA producer
+        // ------------------------------------------------ TMA producer (both CTAs)
         if (lane == 0) {
+            const uint32_t full_leader = mapa_shared(smem_u32(&ctl->full[0]), 0);
             int stage = 0;
             uint32_t phase = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-                const int tm = tile % tiles_m, tn = tile / tiles_m;
-                for (int kb = 0; kb < kblocks; ++kb) {
+            for (int tile = pair; tile < num_tiles; tile += npairs) {
+                const int tm = (tile % mn_tiles) % tiles_m, tn = (tile % mn_tiles) / tiles_m;
+                const int row0 = tm * 2 * BM + (int)rank * BM, col0 = tn * BN + (int)rank * C::BNH;
+                int kb0, kb1;
+                krange(tile, kb0, kb1);
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&ctl->empty[stage], phase ^ 1u, DEV_ERR_GEMM_PRODUCER, abort))
                         goto done;
-                    mbar_arrive_expect_tx(&ctl->full[stage], C::A_BYTES + C::B_BYTES);
+                    if (rank == 0) mbar_arrive_expect_tx(&ctl->full[stage], 2 * C::STAGE_BYTES);
+                    const uint32_t bar = full_leader + stage * 8;
                     if (A_MN) {
 #pragma unroll
                         for (int j = 0; j < BM / 32; ++j)
-                            tma_load_2d(sA(stage) + j * (BK * 128), &tmA, &ctl->full[stage],
-                                        tm * BM + j * 32, kb * BK);
+                            tma_load_2d_pair(sA(stage) + j * (BK * 128), &tmA, bar, row0 + j * 32, kb * BK);
                     } else {
-                        tma_load_2d(sA(stage), &tmA, &ctl->full[stage], kb * BK, tm * BM);
+                        tma_load_2d_pair(sA(stage), &tmA, bar, kb * BK, row0);
                     }
                     if (B_MN) {
 #pragma unroll
-                        for (int j = 0; j < BN / 32; ++j)
-                            tma_load_2d(sB(stage) + j * (BK * 128), &tmB, &ctl->full[stage],
-                                        tn * BN + j * 32, kb * BK);
+                        for (int j = 0; j < C::BNH / 32; ++j)
+                            tma_load_2d_pair(sB(stage) + j * (BK * 128), &tmB, bar, col0 + j * 32, kb * BK);
                     } else {
-                        tma_load_2d(sB(stage), &tmB, &ctl->full[stage], kb * BK, tn * BN);
+                        tma_load_2d_pair(sB(stage), &tmB, bar, kb * BK, col0);
                     }
                     if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
-            // K-major (128B swizzle): rows of 128B, 8-row atoms 1024B apart; a
-            // k-step of 8 elements advances the start address by 32B in the atom.
-            // MN-major (128B swizzle, 32B atoms): 32-element MN atoms 4096B apart
-            // (one TMA box of BK rows each), 4-row K groups 512B apart; a k-step
-            // of 8 rows advances by 1024B.
+        // --------------------------------------------- MMA issuer (leader CTA)
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_tf32(2 * BM, BN, A_MN, B_MN);
             auto descA = [&](uint8_t *p, int kk) -> uint64_t {
                 return A_MN ? smem_desc(smem_u32(p) + kk * 1024, BK * 128, 512, 1)
                             : smem_desc(smem_u32(p) + kk * 32, 16, 1024, 2);
@@ -203,237 +585,63 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             };
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-                if constexpr (SPLIT) {
-                    // one fresh TMEM accumulator per k-block: the epilogue adds
-                    // the k-block partials in fp32 (round to nearest), which
-                    // bounds the tensor core's truncating accumulation to 12
-                    // steps per partial
-                    for (int kb = 0; kb < kblocks; ++kb) {
-                        if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, DEV_ERR_GEMM_MMA, abort))
-                            goto done;
-                        if (!mbar_wait(&ctl->ready[stage], phase, DEV_ERR_GEMM_MMA, abort)) goto done;
-                        tc_fence_after();
-                        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-#pragma unroll
-                        for (int kk = 0; kk < BK / MMA_K; ++kk) {
-                            const uint64_t a = descA(sA(stage), kk), b = descB(sB(stage), kk);
-                            mma_tf32(d_tmem, descA(sAlo(stage), kk), b, idesc, kk != 0);
-                            mma_tf32(d_tmem, a, descB(sBlo(stage), kk), idesc, 1);
-                            mma_tf32(d_tmem, a, b, idesc, 1);
-                        }
-                        mma_commit(&ctl->empty[stage]);
-                        mma_commit(&ctl->tfull[acc]);
-                        if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
-                        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-                    }
-                } else {
-                    if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, DEV_ERR_GEMM_MMA, abort))
-                        goto done;
-                    tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                    for (int kb = 0; kb < kblocks; ++kb) {
-                        if (!mbar_wait(&ctl->full[stage], phase, DEV_ERR_GEMM_MMA, abort)) goto done;
-                        tc_fence_after();
-#pragma unroll
-                        for (int kk = 0; kk < BK / MMA_K; ++kk)
-                            mma_tf32(d_tmem, descA(sA(stage), kk), descB(sB(stage), kk), idesc,
-                                     (kb | kk) != 0);
-                        mma_commit(&ctl->empty[stage]);
-                        if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
-                    }
-                    mma_commit(&ctl->tfull[acc]);
-                    if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-                }
-            }
-        }
-    } else if (warp < 2 + C::EPI_WARPS) {
-        // --------------------------------------------------- epilogue
-        // Warp w owns TMEM lanes [32q, 32q+32), q = w % 4, and half of the
-        // tile's columns. A 32x32 block is read with one tcgen05.ld (thread =
-        // row), transposed through padded shared memory, and written back by
-        // rows so every global access of the warp is coalesced; the block's
-        // second operand rows (residual / GELU input / accumulator) are all
-        // loaded before use so 32 loads are in flight per thread.
-        const int q = warp & 3, half = (warp - 2) >> 2;
-        constexpr int CH = BN / 64;  // 32-column chunks per warp
-        float *stile = (float *)(base + C::STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
-        int acc = 0;
-        uint32_t acc_phase = 0;
-        long ldaux = 0;
-        const float *aux = epi_aux(epi, ldaux);
-        // Writes one 32x32 block (thread = row on entry). After the shared-memory
-        // transpose, lane l handles row (4i + l/8) and columns 4(l%8)..+3 for
-        // i = 0..7: conflict-free shared reads, 16-byte global accesses, and
-        // the epilogue mode switch outside the element loop.
-        auto store_block = [&](const float (&v)[32], int m0, int n0) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) stile[lane * 33 + j] = v[j];
-            __syncwarp();
-            const int rsub = lane >> 3, c4 = (lane & 7) * 4;
-            const int n = n0 + c4;
-            if (epi.vec4 && n + 3 < N) {
-                const float4 b4 = epi.bias ? *(const float4 *)(epi.bias + n) : make_float4(0.f, 0.f, 0.f, 0.f);
-                const float al = epi.alpha;
-                auto run = [&](auto op) {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int r = i * 4 + rsub;
-                        if (m0 + r < M) {
-                            const float *sp = stile + r * 33 + c4;
-                            float4 a = make_float4(sp[0] * al, sp[1] * al, sp[2] * al, sp[3] * al);
-                            op((long)(m0 + r), a);
-                        }
-                    }
-                };
-                switch (epi.mode) {
-                    case EPI_STORE:
-                        run([&](long m, float4 a) {
-                            *(float4 *)(epi.D + m * epi.ldd + n) =
-                                make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
-                        });
-                        break;
-                    case EPI_ACCUM:
-                        run([&](long m, float4 a) {
-                            float4 *d = (float4 *)(epi.D + m * epi.ldd + n);
-                            const float4 o = *d;
-                            *d = make_float4((o.x + a.x) + b4.x, (o.y + a.y) + b4.y, (o.z + a.z) + b4.z,
-                                             (o.w + a.w) + b4.w);
-                        });
-                        break;
-                    case EPI_GELU:
-                        run([&](long m, float4 a) {
-                            a = make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
-                            if (epi.D) *(float4 *)(epi.D + m * epi.ldd + n) = a;
-                            *(float4 *)(epi.D2 + m * epi.ldd2 + n) =
-                                make_float4(gelu_tanh(a.x), gelu_tanh(a.y), gelu_tanh(a.z), gelu_tanh(a.w));
-                        });
-                        break;
-                    case EPI_RESID:
-                        run([&](long m, float4 a) {
-                            a = make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
-                            if (epi.D) *(float4 *)(epi.D + m * epi.ldd + n) = a;
-                            const float4 r = *(const float4 *)(epi.R + m * epi.ldr + n);
-                            *(float4 *)(epi.D2 + m * epi.ldd2 + n) =
-                                make_float4(r.x + a.x, r.y + a.y, r.z + a.z, r.w + a.w);
-                        });
-                        break;
-                    case EPI_GELU_BWD:
-                        run([&](long m, float4 a) {
-                            const float4 g = *(const float4 *)(epi.G + m * epi.ldg + n);
-                            *(float4 *)(epi.D + m * epi.ldd + n) =
-                                make_float4(a.x * gelu_tanh_grad(g.x), a.y * gelu_tanh_grad(g.y),
-                                            a.z * gelu_tanh_grad(g.z), a.w * gelu_tanh_grad(g.w));
-                        });
-                        break;
-                }
-            } else {
-                // ragged edge or unaligned operands: one element at a time
-#pragma unroll 1
-                for (int i = 0; i < 8; ++i) {
-                    const int r = i * 4 + rsub;
-                    if (m0 + r >= M) continue;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int nj = n + j;
-                        if (nj >= N) break;
-                        const float x = aux ? aux[(long)(m0 + r) * ldaux + nj] : 0.0f;
-                        epi_apply(epi, m0 + r, nj, stile[r * 33 + c4 + j], epi.bias ? epi.bias[nj] : 0.0f, x);
-                    }
-                }
-            }
-            __syncwarp();
-        };
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int tm = tile % tiles_m, tn = tile / tiles_m;
-            const int m0 = tm * BM + q * 32;
-            const int c0 = half * CH;
-            if constexpr (SPLIT) {
-                float sum[CH * 32];
-#pragma unroll
-                for (int j = 0; j < CH * 32; ++j) sum[j] = 0.0f;
-                bool ok = true;
-                for (int kb = 0; kb < kblocks && ok; ++kb) {
-                    if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-#pragma unroll
-                    for (int c = 0; c < CH; ++c) {
-                        float v[32];
-                        tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) +
-                                               ((uint32_t)(q * 32) << 16), v);
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) sum[c * 32 + j] += v[j];
-                    }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
-                    if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-                }
-                if (!ok) break;
-#pragma unroll
-                for (int c = 0; c < CH; ++c) {
-                    float v[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = sum[c * 32 + j];
-                    store_block(v, m0, tn * BN + (c0 + c) * 32);
-                }
-            } else {
-                if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) break;
+            for (int tile = pair; tile < num_tiles; tile += npairs) {
+                int kb0, kb1;
+                krange(tile, kb0, kb1);
+                if (!mbar_wait(&ctl->tempty[acc], acc_phase ^ 1u, DEV_ERR_GEMM_MMA, abort)) goto done;
                 tc_fence_after();
-#pragma unroll 1
-                for (int c = 0; c < CH; ++c) {
-                    float v[32];
-                    tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) +
-                                           ((uint32_t)(q * 32) << 16), v);
-                    store_block(v, m0, tn * BN + (c0 + c) * 32);
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!mbar_wait(&ctl->full[stage], phase, DEV_ERR_GEMM_MMA, abort)) goto done;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < BK / MMA_K; ++kk)
+                        mma_tf32_pair(d_tmem, descA(sA(stage), kk), descB(sB(stage), kk), idesc,
+                                      (kb != kb0 || kk != 0));
+                    mma_commit_pair(&ctl->empty[stage]);
+                    if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&ctl->tempty[acc]);
+                mma_commit_pair(&ctl->tfull[acc]);
                 if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
             }
         }
-    } else if (SPLIT) {
-        // ---------------------------------------- 3xTF32 split transform
-        const int t = threadIdx.x - (2 + C::EPI_WARPS) * 32;  // 0..127
-        int stage = 0;
-        uint32_t phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            for (int kb = 0; kb < kblocks; ++kb) {
-                if (!mbar_wait(&ctl->full[stage], phase, DEV_ERR_GEMM_TRANSFORM, abort)) goto done;
-                float4 *hi = (float4 *)sA(stage);
-                float4 *lo = (float4 *)sAlo(stage);
-                constexpr int n4 = (C::A_BYTES + C::B_BYTES) / 16;
-                for (int i = t; i < n4; i += 128) {
-                    float4 x = hi[i], h, l;
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.x) : "f"(x.x));
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.y) : "f"(x.y));
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.z) : "f"(x.z));
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&h.w) : "f"(x.w));
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.x) : "f"(x.x - h.x));
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.y) : "f"(x.y - h.y));
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.z) : "f"(x.z - h.z));
-                    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(*(uint32_t *)&l.w) : "f"(x.w - h.w));
-                    hi[i] = h;
-                    lo[i] = l;
-                }
-                // generic-proxy smem writes -> visible to the tensor core (async proxy)
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&ctl->ready[stage]);
-                if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+    } else {
+        // ------------------------------------------------- epilogue (both CTAs)
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        constexpr int CH = BN / 64;
+        float *stile = (float *)(base + C::STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
+        const uint32_t tempty_leader = mapa_shared(smem_u32(&ctl->tempty[0]), 0);
+        GemmEpi ep = epi;
+        long ldaux = 0;
+        const float *aux = epi_aux(epi, ldaux);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = pair; tile < num_tiles; tile += npairs) {
+            const int tm = (tile % mn_tiles) % tiles_m, tn = (tile % mn_tiles) / tiles_m;
+            ep.D = epi.D + (tile / mn_tiles) * split_stride;
+            const int m0 = tm * 2 * BM + (int)rank * BM + q * 32;
+            const int c0 = half * CH;
+            if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < CH; ++c) {
+                float v[32];
+                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) + ((uint32_t)(q * 32) << 16), v);
+                store_block(ep, stile, lane, v, m0, tn * BN + (c0 + c) * 32, M, N, aux, ldaux);
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
     }
 done:
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();  // no CTA leaves while its pair may still signal or read it
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::TMEM_COLS);
+        tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
     }
 }
 
@@ -490,61 +698,210 @@ gemm_simt_kernel(const float *__restrict__ A, long lda, int a_mn, const float *_
 
 // ------------------------------------------------- skinny GEMM (GEMV) path
 // out[m, n] = sum_k X[m, k] W[n, k] for M <= 8 rows (batch-1..8 decode and
-// the fast path's last-position rows). HBM-bound on W: every warp streams
-// two rows of W with 16-byte loads (both operands K-major, K % 4 == 0,
-// 16-byte aligned), each X load feeds both rows, fp32 FMA accumulation, a
-// warp-shuffle reduction and the fused epilogue of the tensor-core kernel.
-constexpr int GEMV_ROWS = 2;  // W rows per warp
+// the LM head of the last positions): HBM-bound on W, which is streamed once
+// with evict-first loads. A block of 256 threads owns GV_R rows of W and its
+// threads split K in float4 units, so every block keeps R 16-byte loads per
+// thread in flight whatever the shape. The R*MT partial sums of a thread are
+// reduced across the warp by recursive halving (lane L ends with one total),
+// then across the 8 warps through shared memory in warp order (fixed order,
+// deterministic).
+//
+// Launched with programmatic dependent launch: the first two K-steps of W are
+// loaded (and the rest prefetched into L2) before griddepcontrol.wait, so the
+// weight stream overlaps the tail of the kernel that produces X.
+constexpr int GV_R = 4, GV_THREADS = 256;
 
-template <int MT>
-__global__ void __launch_bounds__(256)
+__device__ __forceinline__ float dot4(const float4 a, const float4 b) {
+    return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+}
+
+template <int N>
+__device__ __forceinline__ void halve_step(float *acc, int lane, int o, int &idx) {
+    constexpr int h = N / 2;
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+        const float send = up ? acc[i] : acc[i + h];
+        const float keep = up ? acc[i + h] : acc[i];
+        acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+    if (up) idx += h;
+}
+
+template <int MT, bool LNF>
+__global__ void __launch_bounds__(GV_THREADS)
 gemv_kernel(const float *__restrict__ X, long ldx, const float *__restrict__ W, long ldw, int M, int N,
-            int K, GemmEpi epi) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = (blockIdx.x * 8 + warp) * GEMV_ROWS;
-    if (n0 >= N) return;
-    const int K4 = K / 4;
-    float acc[GEMV_ROWS][MT];
+            int K, GemmEpi epi, const float *__restrict__ lnw, const float *__restrict__ lnb) {
+    constexpr int R = GV_R, NV = R * MT;
+    __shared__ float red[GV_THREADS / 32][NV];
+    __shared__ float lnred[GV_THREADS / 32][MT], lnstat[2][MT];
+    pdl_trigger();
+    const int n0 = blockIdx.x * R, K4 = K >> 2, t = threadIdx.x;
+    const int lane = t & 31, warp = t >> 5;
+    const float4 *w4[R];
 #pragma unroll
-    for (int r = 0; r < GEMV_ROWS; ++r)
+    for (int r = 0; r < R; ++r) w4[r] = (const float4 *)(W + (long)min(n0 + r, N - 1) * ldw);
+    // before the producer of X has finished: W of the first two K-steps into
+    // registers, the rest of this thread's W into L2
+    float4 wp[2][R];
 #pragma unroll
-        for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
-    const float4 *w4[GEMV_ROWS];
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-    for (int r = 0; r < GEMV_ROWS; ++r) w4[r] = (const float4 *)(W + (long)min(n0 + r, N - 1) * ldw);
-#pragma unroll 2
-    for (int k = lane; k < K4; k += 32) {
-        float4 wv[GEMV_ROWS];
+        for (int r = 0; r < R; ++r)
+            wp[i][r] = (t + i * GV_THREADS < K4) ? __ldcs(w4[r] + t + i * GV_THREADS)
+                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = t + 2 * GV_THREADS; k < K4; k += 2 * GV_THREADS)
 #pragma unroll
-        for (int r = 0; r < GEMV_ROWS; ++r) wv[r] = __ldcs(w4[r] + k);  // streamed once: do not keep in L1
+        for (int r = 0; r < R; ++r) asm volatile("prefetch.global.L2 [%0];" ::"l"(w4[r] + k));
+    pdl_wait();
+    float mu[MT], rs[MT];
+    if constexpr (LNF) {
+        // LayerNorm statistics of the MT rows of X: mean, then the biased
+        // variance about it (two passes, as src/ops.c:231-247), block-reduced
+        // in fixed order
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            if (m < M) {
-                const float4 xv = __ldg((const float4 *)(X + (long)m * ldx) + k);
+        for (int pass = 0; pass < 2; ++pass) {
+            float ps[MT];
 #pragma unroll
-                for (int r = 0; r < GEMV_ROWS; ++r)
-                    acc[r][m] += wv[r].x * xv.x + wv[r].y * xv.y + wv[r].z * xv.z + wv[r].w * xv.w;
+            for (int m = 0; m < MT; ++m) ps[m] = 0.f;
+            for (int k = t; k < K4; k += GV_THREADS) {
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    if (m < M) {
+                        const float4 xv = __ldg((const float4 *)(X + (long)m * ldx) + k);
+                        if (pass == 0) {
+                            ps[m] += (xv.x + xv.y) + (xv.z + xv.w);
+                        } else {
+                            const float a = xv.x - mu[m], b = xv.y - mu[m], c = xv.z - mu[m], d = xv.w - mu[m];
+                            ps[m] += (a * a + b * b) + (c * c + d * d);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const float v = warp_sum(ps[m]);
+                if (lane == 0) lnred[warp][m] = v;
+            }
+            __syncthreads();
+            if (t < MT) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < GV_THREADS / 32; ++w) v += lnred[w][t];
+                lnstat[pass][t] = v / (float)K;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (pass == 0) mu[m] = lnstat[0][m];
+                else rs[m] = 1.0f / sqrtf(lnstat[1][m] + 1e-5f);
             }
         }
     }
+    auto xload = [&](int m, int k) -> float4 {
+        float4 xv = __ldg((const float4 *)(X + (long)m * ldx) + k);
+        if constexpr (LNF) {
+            const float4 g = __ldg((const float4 *)lnw + k), bb = __ldg((const float4 *)lnb + k);
+            xv.x = (xv.x - mu[m]) * rs[m] * g.x + bb.x;
+            xv.y = (xv.y - mu[m]) * rs[m] * g.y + bb.y;
+            xv.z = (xv.z - mu[m]) * rs[m] * g.z + bb.z;
+            xv.w = (xv.w - mu[m]) * rs[m] * g.w + bb.w;
+        }
+        return xv;
+    };
+    float acc[NV];
 #pragma unroll
-    for (int r = 0; r < GEMV_ROWS; ++r)
+    for (int i = 0; i < NV; ++i) acc[i] = 0.f;
 #pragma unroll
-        for (int m = 0; m < MT; ++m) acc[r][m] = warp_sum(acc[r][m]);
-    if (lane < GEMV_ROWS * MT) {
-        const int r = lane / MT, m = lane % MT, n = n0 + r;
+    for (int i = 0; i < 2; ++i) {
+        const int k = t + i * GV_THREADS;
+        if (k < K4) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (m < M) {
+                    const float4 xv = xload(m, k);
+#pragma unroll
+                    for (int r = 0; r < R; ++r) acc[r * MT + m] += dot4(wp[i][r], xv);
+                }
+            }
+        }
+    }
+#pragma unroll 2
+    for (int k = t + 2 * GV_THREADS; k < K4; k += GV_THREADS) {
+        float4 wv[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) wv[r] = __ldcs(w4[r] + k);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m < M) {
+                const float4 xv = xload(m, k);
+#pragma unroll
+                for (int r = 0; r < R; ++r) acc[r * MT + m] += dot4(wv[r], xv);
+            }
+        }
+    }
+    // recursive halving: at offset o a lane keeps the upper half of its
+    // values if (lane & o), the lower half otherwise, and adds the partner's
+    int idx = 0, o = 16;
+    if constexpr (NV >= 32) { halve_step<32>(acc, lane, o, idx); o >>= 1; }
+    if constexpr (NV >= 16) { halve_step<16>(acc, lane, o, idx); o >>= 1; }
+    if constexpr (NV >= 8) { halve_step<8>(acc, lane, o, idx); o >>= 1; }
+    if constexpr (NV >= 4) { halve_step<4>(acc, lane, o, idx); o >>= 1; }
+    if constexpr (NV >= 2) { halve_step<2>(acc, lane, o, idx); o >>= 1; }
+    for (; o > 0; o >>= 1) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
+    if ((lane & (32 / NV - 1)) == 0) red[warp][idx] = acc[0];
+    __syncthreads();
+    if (t < NV) {
         float v = 0.f;
 #pragma unroll
-        for (int rr = 0; rr < GEMV_ROWS; ++rr)
-#pragma unroll
-            for (int mm = 0; mm < MT; ++mm)
-                if (rr == r && mm == m) v = acc[rr][mm];
+        for (int w = 0; w < GV_THREADS / 32; ++w) v += red[w][t];
+        const int r = t / MT, m = t % MT, n = n0 + r;
         if (m < M && n < N) {
             long ld = 0;
             const float *ax = epi_aux(epi, ld);
-            epi_apply(epi, m, n, v, epi.bias ? epi.bias[n] : 0.0f, ax ? ax[(long)m * ld + n] : 0.0f);
+            const float bias = epi.bias ? epi.bias[n] : 0.0f;
+            epi_apply(epi, m, n, v, bias, ax ? ax[(long)m * ld + n] : 0.0f);
+            if (epi.kc && n >= epi.kv_C) {  // STORE mode: the K / V value just stored
+                const float val = v * epi.alpha + bias;
+                const long at = (long)m * epi.kv_ld + (long)(*epi.kv_pos) * epi.kv_C;
+                if (n < 2 * epi.kv_C) epi.kc[at + (n - epi.kv_C)] = val;
+                else epi.vc[at + (n - 2 * epi.kv_C)] = val;
+            }
         }
     }
+}
+
+template <int MT, bool LNF>
+int launch_gemv(const float *A, long lda, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi,
+                const float *lnw, const float *lnb, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((N + GV_R - 1) / GV_R);
+    cfg.blockDim = dim3(GV_THREADS);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    CG_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<MT, LNF>, A, lda, B, ldb, M, N, K, epi, lnw, lnb));
+    ++g_launch_count;
+    return OK;
+}
+
+template <bool LNF>
+int dispatch_gemv(const float *A, long lda, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi,
+                  const float *lnw, const float *lnb, cudaStream_t s) {
+    if (M <= 1) return launch_gemv<1, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, s);
+    if (M <= 2) return launch_gemv<2, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, s);
+    if (M <= 4) return launch_gemv<4, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, s);
+    return launch_gemv<8, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, s);
+}
+
+bool gemv_ok(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_mn, int M, int K,
+             const GemmEpi &epi) {
+    auto al = [](const void *p) { return ((uintptr_t)p % 16) == 0; };
+    return M <= 8 && !a_mn && !b_mn && K % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 && al(A) && al(B) &&
+           (!epi.kc || epi.mode == EPI_STORE);
 }
 
 // ------------------------------------------------------- tensor maps
@@ -616,6 +973,68 @@ int make_map(CUtensorMap *out, const float *p, long inner, long outer, long ld, 
     return OK;
 }
 
+// Split-K partial sums live in one fixed device buffer, allocated on first
+// use outside stream capture and never moved, so a captured graph that
+// replays a split GEMM keeps a valid pointer.
+constexpr size_t SPLITK_WS_FLOATS = size_t(32) << 20;  // 128 MiB
+float *g_splitk_ws = nullptr;
+int g_splitk_dev = -1;
+
+float *splitk_workspace(size_t floats, cudaStream_t s) {
+    if (floats > SPLITK_WS_FLOATS) return nullptr;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_splitk_ws) return g_splitk_dev == dev ? g_splitk_ws : nullptr;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+    if (cudaMalloc(&g_splitk_ws, SPLITK_WS_FLOATS * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        g_splitk_ws = nullptr;
+        return nullptr;
+    }
+    g_splitk_dev = dev;
+    return g_splitk_ws;
+}
+
+// out = epilogue(sum over splits of ws[s]) in split order (deterministic)
+__global__ void splitk_reduce_kernel(const float *__restrict__ ws, int S, long stride, int M, int N,
+                                     GemmEpi epi) {
+    long ld = 0;
+    const float *aux = epi_aux(epi, ld);
+    const long total = (long)M * N;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        float a = ws[i];
+        for (int k = 1; k < S; ++k) a += ws[k * stride + i];
+        const long m = i / N;
+        const int n = (int)(i - m * N);
+        epi_apply(epi, m, n, a, epi.bias ? epi.bias[n] : 0.0f, aux ? aux[m * ld + n] : 0.0f);
+    }
+}
+
+// Number of K splits for a GEMM with `tiles` output tiles: more work units
+// fill the last wave of the persistent grid, each extra split costs a write
+// and a read of an M x N partial. Modelled time, realistic rates.
+int choose_ksplit(int tiles, int kblocks, int M, int N, long K, bool split3, int workers = 0) {
+    const double sms = workers > 0 ? workers / 2 : num_sms();  // pair kernels: one worker per pair
+    const double flops = 2.0 * M * (double)N * K * (split3 ? 3.0 : 1.0);
+    const double peak = 450e12, hbm = 6e12;
+    auto cost = [&](int k) {
+        const double units = (double)tiles * k, waves = std::ceil(units / sms);
+        return flops / (peak * units / (waves * sms)) + (k > 1 ? 2.0 * k * M * (double)N * 4 / hbm : 0.0);
+    };
+    int best = 1;
+    double bt = cost(1);
+    for (int k = 2; k <= 8 && kblocks / k >= 4; ++k) {
+        const double t = cost(k);
+        if (t < 0.97 * bt) {
+            bt = t;
+            best = k;
+        }
+    }
+    return best;
+}
+
 template <int BN, bool A_MN, bool B_MN, bool SPLIT>
 int launch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, int K,
               const GemmEpi &epi, cudaStream_t s) {
@@ -633,8 +1052,111 @@ int launch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, 
     else      CG_TRY(make_map(&tb, B, K, N, ldb, BK, BN, false));
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n;
-    const int grid = std::min(tiles, num_sms());
-    kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, epi);
+    const int kblocks = (K + BK - 1) / BK;
+    int ks = choose_ksplit(tiles, kblocks, M, N, K, SPLIT);
+    int kb_per = (kblocks + ks - 1) / ks;
+    ks = (kblocks + kb_per - 1) / kb_per;  // every split non-empty
+    float *ws = ks > 1 ? splitk_workspace((size_t)ks * M * N, s) : nullptr;
+    if (!ws) {
+        ks = 1;
+        kb_per = kblocks;
+    }
+    const int grid = std::min(tiles * ks, num_sms());
+    if (ks == 1) {
+        kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, 1, kb_per, 0L, epi);
+        ++g_launch_count;
+        CG_CUDA(cudaGetLastError());
+        return OK;
+    }
+    GemmEpi pe;
+    pe.mode = EPI_STORE;
+    pe.D = ws;
+    pe.ldd = N;
+    pe.vec4 = (N % 4) == 0;
+    const long stride = (long)M * N;
+    kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, ks, kb_per, stride, pe);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    const int rgrid = (int)std::min<long>((stride + 255) / 256, (long)num_sms() * 8);
+    splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(ws, ks, stride, M, N, epi);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    return OK;
+}
+
+bool pair_gemm_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("CNGPT_CUDA_GEMM_PAIR");
+        on = (e && e[0] == '1') ? 1 : 0;
+    }
+    return on == 1;
+}
+
+// CTA pairs that can be resident at once for the pair kernel (clusters of 2
+// need both CTAs in one GPC; the count can be below num_sms / 2)
+template <typename Kern>
+int pair_slots(Kern kern, int threads, int smem) {
+    static int cached = -1;
+    if (cached > 0) return cached;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = num_sms() / 2;
+    }
+    cached = n;
+    return n;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi,
+               cudaStream_t s) {
+    using C = Cfg2<BN>;
+    static bool attr_set = false;
+    auto kern = gemm_tc2_kernel<BN, A_MN, B_MN>;
+    if (!attr_set) {
+        CG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_set = true;
+    }
+    CUtensorMap ta, tb;
+    if (A_MN) CG_TRY(make_map(&ta, A, M, K, lda, 32, BK, true));
+    else      CG_TRY(make_map(&ta, A, K, M, lda, BK, BM, false));
+    if (B_MN) CG_TRY(make_map(&tb, B, N, K, ldb, 32, BK, true));
+    else      CG_TRY(make_map(&tb, B, K, N, ldb, BK, C::BNH, false));
+    const int tiles_m = (M + 2 * BM - 1) / (2 * BM), tiles_n = (N + BN - 1) / BN;
+    const int tiles = tiles_m * tiles_n;
+    const int kblocks = (K + BK - 1) / BK;
+    const int slots = pair_slots(kern, C::THREADS, C::SMEM);
+    int ks = choose_ksplit(tiles, kblocks, M, N, K, false, slots * 2);
+    int kb_per = (kblocks + ks - 1) / ks;
+    ks = (kblocks + kb_per - 1) / kb_per;
+    float *ws = ks > 1 ? splitk_workspace((size_t)ks * M * N, s) : nullptr;
+    if (!ws) {
+        ks = 1;
+        kb_per = kblocks;
+    }
+    const int grid = 2 * std::min(tiles * ks, slots);
+    if (ks == 1) {
+        kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, 1, kb_per, 0L, epi);
+        ++g_launch_count;
+        CG_CUDA(cudaGetLastError());
+        return OK;
+    }
+    GemmEpi pe;
+    pe.mode = EPI_STORE;
+    pe.D = ws;
+    pe.ldd = N;
+    pe.vec4 = (N % 4) == 0;
+    const long stride = (long)M * N;
+    kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, ks, kb_per, stride, pe);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    const int rgrid = (int)std::min<long>((stride + 255) / 256, (long)num_sms() * 8);
+    splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(ws, ks, stride, M, N, epi);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
     return OK;
@@ -644,6 +1166,16 @@ template <bool A_MN, bool B_MN>
 int dispatch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, int K,
                 const GemmEpi &epi, cudaStream_t s, bool split) {
     if (split) return launch_tc<128, A_MN, B_MN, true>(A, lda, B, ldb, M, N, K, epi, s);
+    if (pair_gemm_enabled() && M > BM) {
+        // CTA pairs, 256 x 256 tiles unless their last wave leaves the pairs
+        // much emptier than 256 x 128 tiles would
+        const long pairs = num_sms() / 2, tm2 = (M + 2 * BM - 1) / (2 * BM);
+        const long t256 = tm2 * ((N + 255) / 256);
+        auto eff2 = [&](long t) { return (double)t / (double)(((t + pairs - 1) / pairs) * pairs); };
+        if (N > 128 && eff2(t256) >= 0.8)
+            return launch_tc2<256, A_MN, B_MN>(A, lda, B, ldb, M, N, K, epi, s);
+        return launch_tc2<128, A_MN, B_MN>(A, lda, B, ldb, M, N, K, epi, s);
+    }
     // 128 x 256 tiles halve the A traffic per FLOP; take them unless their
     // last wave leaves the machine much emptier than 128 x 128 tiles would
     const long sms = num_sms(), tm = (M + BM - 1) / BM;
@@ -660,6 +1192,15 @@ bool tma_ok(const float *p, long ld) {
 
 }  // namespace
 
+int gemm_ln(const float *X, long ldx, const float *ln_w, const float *ln_b, float *ln_out, const float *B,
+            long ldb, int M, int N, int K, const GemmEpi &epi, cudaStream_t s) {
+    auto al = [](const void *p) { return ((uintptr_t)p % 16) == 0; };
+    if (M > 0 && N > 0 && gemv_ok(X, ldx, false, B, ldb, false, M, K, epi) && al(ln_w) && al(ln_b))
+        return dispatch_gemv<true>(X, ldx, B, ldb, M, N, K, epi, ln_w, ln_b, s);
+    CG_TRY(layernorm_fwd(X, ldx, ln_w, ln_b, ln_out, K, nullptr, nullptr, M, K, s));
+    return gemm(ln_out, K, false, B, ldb, false, M, N, K, epi, s);
+}
+
 int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_mn, int M, int N,
          int K, const GemmEpi &epi, cudaStream_t s) {
     if (M < 0 || N < 0 || K < 0) {
@@ -675,15 +1216,17 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
                   (!epi.R || epi.ldr % 4 == 0) && (!epi.G || epi.ldg % 4 == 0);
     }
     const int prec = precision();
-    if (M <= 8 && !a_mn && !b_mn && K % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 &&
-        ((uintptr_t)A % 16) == 0 && ((uintptr_t)B % 16) == 0 && (long)N * K >= (1L << 16)) {
-        const int blocks = (N + 8 * GEMV_ROWS - 1) / (8 * GEMV_ROWS);
-        if (M <= 1) gemv_kernel<1><<<blocks, 256, 0, s>>>(A, lda, B, ldb, M, N, K, epi);
-        else if (M <= 4) gemv_kernel<4><<<blocks, 256, 0, s>>>(A, lda, B, ldb, M, N, K, epi);
-        else gemv_kernel<8><<<blocks, 256, 0, s>>>(A, lda, B, ldb, M, N, K, epi);
-        ++g_launch_count;
-        CG_CUDA(cudaGetLastError());
-        return OK;
+    if (gemv_ok(A, lda, a_mn, B, ldb, b_mn, M, K, epi) && ((long)N * K >= (1L << 16) || epi.kc))
+        return dispatch_gemv<false>(A, lda, B, ldb, M, N, K, epi, nullptr, nullptr, s);
+    if (epi.kc) {  // KV-cache columns: the GEMM, then the cache append
+        GemmEpi e3 = epi;
+        e3.kc = e3.vc = nullptr;
+        CG_TRY(gemm(A, lda, a_mn, B, ldb, b_mn, M, N, K, e3, s));
+        if (epi.mode != EPI_STORE || epi.ldd != 3L * epi.kv_C) {
+            set_last_error(ERR_ARG, "gemm: KV-cache epilogue needs STORE into packed qkv rows");
+            return ERR_ARG;
+        }
+        return kv_append_at(epi.D, epi.kc, epi.vc, M, epi.kv_ld / epi.kv_C, epi.kv_C, epi.kv_pos, s);
     }
     const bool big = (long)M * N * (long)std::max(K, 1) >= (1L << 18) && K > 0;
     const bool tc = prec != PREC_FP32 && big && tma_ok(A, lda) && tma_ok(B, ldb) &&

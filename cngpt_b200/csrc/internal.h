@@ -77,6 +77,13 @@ struct GemmEpi {
     const float *G = nullptr;
     long ldg = 0;
     int vec4 = 0;  // set by gemm(): every pointer 16B-aligned and every pitch % 4 == 0
+    // KV-cache decode (STORE mode, D = packed qkv rows): the K and V columns
+    // [kv_C, 3 kv_C) are also written to kc / vc at position *kv_pos:
+    // kc[m * kv_ld + pos * kv_C + (n - kv_C)], vc likewise for n >= 2 kv_C
+    float *kc = nullptr, *vc = nullptr;
+    long kv_ld = 0;
+    const int *kv_pos = nullptr;
+    int kv_C = 0;
 };
 
 // out[M,N] = op(A)[M,K] * op(B)[N,K]^T, with the epilogue applied per element.
@@ -84,6 +91,19 @@ struct GemmEpi {
 // B element (n,k) is B[n*ldb+k] (b_mn=false, K-major) or B[k*ldb+n] (b_mn=true).
 int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_mn,
          int M, int N, int K, const GemmEpi &epi, cudaStream_t s);
+
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialisation attribute may start before its predecessor finishes;
+// it must call pdl_wait() before reading anything the predecessor writes.
+// pdl_trigger() lets the dependent start launching (harmless without one).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// y = LayerNorm(X) (eps 1e-5, weights ln_w / ln_b) then the GEMM above with
+// A = y (K-major, M x K). For M <= 8 the normalisation is fused into the GEMV
+// (no y is written); otherwise y goes to ln_out [M, K] first.
+int gemm_ln(const float *X, long ldx, const float *ln_w, const float *ln_b, float *ln_out,
+            const float *B, long ldb, int M, int N, int K, const GemmEpi &epi, cudaStream_t s);
 
 // Counts of kernel launches issued by this library (for benchmarks).
 extern unsigned long long g_launch_count;

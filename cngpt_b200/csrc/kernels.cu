@@ -24,6 +24,7 @@ __global__ void layernorm_fwd_kernel(const float *__restrict__ x, long ldx,
                                      const float *__restrict__ w, const float *__restrict__ b,
                                      float *__restrict__ out, long ldo, float *__restrict__ mean,
                                      float *__restrict__ rstd, int T, int C) {
+    pdl_trigger();  // a GEMV launched after this may start prefetching its weights
     const int warps = blockDim.x >> 5;
     const int lane = threadIdx.x & 31;
     for (long t = (long)blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += (long)gridDim.x * warps) {

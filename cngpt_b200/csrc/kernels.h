@@ -71,11 +71,16 @@ int attention_fwd_rows(const float *qkv, float *out, int B, int T, int C, int H,
                        cudaStream_t s);
 // Single-query decode attention over a KV cache: q [B, C] (head h at h*hs),
 // kcache/vcache [B, Tmax, C], attends positions [0, len). out [B, C].
+// part: attention_decode_scratch_floats(B, H, Tmax) floats for the split-
+// context kernel (head size 64), zero-filled once after allocation (its tail
+// holds per-head tickets that every call leaves at zero); NULL selects the
+// one-block-per-head kernel.
+size_t attention_decode_scratch_floats(int B, int H, long Tmax);
 int attention_decode(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
-                     int len, float *out, int B, int C, int H, cudaStream_t s);
-// same, with the attended length (position + 1) read from a device counter;
-// shared memory is sized for the cache capacity Tmax
+                     int len, float *out, int B, int C, int H, float *part, cudaStream_t s);
+// same, with the attended length (position + 1) read from a device counter
 int attention_decode_at(const float *q, long ldq, const float *kcache, const float *vcache, long Tmax,
-                        const int *pos_dev, float *out, int B, int C, int H, cudaStream_t s);
+                        const int *pos_dev, float *out, int B, int C, int H, float *part,
+                        cudaStream_t s);
 
 }  // namespace cg

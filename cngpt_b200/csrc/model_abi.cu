@@ -658,6 +658,7 @@ extern "C" void gpt_free(GPT *m) {
     }
     cudaStreamSynchronize(g_stream);
     if (c && c->nccl_comm) cngpt_cuda_dp_free(m);
+    tp_release(m);
     dev_free(m->param_buf);
     dev_free(m->grad_buf);
     dev_free(m->m_buf);

@@ -47,6 +47,7 @@ struct FastDev {
     size_t tok_cap = 0;
     // KV cache for greedy decode: [L][B][Tmax][C] each
     float *kc = nullptr, *vc = nullptr;
+    float *dec_part = nullptr;  // split-context decode attention partials
     int kv_B = 0, kv_T = 0;
     int *next = nullptr;   // [B] argmax tokens (the next step's input)
     int *gen = nullptr;    // [n_new][B] generated tokens

@@ -1,0 +1,550 @@
+// tp_abi.cu - tensor-parallel GPT-2 inference, one process per GPU over NCCL.
+//
+// The reference runs inference on one CPU (src/fast.c:227-333, greedy
+// decoding as in src/model.c:991-1016); this splits the same forward across
+// ranks the Megatron way, with the rank's slices read straight out of the
+// reference's single parameter arena:
+//   QKV     column split by heads: rank r owns heads [h0, h0+nh) of q, k, v
+//           (packed once into a local [3*nh*hs, C] block, the only copy);
+//   c_proj  row split: columns [h0*hs, (h0+nh)*hs) of c_proj_w, read in place
+//           with leading dimension C;
+//   mlp_fc  column split: rows [f0, f0+nf) of mlp_fc_w, in place;
+//   mlp_proj row split: columns [f0, f0+nf) of mlp_proj_w, in place (ld 4C);
+//   LM head vocabulary split: rows [v0, v0+nv) of the tied wte, in place.
+// Each row-split projection writes its partial sum over the rank's slice into
+// the residual stream - rank 0 adds the bias and the old residual in its GEMM
+// epilogue, the others store the bare partial - and one sum-allreduce of the
+// [rows, C] stream then leaves x + proj(...) + b on every rank (two per
+// block). LayerNorms, embeddings and attention of the local heads run
+// replicated / locally. The greedy token is the max over ranks of each rank's
+// (max logit, lowest index) pair, gathered with one allgather; ties between
+// ranks go to the lower vocabulary index, as in the one-GPU argmax.
+#include <climits>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "abi_common.h"
+#include "kernels.h"
+#include "model_ctx.h"
+
+extern "C" {
+#include "cngpt_cuda.h"
+}
+
+namespace cg {
+namespace {
+
+struct TpPlan {
+    int h0 = 0, nh = 0;  // local heads
+    int f0 = 0, nf = 0;  // local MLP hidden columns
+    int v0 = 0, nv = 0;  // local vocabulary rows
+    int vpad = 0;        // vocabulary rows per rank before the ragged last one
+};
+
+int make_plan(int H, int C, int V, int world, int rank, TpPlan *p) {
+    if (H <= 0 || C <= 0 || V <= 0 || C % H != 0 || world < 1 || rank < 0 || rank >= world ||
+        world > H) {
+        set_last_error(ERR_ARG, "tp plan: n_head=%d n_embd=%d vocab=%d world=%d rank=%d", H, C, V, world,
+                       rank);
+        return ERR_ARG;
+    }
+    // heads: the first H % world ranks take one extra
+    const int hq = H / world, hr = H % world;
+    p->nh = hq + (rank < hr ? 1 : 0);
+    p->h0 = rank * hq + (rank < hr ? rank : hr);
+    // MLP hidden width 4C in units of 4 columns (16-byte aligned slices)
+    const int units = C, uq = units / world, ur = units % world;
+    p->nf = 4 * (uq + (rank < ur ? 1 : 0));
+    p->f0 = 4 * (rank * uq + (rank < ur ? rank : ur));
+    // vocabulary: equal blocks of ceil(V / world), the last one ragged
+    p->vpad = (V + world - 1) / world;
+    p->v0 = rank * p->vpad;
+    p->nv = std::min(p->vpad, V - p->v0);
+    if (p->nv <= 0) {
+        set_last_error(ERR_ARG, "tp plan: vocab %d too small for world %d", V, world);
+        return ERR_ARG;
+    }
+    return OK;
+}
+
+struct TpState {
+    int world = 1, rank = 0;
+    void *comm = nullptr;
+    TpPlan p;
+    int L = 0, C = 0, V = 0, H = 0, hs = 0, Cl = 0;
+    long ldlog = 0;
+    float *wbuf = nullptr;  // packed QKV weights [L][3Cl][C] then biases [L][3Cl]
+    // activations, sized for (B, T)
+    int B = 0, T = 0;
+    float *x = nullptr, *ln = nullptr, *qkv = nullptr, *aout = nullptr, *hid = nullptr;
+    float *mean = nullptr, *rstd = nullptr, *xl = nullptr, *al = nullptr, *logits = nullptr;
+    int *pairs = nullptr, *gath = nullptr;  // [2B] local (value bits, index); [world][2B]
+    float *lgath = nullptr;                 // [world][B][ldlog] full-logit gather
+    int *tok = nullptr;
+    size_t tok_cap = 0;
+    // KV cache of the local heads [L][B][Tmax][Cl]
+    float *kc = nullptr, *vc = nullptr, *dec_part = nullptr;
+    int kv_B = 0, kv_T = 0;
+    int *next = nullptr, *gen = nullptr, *ctr = nullptr;
+    size_t gen_cap = 0;
+    cudaStream_t cap_stream = nullptr;
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    int graph_B = 0, graph_T = 0, graph_prec = -1;
+
+    const float *qkv_w(int l) const { return wbuf + (size_t)l * 3 * Cl * C; }
+    const float *qkv_b(int l) const { return wbuf + (size_t)L * 3 * Cl * C + (size_t)l * 3 * Cl; }
+};
+
+std::mutex g_tp_mu;
+std::map<const GPT *, TpState *> g_tp;
+
+TpState *tp_state(const GPT *m) {
+    std::lock_guard<std::mutex> lk(g_tp_mu);
+    auto it = g_tp.find(m);
+    if (it == g_tp.end()) {
+        set_last_error(ERR_STATE, "tensor parallelism not initialised for this model (tp_init)");
+        return nullptr;
+    }
+    return it->second;
+}
+
+// greedy token over ranks: gath holds, per rank r, [B] max values (as bits)
+// then [B] local indices; global index = local + r * vpad
+__global__ void tp_argmax_merge_kernel(const int *__restrict__ gath, int B, int world, int vpad,
+                                       int *__restrict__ next, int *__restrict__ log,
+                                       const int *__restrict__ step_dev) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    float best = -INFINITY;
+    int bi = INT_MAX;
+    for (int r = 0; r < world; ++r) {
+        const int *g = gath + (size_t)r * 2 * B;
+        const float v = __int_as_float(g[b]);
+        const int i = g[B + b] + r * vpad;
+        if (v > best || (v == best && i < bi)) {
+            best = v;
+            bi = i;
+        }
+    }
+    next[b] = bi;
+    if (log) log[(size_t)(*step_dev) * B + b] = bi;
+}
+
+void drop_graph(TpState *t) {
+    if (t->graph) cudaGraphExecDestroy(t->graph);
+    t->graph = nullptr;
+}
+
+int allreduce(TpState *t, float *buf, size_t n, cudaStream_t s) {
+    if (t->world == 1) return OK;
+    return nccl_allreduce_sum(buf, n, t->comm, s);
+}
+
+GemmEpi epi_store(float *D, long ldd, const float *bias) {
+    GemmEpi e;
+    e.mode = EPI_STORE;
+    e.D = D;
+    e.ldd = ldd;
+    e.bias = bias;
+    return e;
+}
+
+// rank 0: x = x + acc + bias; other ranks: x = acc (their partial sums)
+GemmEpi epi_partial(const TpState *t, float *x, long ld, const float *bias) {
+    GemmEpi e;
+    if (t->rank == 0) {
+        e.mode = EPI_RESID;
+        e.bias = bias;
+        e.D2 = x;
+        e.ldd2 = ld;
+        e.R = x;
+        e.ldr = ld;
+    } else {
+        e.mode = EPI_STORE;
+        e.D = x;
+        e.ldd = ld;
+    }
+    return e;
+}
+
+int resize(TpState *t, int B, int T) {
+    if (t->x && t->B == B && t->T == T) return OK;
+    cudaStreamSynchronize(g_stream);
+    if (t->cap_stream) cudaStreamSynchronize(t->cap_stream);
+    drop_graph(t);
+    float **bufs[] = {&t->x, &t->ln, &t->qkv, &t->aout, &t->hid, &t->mean, &t->rstd, &t->xl, &t->al,
+                      &t->logits, &t->lgath};
+    for (auto b : bufs) {
+        dev_free(*b);
+        *b = nullptr;
+    }
+    dev_free(t->pairs);
+    dev_free(t->gath);
+    t->pairs = t->gath = nullptr;
+    const size_t N = (size_t)B * T, C = t->C, Cl = t->Cl, W = t->world;
+    CG_TRY(dev_alloc((void **)&t->x, N * C * 4, false));
+    CG_TRY(dev_alloc((void **)&t->ln, N * C * 4, false));
+    CG_TRY(dev_alloc((void **)&t->qkv, N * 3 * Cl * 4, false));
+    CG_TRY(dev_alloc((void **)&t->aout, N * Cl * 4, false));
+    CG_TRY(dev_alloc((void **)&t->hid, N * t->p.nf * 4, false));
+    CG_TRY(dev_alloc((void **)&t->mean, N * 4, false));
+    CG_TRY(dev_alloc((void **)&t->rstd, N * 4, false));
+    CG_TRY(dev_alloc((void **)&t->xl, (size_t)B * C * 4, false));
+    CG_TRY(dev_alloc((void **)&t->al, (size_t)B * Cl * 4, false));
+    CG_TRY(dev_alloc((void **)&t->logits, (size_t)B * t->ldlog * 4, false));
+    CG_TRY(dev_alloc((void **)&t->lgath, W * B * t->ldlog * 4, false));
+    CG_TRY(dev_alloc((void **)&t->pairs, (size_t)2 * B * 4, false));
+    CG_TRY(dev_alloc((void **)&t->gath, W * 2 * B * 4, false));
+    t->B = B;
+    t->T = T;
+    return OK;
+}
+
+// post-attention part of block l for `rows` rows of x (aout: local heads)
+int block_tail(const GPT *m, TpState *t, int l, float *x, const float *aout, int rows, cudaStream_t s) {
+    const GPTWeights *w = &m->params;
+    const int C = t->C, Cl = t->Cl, nf = t->p.nf;
+    CG_TRY(gemm(aout, Cl, false, w->c_proj_w[l] + (size_t)t->p.h0 * t->hs, C, false, rows, C, Cl,
+                epi_partial(t, x, C, w->c_proj_b[l]), s));
+    CG_TRY(allreduce(t, x, (size_t)rows * C, s));
+    CG_TRY(layernorm_fwd(x, C, w->ln2_w[l], w->ln2_b[l], t->ln, C, t->mean, t->rstd, rows, C, s));
+    GemmEpi g;
+    g.mode = EPI_GELU;
+    g.bias = w->mlp_fc_b[l] + t->p.f0;
+    g.D2 = t->hid;
+    g.ldd2 = nf;
+    CG_TRY(gemm(t->ln, C, false, w->mlp_fc_w[l] + (size_t)t->p.f0 * C, C, false, rows, nf, C, g, s));
+    CG_TRY(gemm(t->hid, nf, false, w->mlp_proj_w[l] + t->p.f0, 4L * C, false, rows, C, nf,
+                epi_partial(t, x, C, w->mlp_proj_b[l]), s));
+    return allreduce(t, x, (size_t)rows * C, s);
+}
+
+// local logits of the final rows xl [B, C] -> t->logits [B, ldlog]
+int lm_head(const GPT *m, TpState *t, int B, cudaStream_t s) {
+    const GPTWeights *w = &m->params;
+    const int C = t->C;
+    CG_TRY(layernorm_fwd(t->xl, C, w->ln_f_w, w->ln_f_b, t->ln, C, t->mean, t->rstd, B, C, s));
+    return gemm(t->ln, C, false, w->wte + (size_t)t->p.v0 * C, C, false, B, t->p.nv, C,
+                epi_store(t->logits, t->ldlog, nullptr), s);
+}
+
+// greedy token of the local logits, merged over ranks -> t->next, t->gen[step]
+int greedy(TpState *t, int B, cudaStream_t s) {
+    CG_TRY(argmax_rows(t->logits, t->ldlog, B, t->p.nv, t->pairs + B, (float *)t->pairs, s));
+    const int *g = t->pairs;
+    if (t->world > 1) {
+        CG_TRY(nccl_allgather_words(t->pairs, t->gath, (size_t)2 * B, t->comm, s));
+        g = t->gath;
+    }
+    tp_argmax_merge_kernel<<<(B + 127) / 128, 128, 0, s>>>(g, B, t->world, t->p.vpad, t->next, t->gen,
+                                                           t->ctr + 1);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    return OK;
+}
+
+// full-prefix forward over (B, T); stores K/V of the local heads when kv
+int prefill(const GPT *m, TpState *t, const int *tok, int B, int T, bool kv, cudaStream_t s) {
+    const GPTWeights *w = &m->params;
+    const int C = t->C, Cl = t->Cl, BT = B * T;
+    CG_TRY(embed_fwd(tok, w->wte, w->wpe, t->x, BT, T, C, 0, s));
+    const size_t per = (size_t)t->kv_B * t->kv_T * Cl;
+    for (int l = 0; l < t->L; ++l) {
+        CG_TRY(layernorm_fwd(t->x, C, w->ln1_w[l], w->ln1_b[l], t->ln, C, t->mean, t->rstd, BT, C, s));
+        CG_TRY(gemm(t->ln, C, false, t->qkv_w(l), C, false, BT, 3 * Cl, C,
+                    epi_store(t->qkv, 3 * Cl, t->qkv_b(l)), s));
+        if (kv) CG_TRY(kv_append(t->qkv, t->kc + l * per, t->vc + l * per, B, T, t->kv_T, 0, Cl, s));
+        if (l < t->L - 1) {
+            CG_TRY(attention_fwd(t->qkv, t->aout, nullptr, B, T, Cl, t->p.nh, s));
+            CG_TRY(block_tail(m, t, l, t->x, t->aout, BT, s));
+        } else {
+            CG_TRY(attention_fwd_rows(t->qkv, t->aout, B, T, Cl, t->p.nh, T - 1, s));
+            CG_TRY(gather_last(t->aout, t->al, B, T, Cl, s));
+            CG_TRY(gather_last(t->x, t->xl, B, T, C, s));
+            CG_TRY(block_tail(m, t, l, t->xl, t->al, B, s));
+        }
+    }
+    if (t->L == 0) CG_TRY(gather_last(t->x, t->xl, B, T, C, s));
+    return lm_head(m, t, B, s);
+}
+
+// one decode step: tokens t->next at position ctr[0] (see fast_abi.cu); the
+// LayerNorms are fused into the GEMVs that consume them and the qkv GEMV's
+// epilogue appends K and V to the cache
+int decode_step(const GPT *m, TpState *t, int B, cudaStream_t s) {
+    const GPTWeights *w = &m->params;
+    const int C = t->C, Cl = t->Cl, nf = t->p.nf;
+    float *x = t->xl;
+    CG_TRY(embed_fwd_at(t->next, w->wte, w->wpe, x, B, C, t->ctr, s));
+    const size_t per = (size_t)t->kv_B * t->kv_T * Cl;
+    for (int l = 0; l < t->L; ++l) {
+        GemmEpi eq = epi_store(t->qkv, 3 * Cl, t->qkv_b(l));
+        eq.kc = t->kc + l * per;
+        eq.vc = t->vc + l * per;
+        eq.kv_ld = (long)t->kv_T * Cl;
+        eq.kv_pos = t->ctr;
+        eq.kv_C = Cl;
+        CG_TRY(gemm_ln(x, C, w->ln1_w[l], w->ln1_b[l], t->ln, t->qkv_w(l), C, B, 3 * Cl, C, eq, s));
+        CG_TRY(attention_decode_at(t->qkv, 3L * Cl, t->kc + l * per, t->vc + l * per, t->kv_T, t->ctr,
+                                   t->al, B, Cl, t->p.nh, t->dec_part, s));
+        CG_TRY(gemm(t->al, Cl, false, w->c_proj_w[l] + (size_t)t->p.h0 * t->hs, C, false, B, C, Cl,
+                    epi_partial(t, x, C, w->c_proj_b[l]), s));
+        CG_TRY(allreduce(t, x, (size_t)B * C, s));
+        GemmEpi g;
+        g.mode = EPI_GELU;
+        g.bias = w->mlp_fc_b[l] + t->p.f0;
+        g.D2 = t->hid;
+        g.ldd2 = nf;
+        CG_TRY(gemm_ln(x, C, w->ln2_w[l], w->ln2_b[l], t->ln, w->mlp_fc_w[l] + (size_t)t->p.f0 * C, C, B, nf,
+                       C, g, s));
+        CG_TRY(gemm(t->hid, nf, false, w->mlp_proj_w[l] + t->p.f0, 4L * C, false, B, C, nf,
+                    epi_partial(t, x, C, w->mlp_proj_b[l]), s));
+        CG_TRY(allreduce(t, x, (size_t)B * C, s));
+    }
+    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, t->ln, w->wte + (size_t)t->p.v0 * C, C, B, t->p.nv, C,
+                   epi_store(t->logits, t->ldlog, nullptr), s));
+    CG_TRY(greedy(t, B, s));
+    return decode_advance(t->ctr, s);
+}
+
+int capture_step(const GPT *m, TpState *t, int B) {
+    if (t->graph && t->graph_B == B && t->graph_T == t->kv_T && t->graph_prec == precision()) return OK;
+    drop_graph(t);
+    cudaGraph_t g = nullptr;
+    CG_CUDA(cudaStreamBeginCapture(t->cap_stream, cudaStreamCaptureModeThreadLocal));
+    const int st = decode_step(m, t, B, t->cap_stream);
+    const cudaError_t e = cudaStreamEndCapture(t->cap_stream, &g);
+    if (st != OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (e != cudaSuccess) {
+        set_last_error(ERR_CUDA, "tp decode graph capture: %s", cudaGetErrorString(e));
+        return ERR_CUDA;
+    }
+    const cudaError_t ei = cudaGraphInstantiate(&t->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) {
+        t->graph = nullptr;
+        set_last_error(ERR_CUDA, "tp decode graph instantiate: %s", cudaGetErrorString(ei));
+        return ERR_CUDA;
+    }
+    t->graph_B = B;
+    t->graph_T = t->kv_T;
+    t->graph_prec = precision();
+    return OK;
+}
+
+void release(TpState *t) {
+    cudaStreamSynchronize(g_stream);
+    if (t->cap_stream) cudaStreamSynchronize(t->cap_stream);
+    drop_graph(t);  // before the communicator its NCCL nodes use
+    float *bufs[] = {t->wbuf, t->x,  t->ln,     t->qkv, t->aout, t->hid, t->mean, t->rstd,
+                     t->xl,   t->al, t->logits, t->lgath, t->kc,  t->vc, t->dec_part};
+    for (auto b : bufs) dev_free(b);
+    int *ibufs[] = {t->pairs, t->gath, t->tok, t->next, t->gen, t->ctr};
+    for (auto b : ibufs) dev_free(b);
+    if (t->ev_a) cudaEventDestroy(t->ev_a);
+    if (t->ev_b) cudaEventDestroy(t->ev_b);
+    if (t->cap_stream) cudaStreamDestroy(t->cap_stream);
+    nccl_comm_destroy(t->comm);
+    delete t;
+}
+
+}  // namespace
+
+void tp_release(const GPT *m) {
+    TpState *t = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_tp_mu);
+        auto it = g_tp.find(m);
+        if (it == g_tp.end()) return;
+        t = it->second;
+        g_tp.erase(it);
+    }
+    release(t);
+}
+
+}  // namespace cg
+
+using namespace cg;
+
+extern "C" int cngpt_cuda_tp_plan(int n_head, int n_embd, int vocab, int world, int rank, int plan[7]) {
+    TpPlan p;
+    CG_TRY(make_plan(n_head, n_embd, vocab, world, rank, &p));
+    const int v[7] = {p.h0, p.nh, p.f0, p.nf, p.v0, p.nv, p.vpad};
+    memcpy(plan, v, sizeof(v));
+    return OK;
+}
+
+extern "C" int cngpt_cuda_tp_init(GPT *m, const unsigned char id[128], int world, int rank) {
+    ModelCtx *c = model_ctx(m);
+    if (!c) return ERR_STATE;
+    tp_release(m);
+    TpPlan p;
+    const GPTConfig &cfg = m->cfg;
+    CG_TRY(make_plan(cfg.n_head, cfg.n_embd, cfg.vocab_size, world, rank, &p));
+    TpState *t = new TpState;
+    t->world = world;
+    t->rank = rank;
+    t->p = p;
+    t->L = cfg.n_layer;
+    t->C = cfg.n_embd;
+    t->V = cfg.vocab_size;
+    t->H = cfg.n_head;
+    t->hs = t->C / t->H;
+    t->Cl = p.nh * t->hs;
+    t->ldlog = (p.vpad + 3) & ~3L;
+    auto fail = [&](int st) {
+        release(t);
+        return st;
+    };
+    if (world > 1) {
+        const int st = nccl_comm_init(&t->comm, id, world, rank);
+        if (st != OK) return fail(st);
+    }
+    // pack this rank's q, k and v rows (and biases) of every layer
+    const size_t C = t->C, Cl = t->Cl, L = t->L, off = (size_t)p.h0 * t->hs;
+    int st = dev_alloc((void **)&t->wbuf, (L * 3 * Cl * C + L * 3 * Cl) * 4, false);
+    if (st != OK) return fail(st);
+    for (size_t l = 0; l < L; ++l) {
+        float *dw = t->wbuf + l * 3 * Cl * C;
+        float *db = t->wbuf + L * 3 * Cl * C + l * 3 * Cl;
+        for (size_t part = 0; part < 3; ++part) {
+            const float *sw = m->params.c_attn_w[l] + (part * C + off) * C;
+            const float *sb = m->params.c_attn_b[l] + part * C + off;
+            if (cudaMemcpyAsync(dw + part * Cl * C, sw, Cl * C * 4, cudaMemcpyDeviceToDevice, g_stream) !=
+                    cudaSuccess ||
+                cudaMemcpyAsync(db + part * Cl, sb, Cl * 4, cudaMemcpyDeviceToDevice, g_stream) !=
+                    cudaSuccess) {
+                set_last_error(ERR_CUDA, "tp_init: packing the qkv slices failed");
+                return fail(ERR_CUDA);
+            }
+        }
+    }
+    if (cudaStreamCreateWithFlags(&t->cap_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t->ev_a, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t->ev_b, cudaEventDisableTiming) != cudaSuccess) {
+        set_last_error(ERR_CUDA, "tp_init: stream / event creation failed");
+        return fail(ERR_CUDA);
+    }
+    st = dev_alloc((void **)&t->ctr, 2 * sizeof(int), false);
+    if (st != OK) return fail(st);
+    if (cudaStreamSynchronize(g_stream) != cudaSuccess) {
+        set_last_error(ERR_CUDA, "tp_init: %s", cudaGetErrorString(cudaGetLastError()));
+        return fail(ERR_CUDA);
+    }
+    std::lock_guard<std::mutex> lk(g_tp_mu);
+    g_tp[m] = t;
+    return OK;
+}
+
+extern "C" int cngpt_cuda_tp_forward_last(GPT *m, const int *tokens, int B, int T, float *logits_out) {
+    TpState *t = tp_state(m);
+    if (!t) return ERR_STATE;
+    if (B <= 0 || T <= 0 || T > m->cfg.block_size) {
+        set_last_error(ERR_ARG, "tp_forward_last: bad shape B=%d T=%d", B, T);
+        return ERR_ARG;
+    }
+    cudaStream_t s = g_stream;
+    CG_TRY(resize(t, B, T));
+    const int *tok = nullptr;
+    CG_TRY(stage_tokens(tokens, (size_t)B * T, &t->tok, &t->tok_cap, &tok, s));
+    CG_TRY(prefill(m, t, tok, B, T, false, s));
+    if (!logits_out) {
+        CG_CUDA(cudaStreamSynchronize(s));
+        return check_device_error();
+    }
+    const float *g = t->logits;
+    if (t->world > 1) {
+        CG_TRY(nccl_allgather_words(t->logits, t->lgath, (size_t)B * t->ldlog, t->comm, s));
+        g = t->lgath;
+    }
+    std::vector<float> h((size_t)t->world * B * t->ldlog);
+    CG_CUDA(cudaMemcpyAsync(h.data(), g, h.size() * 4, cudaMemcpyDeviceToHost, s));
+    CG_CUDA(cudaStreamSynchronize(s));
+    CG_TRY(check_device_error());
+    for (int r = 0; r < t->world; ++r) {
+        const int v0 = r * t->p.vpad, nv = std::min(t->p.vpad, t->V - v0);
+        for (int b = 0; b < B; ++b)
+            memcpy(logits_out + (size_t)b * t->V + v0, h.data() + ((size_t)r * B + b) * t->ldlog,
+                   (size_t)nv * 4);
+    }
+    return OK;
+}
+
+extern "C" int cngpt_cuda_tp_generate(GPT *m, const int *prompt, int B, int T, int n_new, int *out_tokens) {
+    TpState *t = tp_state(m);
+    if (!t) return ERR_STATE;
+    if (B <= 0 || T <= 0 || n_new <= 0 || T + n_new - 1 > m->cfg.block_size) {
+        set_last_error(ERR_ARG, "tp_generate: B=%d T=%d n_new=%d exceeds block_size %d", B, T, n_new,
+                       m->cfg.block_size);
+        return ERR_ARG;
+    }
+    cudaStream_t s = g_stream;
+    CG_TRY(resize(t, B, T));
+    const int Tmax = T + n_new;
+    const size_t Cl = t->Cl, L = t->L;
+    if (t->kv_B != B || t->kv_T < Tmax) {
+        CG_CUDA(cudaStreamSynchronize(s));
+        CG_CUDA(cudaStreamSynchronize(t->cap_stream));
+        drop_graph(t);
+        dev_free(t->kc);
+        dev_free(t->vc);
+        dev_free(t->next);
+        dev_free(t->dec_part);
+        t->kc = t->vc = t->dec_part = nullptr;
+        t->next = nullptr;
+        CG_TRY(dev_alloc((void **)&t->kc, L * B * Tmax * Cl * 4, false));
+        CG_TRY(dev_alloc((void **)&t->vc, L * B * Tmax * Cl * 4, false));
+        CG_TRY(dev_alloc((void **)&t->dec_part, attention_decode_scratch_floats(B, t->p.nh, Tmax) * 4, false));
+        CG_CUDA(cudaMemsetAsync(t->dec_part, 0, attention_decode_scratch_floats(B, t->p.nh, Tmax) * 4, s));
+        CG_TRY(dev_alloc((void **)&t->next, (size_t)B * 4, false));
+        t->kv_B = B;
+        t->kv_T = Tmax;
+    }
+    if ((size_t)B * n_new > t->gen_cap) {
+        CG_CUDA(cudaStreamSynchronize(s));
+        CG_CUDA(cudaStreamSynchronize(t->cap_stream));
+        drop_graph(t);
+        dev_free(t->gen);
+        t->gen = nullptr;
+        CG_TRY(dev_alloc((void **)&t->gen, (size_t)B * n_new * 4, false));
+        t->gen_cap = (size_t)B * n_new;
+    }
+    const int *tok = nullptr;
+    CG_TRY(stage_tokens(prompt, (size_t)B * T, &t->tok, &t->tok_cap, &tok, s));
+    const int ctr0[2] = {T - 1, 0};
+    CG_CUDA(cudaMemcpyAsync(t->ctr, ctr0, sizeof(ctr0), cudaMemcpyHostToDevice, s));
+    CG_TRY(prefill(m, t, tok, B, T, true, s));
+    CG_TRY(greedy(t, B, s));
+    CG_TRY(decode_advance(t->ctr, s));
+    if (n_new > 1) {
+        CG_CUDA(cudaEventRecord(t->ev_a, s));
+        CG_CUDA(cudaStreamWaitEvent(t->cap_stream, t->ev_a, 0));
+        CG_TRY(decode_step(m, t, B, t->cap_stream));
+        if (n_new > 2) {
+            CG_TRY(capture_step(m, t, B));
+            for (int i = 2; i < n_new; ++i) CG_CUDA(cudaGraphLaunch(t->graph, t->cap_stream));
+        }
+        CG_CUDA(cudaEventRecord(t->ev_b, t->cap_stream));
+        CG_CUDA(cudaStreamWaitEvent(s, t->ev_b, 0));
+    }
+    std::vector<int> h((size_t)B * n_new);
+    CG_CUDA(cudaMemcpyAsync(h.data(), t->gen, h.size() * 4, cudaMemcpyDeviceToHost, s));
+    CG_CUDA(cudaStreamSynchronize(s));
+    CG_TRY(check_device_error());
+    for (int b = 0; b < B; ++b)
+        for (int i = 0; i < n_new; ++i) out_tokens[(size_t)b * n_new + i] = h[(size_t)i * B + b];
+    return OK;
+}
+
+extern "C" int cngpt_cuda_tp_free(GPT *m) {
+    if (!model_ctx(m)) return ERR_STATE;
+    tp_release(m);
+    return OK;
+}

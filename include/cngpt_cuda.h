@@ -133,6 +133,27 @@ int cngpt_cuda_dp_init(GPT *m, const unsigned char id[128], int world, int rank)
 int cngpt_cuda_dp_allreduce_grads(GPT *m);
 int cngpt_cuda_dp_free(GPT *m);
 
+/* ---- tensor-parallel inference over NCCL -----------------------------------
+ * The reference runs src/fast.c:227-333 on one CPU; these split the same
+ * forward over `world` processes, one GPU each, in the Megatron way: QKV by
+ * heads (the first n_head % world ranks take one head more), c_proj by the
+ * matching input columns, mlp_fc / mlp_proj by 4-column units of the hidden
+ * width, the LM head by blocks of ceil(vocab / world) rows of the tied wte.
+ * Every rank holds the full model (same weights on every rank: initialise
+ * them from the same seed, or load the same file) and gets the id from
+ * cngpt_cuda_dp_unique_id on rank 0. Each block ends in two sum-allreduces of
+ * the [rows, n_embd] residual stream; the greedy token is merged from every
+ * rank's (max, lowest index) pair. All ranks make the same calls in order.
+ * plan (host only, no GPU): h0, nh, f0, nf, v0, nv, vpad of `rank`. */
+int cngpt_cuda_tp_plan(int n_head, int n_embd, int vocab, int world, int rank, int plan[7]);
+int cngpt_cuda_tp_init(GPT *m, const unsigned char id[128], int world, int rank);
+/* final-position logits of every sequence, gathered: host float[B * vocab]
+ * (may be NULL to skip the gather) - what gpt_forward_fast returns */
+int cngpt_cuda_tp_forward_last(GPT *m, const int *tokens, int B, int T, float *logits_out);
+/* cngpt_cuda_generate split over the ranks; out_tokens (host) on every rank */
+int cngpt_cuda_tp_generate(GPT *m, const int *prompt, int B, int T, int n_new, int *out_tokens);
+int cngpt_cuda_tp_free(GPT *m);
+
 #ifdef __cplusplus
 }
 #endif

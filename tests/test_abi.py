@@ -115,3 +115,36 @@ def test_num_params_formula():
                    ((48, 25, 1600, 50257, 1024), 1557611200), ((6, 6, 384, 65, 256), 10770816)]:
         c = abi.GPTConfig(*cfg, 0.0)
         assert lib.gpt_num_params(C.byref(c)) == n
+
+
+@pytest.mark.parametrize("H,Cemb,V", [(25, 1600, 50257), (12, 768, 50257), (5, 320, 1001), (3, 96, 77)])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_tp_plan_partitions_heads_hidden_and_vocab(H, Cemb, V, world):
+    """cngpt_cuda_tp_plan is host-only: the ranks' slices tile every split
+    dimension exactly once, in rank order, 16-byte aligned where read in place."""
+    lib = abi.load()
+    plans = []
+    for rank in range(world):
+        p = (C.c_int * 7)()
+        st = lib.cngpt_cuda_tp_plan(H, Cemb, V, world, rank, p)
+        if world > H:
+            assert st == abi.ERR_ARG
+            lib.cngpt_cuda_clear_status()
+            return
+        assert st == abi.OK
+        plans.append(list(p))
+    h = f = v = 0
+    for h0, nh, f0, nf, v0, nv, vpad in plans:
+        assert (h0, f0, v0) == (h, f, v) and nh >= 1 and nf > 0 and nv > 0
+        assert f0 % 4 == 0 and nf % 4 == 0 and vpad == -(-V // world)
+        h, f, v = h + nh, f + nf, v + nv
+    assert (h, f, v) == (H, 4 * Cemb, V)
+    assert max(p[1] for p in plans) - min(p[1] for p in plans) <= 1
+
+
+def test_tp_plan_rejects_bad_rank():
+    lib = abi.load()
+    p = (C.c_int * 7)()
+    assert lib.cngpt_cuda_tp_plan(12, 768, 50257, 2, 2, p) == abi.ERR_ARG
+    assert lib.cngpt_cuda_tp_plan(12, 770, 50257, 2, 0, p) == abi.ERR_ARG
+    lib.cngpt_cuda_clear_status()

@@ -68,6 +68,8 @@ def prec(request, lib):
 # (M, N, K) - GPT-2 small call sites with M reduced, LM-head ragged N, odd K
 SHAPES = [(256, 2304, 768), (256, 768, 3072), (384, 50257, 64), (300, 200, 100), (128, 128, 32),
           (1000, 520, 72), (64, 3072, 768)]
+# few output tiles over a long K: split into K ranges, partials summed in order
+SPLITK = [(256, 384, 4096), (768, 768, 8192), (130, 200, 2080)]
 # decode-shaped rows (M <= 8 takes the GEMV kernel when A and B are K-major)
 SKINNY = [(1, 2304, 768), (5, 768, 3072), (8, 50257, 768), (3, 3072, 768)]
 
@@ -124,6 +126,23 @@ def test_gemm_skinny_rows(lib, cuda, prec, M, N, K, mode):
         assert nwerr(r["D"], ref * gp) < max(TOL[prec], 1e-5)
     else:
         assert nwerr(r["D"], ref) < TOL[prec]
+
+
+@pytest.mark.parametrize("M,N,K", SPLITK)
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True)], ids=["NT", "TN"])
+@pytest.mark.parametrize("mode", [abi.EPI_STORE, abi.EPI_ACCUM, abi.EPI_RESID])
+def test_gemm_split_k(lib, cuda, prec, M, N, K, a_mn, b_mn, mode):
+    r = run_gemm(lib, cuda, M, N, K, a_mn, b_mn, mode=mode, bias=True, alpha=0.5, seed=K)
+    ref = r["ref"]
+    assert nwerr(r["D"], ref) < TOL[prec]
+    if mode == abi.EPI_RESID:
+        assert nwerr(r["D2"], r["R"] + ref) < TOL[prec]
+
+
+def test_gemm_split_k_deterministic(lib, cuda, prec):
+    a = run_gemm(lib, cuda, 768, 768, 8192, True, True, seed=5)["D"]
+    b = run_gemm(lib, cuda, 768, 768, 8192, True, True, seed=5)["D"]
+    assert np.array_equal(a, b)
 
 
 def test_gemm_alpha_and_pitch(lib, cuda, prec):
