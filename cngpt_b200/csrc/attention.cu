@@ -716,8 +716,7 @@ attn_decode_split_kernel(const float *__restrict__ q, long ldq, const float *__r
     const int bh = blockIdx.x, split = blockIdx.y, b = bh / H, h = bh % H;
     const int j0 = split * DEC_KEYS;
     if (j0 >= len) return;  // uniform over the block: an empty chunk takes no ticket
-    float *pp = part + ((long)bh * S + split) * DEC_PART;
-    __shared__ float sc[DEC_KEYS], pr[DEC_KEYS], so[64], red[2];
+    __shared__ float sc[DEC_KEYS], pr[DEC_KEYS], so[64], red[2], cm[64], cl[64];
     __shared__ int last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, half = lane >> 4, l16 = lane & 15;
     const float4 qv = *(const float4 *)(q + (long)b * ldq + h * 64 + 4 * l16);
@@ -730,6 +729,14 @@ attn_decode_split_kernel(const float *__restrict__ q, long ldq, const float *__r
         if (j < len) kv = *(const float4 *)(kb + (long)j * C);
         d[i] = qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
     }
+    // V of this thread's 32 keys (thread (kh, dim): keys kh*32.., one
+    // dimension), loaded while the scores are reduced
+    const int dim = threadIdx.x & 63, kh = threadIdx.x >> 6;
+    const int kend = min(DEC_KEYS, len - j0);
+    const float *vb = vc + (long)b * Tmax * C + h * 64 + dim + (long)j0 * C;
+    float vr[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) vr[i] = (kh * 32 + i < kend) ? vb[(long)(kh * 32 + i) * C] : 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -756,16 +763,12 @@ attn_decode_split_kernel(const float *__restrict__ q, long ldq, const float *__r
         if (lane == 0) red[warp] = w;
     }
     __syncthreads();
-    // P V: thread (kh, dim) sums keys kh*32 .. kh*32+31 of its dim
-    const int dim = threadIdx.x & 63, kh = threadIdx.x >> 6;
-    const float *vb = vc + (long)b * Tmax * C + h * 64 + dim;
-    const int kend = min(DEC_KEYS, len - j0);
     float acc = 0.f;
-#pragma unroll 8
-    for (int k = kh * 32; k < kh * 32 + 32; ++k)
-        if (k < kend) acc += pr[k] * vb[(long)(j0 + k) * C];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc += pr[kh * 32 + i] * vr[i];
     if (kh == 1) so[dim] = acc;
     __syncthreads();
+    float *pp = part + ((long)bh * S + split) * DEC_PART;
     if (kh == 0) {
         pp[2 + dim] = acc + so[dim];
         if (dim == 0) {
@@ -780,14 +783,22 @@ attn_decode_split_kernel(const float *__restrict__ q, long ldq, const float *__r
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // merge the chunks in chunk order: (max, sum) of every chunk first, then
+    // each dimension's partial outputs (independent loads)
+    const float *pb = part + (long)bh * S * DEC_PART;
+    if ((int)threadIdx.x < ns) {
+        cm[threadIdx.x] = __ldcg(pb + threadIdx.x * DEC_PART);
+        cl[threadIdx.x] = __ldcg(pb + threadIdx.x * DEC_PART + 1);
+    }
+    __syncthreads();
     if (threadIdx.x < 64) {
-        const float *pb = part + (long)bh * S * DEC_PART;
         float M = -INFINITY;
-        for (int k = 0; k < ns; ++k) M = fmaxf(M, __ldcg(pb + k * DEC_PART));
+        for (int k = 0; k < ns; ++k) M = fmaxf(M, cm[k]);
         float L = 0.f, O = 0.f;
+#pragma unroll 4
         for (int k = 0; k < ns; ++k) {
-            const float w = expf(__ldcg(pb + k * DEC_PART) - M);
-            L += __ldcg(pb + k * DEC_PART + 1) * w;
+            const float w = expf(cm[k] - M);
+            L += cl[k] * w;
             O += __ldcg(pb + k * DEC_PART + 2 + threadIdx.x) * w;
         }
         out[(long)b * C + h * 64 + threadIdx.x] = O / L;
@@ -930,7 +941,7 @@ int attention_decode_impl(const float *q, long ldq, const float *kcache, const f
     const float scale = 1.0f / sqrtf((float)hs);
     const bool vec4 = (C % 4 == 0) && (ldq % 4 == 0) && ((uintptr_t)kcache % 16) == 0 &&
                       ((uintptr_t)vcache % 16) == 0 && ((uintptr_t)q % 16) == 0;
-    if (part && hs == 64 && vec4) {
+    if (part && hs == 64 && vec4 && cap <= 64 * DEC_KEYS) {
         const int S = (cap + DEC_KEYS - 1) / DEC_KEYS;
         int *tickets = (int *)(part + (size_t)B * H * S * DEC_PART);
         cudaLaunchConfig_t cfg = {};

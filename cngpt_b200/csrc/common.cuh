@@ -1,7 +1,8 @@
 // common.cuh - shared device helpers for libcngpt_cuda (sm_100a only).
 //
-// Inline-PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor, never with
-// cluster multicast), and the tcgen05 tensor-memory / MMA instructions, plus
+// Inline-PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor: each CTA
+// loads only into its own shared memory), and the tcgen05 tensor-memory / MMA
+// instructions, plus
 // the library-wide error channel. Every spin-wait here is bounded: after
 // kWaitLimitNs of global time it records an error code in g_cngpt_dev_error
 // and returns false so the kernel can wind down instead of hanging the GPU.
@@ -98,7 +99,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
-// 2-D tiled TMA load (no multicast) completing on an mbarrier.
+// 2-D tiled TMA load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, uint64_t *bar,
                                            int x, int y) {
     asm volatile(
@@ -143,7 +144,7 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
 }
 
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread
-// have completed (local CTA; no multicast).
+// have completed (this CTA's barrier only).
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
@@ -223,9 +224,8 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-// 2-D tiled TMA load into this CTA's shared memory whose completion is
-// counted on an mbarrier of either CTA of the pair (cluster address); no
-// multicast.
+// 2-D tiled TMA load into this CTA's shared memory only, whose completion is
+// counted on an mbarrier of either CTA of the pair (cluster address).
 __device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap, uint32_t bar_cluster,
                                                 int x, int y) {
     asm volatile(

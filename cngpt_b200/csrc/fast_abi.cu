@@ -156,6 +156,19 @@ int decode_step(const GPT *m, FastCtx *f, FastDev *d, int B, cudaStream_t s) {
     float *x = d->xl;
     CG_TRY(embed_fwd_at(d->next, w->wte, w->wpe, x, B, C, d->ctr, s));
     const size_t per = (size_t)d->kv_B * d->kv_T * C;
+    // LayerNorm statistics of the residual stream come from the last block of
+    // the GEMV that produced it (stats[0]: after c_proj, stats[1]: after
+    // mlp_proj); layer 0's come from the embedding inside the first GEMV
+    const bool st = B <= 8;
+    float *st_attn = d->ln_stats, *st_mlp = d->ln_stats + 16;
+    auto resid = [&](float *xx, const float *bias, float *stats, int *ticket) {
+        GemmEpi e = epi_resid_inplace(xx, C, bias);
+        if (st) {
+            e.ln_stats_out = stats;
+            e.ln_ticket = ticket;
+        }
+        return e;
+    };
     for (int l = 0; l < L; l++) {
         // LN1 fused into the qkv GEMV, whose epilogue also appends K and V
         GemmEpi eq = epi_store(f->qkv, 3 * C, w->c_attn_b[l]);
@@ -164,17 +177,19 @@ int decode_step(const GPT *m, FastCtx *f, FastDev *d, int B, cudaStream_t s) {
         eq.kv_ld = (long)d->kv_T * C;
         eq.kv_pos = d->ctr;
         eq.kv_C = C;
-        CG_TRY(gemm_ln(x, C, w->ln1_w[l], w->ln1_b[l], f->ln, w->c_attn_w[l], C, B, 3 * C, C, eq, s));
+        CG_TRY(gemm_ln(x, C, w->ln1_w[l], w->ln1_b[l], (st && l > 0) ? st_mlp : nullptr, f->ln,
+                       w->c_attn_w[l], C, B, 3 * C, C, eq, s));
         CG_TRY(attention_decode_at(f->qkv, 3L * C, d->kc + l * per, d->vc + l * per, d->kv_T, d->ctr,
                                    d->al, B, C, H, d->dec_part, s));
         CG_TRY(gemm(d->al, C, false, w->c_proj_w[l], C, false, B, C, C,
-                    epi_resid_inplace(x, C, w->c_proj_b[l]), s));
-        CG_TRY(gemm_ln(x, C, w->ln2_w[l], w->ln2_b[l], f->ln, w->mlp_fc_w[l], C, B, 4 * C, C,
-                       epi_gelu_only(f->hid, 4 * C, w->mlp_fc_b[l]), s));
+                    resid(x, w->c_proj_b[l], st_attn, d->ln_ticket), s));
+        CG_TRY(gemm_ln(x, C, w->ln2_w[l], w->ln2_b[l], st ? st_attn : nullptr, f->ln, w->mlp_fc_w[l], C, B,
+                       4 * C, C, epi_gelu_only(f->hid, 4 * C, w->mlp_fc_b[l]), s));
         CG_TRY(gemm(f->hid, 4 * C, false, w->mlp_proj_w[l], 4 * C, false, B, C, 4 * C,
-                    epi_resid_inplace(x, C, w->mlp_proj_b[l]), s));
+                    resid(x, w->mlp_proj_b[l], st_mlp, d->ln_ticket + 1), s));
     }
-    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, f->ln, w->wte, C, B, V, C, epi_store(f->logits, V, nullptr), s));
+    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, (st && L > 0) ? st_mlp : nullptr, f->ln, w->wte, C, B, V, C,
+                   epi_store(f->logits, V, nullptr), s));
     CG_TRY(argmax_log(f->logits, V, B, V, d->next, d->gen, d->ctr + 1, s));
     return decode_advance(d->ctr, s);
 }
@@ -238,6 +253,8 @@ extern "C" void fast_free(FastCtx *f) {
         dev_free(d->next);
         dev_free(d->gen);
         dev_free(d->ctr);
+        dev_free(d->ln_stats);
+        dev_free(d->ln_ticket);
         drop_graph(d);
         if (d->ev_a) cudaEventDestroy(d->ev_a);
         if (d->ev_b) cudaEventDestroy(d->ev_b);
@@ -287,6 +304,9 @@ extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B,
         CG_CUDA(cudaEventCreateWithFlags(&d->ev_a, cudaEventDisableTiming));
         CG_CUDA(cudaEventCreateWithFlags(&d->ev_b, cudaEventDisableTiming));
         CG_TRY(dev_alloc((void **)&d->ctr, 2 * sizeof(int), false));
+        CG_TRY(dev_alloc((void **)&d->ln_stats, 32 * sizeof(float), false));
+        CG_TRY(dev_alloc((void **)&d->ln_ticket, 2 * sizeof(int), false));
+        CG_CUDA(cudaMemsetAsync(d->ln_ticket, 0, 2 * sizeof(int), s));
     }
     if (d->kv_B != B || d->kv_T < Tmax) {
         CG_CUDA(cudaStreamSynchronize(s));

@@ -5,7 +5,7 @@
 // src/model.c / src/fast.c):
 //
 //   warp 0      TMA producer: 128B-swizzled tiles of A and B into a ring of
-//               shared-memory stages (plain per-CTA loads, no multicast)
+//               shared-memory stages (plain per-CTA loads of this GPU's memory)
 //   warp 1      MMA issuer: tcgen05.mma.kind::tf32, 128 x BN x 8 per
 //               instruction, accumulating into one of two TMEM buffers
 //   warps 2-9   epilogue: tcgen05.ld of the finished accumulator, then the
@@ -471,7 +471,7 @@ done:
 // issues tcgen05.mma.cta_group::2 with M = 256, which reads both CTAs' halves
 // and leaves rows [128r, 128r + 128) of the accumulator in CTA r's TMEM. Per
 // CTA that halves the B bytes per FLOP, so a k-block stage is 24-32 KB
-// instead of 48 KB and 6-8 stages fit. Loads are plain (no multicast); both
+// instead of 48 KB and 6-8 stages fit. Every load is a plain per-CTA load; both
 // CTAs' TMA completions count on the leader's `full` barrier, the MMA commits
 // arrive on `empty` / `tfull` in both CTAs, and the epilogue warps of both
 // CTAs release an accumulator on the leader's `tempty`. TF32 mode only.
@@ -728,10 +728,60 @@ __device__ __forceinline__ void halve_step(float *acc, int lane, int o, int &idx
     if (up) idx += h;
 }
 
+// LayerNorm statistics of M <= MT rows of X ([M, 4*K4], row pitch ldx):
+// the mean, then the biased variance about it (two passes, as
+// src/ops.c:231-247), each block-reduced over the 256 threads in fixed
+// order; eps 1e-5. CG reads bypass L1 (rows written by other blocks).
+template <int MT, bool CG>
+__device__ __forceinline__ void block_row_stats(const float *X, long ldx, int M, int K4, float (&mu)[MT],
+                                                float (&rs)[MT], float (*lnred)[MT], float (*lnstat)[MT]) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+        float ps[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) ps[m] = 0.f;
+        for (int k = t; k < K4; k += GV_THREADS) {
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (m < M) {
+                    const float4 *p = (const float4 *)(X + (long)m * ldx) + k;
+                    const float4 xv = CG ? __ldcg(p) : __ldg(p);
+                    if (pass == 0) {
+                        ps[m] += (xv.x + xv.y) + (xv.z + xv.w);
+                    } else {
+                        const float a = xv.x - mu[m], b = xv.y - mu[m], c = xv.z - mu[m], d = xv.w - mu[m];
+                        ps[m] += (a * a + b * b) + (c * c + d * d);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            const float v = warp_sum(ps[m]);
+            if (lane == 0) lnred[warp][m] = v;
+        }
+        __syncthreads();
+        if (t < MT) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < GV_THREADS / 32; ++w) v += lnred[w][t];
+            lnstat[pass][t] = v / (float)(4 * K4);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (pass == 0) mu[m] = lnstat[0][m];
+            else rs[m] = 1.0f / sqrtf(lnstat[1][m] + 1e-5f);
+        }
+    }
+}
+
 template <int MT, bool LNF>
 __global__ void __launch_bounds__(GV_THREADS)
 gemv_kernel(const float *__restrict__ X, long ldx, const float *__restrict__ W, long ldw, int M, int N,
-            int K, GemmEpi epi, const float *__restrict__ lnw, const float *__restrict__ lnb) {
+            int K, GemmEpi epi, const float *__restrict__ lnw, const float *__restrict__ lnb,
+            const float *__restrict__ ln_stats) {
     constexpr int R = GV_R, NV = R * MT;
     __shared__ float red[GV_THREADS / 32][NV];
     __shared__ float lnred[GV_THREADS / 32][MT], lnstat[2][MT];
@@ -756,46 +806,14 @@ gemv_kernel(const float *__restrict__ X, long ldx, const float *__restrict__ W, 
     pdl_wait();
     float mu[MT], rs[MT];
     if constexpr (LNF) {
-        // LayerNorm statistics of the MT rows of X: mean, then the biased
-        // variance about it (two passes, as src/ops.c:231-247), block-reduced
-        // in fixed order
-#pragma unroll
-        for (int pass = 0; pass < 2; ++pass) {
-            float ps[MT];
-#pragma unroll
-            for (int m = 0; m < MT; ++m) ps[m] = 0.f;
-            for (int k = t; k < K4; k += GV_THREADS) {
-#pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    if (m < M) {
-                        const float4 xv = __ldg((const float4 *)(X + (long)m * ldx) + k);
-                        if (pass == 0) {
-                            ps[m] += (xv.x + xv.y) + (xv.z + xv.w);
-                        } else {
-                            const float a = xv.x - mu[m], b = xv.y - mu[m], c = xv.z - mu[m], d = xv.w - mu[m];
-                            ps[m] += (a * a + b * b) + (c * c + d * d);
-                        }
-                    }
-                }
-            }
+        if (ln_stats) {
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
-                const float v = warp_sum(ps[m]);
-                if (lane == 0) lnred[warp][m] = v;
+                mu[m] = m < M ? ln_stats[2 * m] : 0.f;
+                rs[m] = m < M ? ln_stats[2 * m + 1] : 0.f;
             }
-            __syncthreads();
-            if (t < MT) {
-                float v = 0.f;
-#pragma unroll
-                for (int w = 0; w < GV_THREADS / 32; ++w) v += lnred[w][t];
-                lnstat[pass][t] = v / (float)K;
-            }
-            __syncthreads();
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                if (pass == 0) mu[m] = lnstat[0][m];
-                else rs[m] = 1.0f / sqrtf(lnstat[1][m] + 1e-5f);
-            }
+        } else {
+            block_row_stats<MT, false>(X, ldx, M, K4, mu, rs, lnred, lnstat);
         }
     }
     auto xload = [&](int m, int k) -> float4 {
@@ -869,11 +887,31 @@ gemv_kernel(const float *__restrict__ X, long ldx, const float *__restrict__ W, 
             }
         }
     }
+    if (epi.ln_stats_out) {
+        // the last block to finish (integer ticket, writes fenced first)
+        // computes the LayerNorm statistics of the completed D2 rows for the
+        // consumer of this residual stream; the ticket is left at zero
+        __shared__ int last;
+        __threadfence();
+        __syncthreads();
+        if (t == 0) last = atomicAdd(epi.ln_ticket, 1) == (int)gridDim.x - 1;
+        __syncthreads();
+        if (last) {
+            __threadfence();
+            float smu[MT], srs[MT];
+            block_row_stats<MT, true>(epi.D2, epi.ldd2, M, N >> 2, smu, srs, lnred, lnstat);
+            if (t < MT && t < M) {
+                epi.ln_stats_out[2 * t] = lnstat[0][t];
+                epi.ln_stats_out[2 * t + 1] = 1.0f / sqrtf(lnstat[1][t] + 1e-5f);
+            }
+            if (t == 0) *epi.ln_ticket = 0;
+        }
+    }
 }
 
 template <int MT, bool LNF>
 int launch_gemv(const float *A, long lda, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi,
-                const float *lnw, const float *lnb, cudaStream_t s) {
+                const float *lnw, const float *lnb, const float *lns, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((N + GV_R - 1) / GV_R);
     cfg.blockDim = dim3(GV_THREADS);
@@ -883,25 +921,39 @@ int launch_gemv(const float *A, long lda, const float *B, long ldb, int M, int N
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    CG_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<MT, LNF>, A, lda, B, ldb, M, N, K, epi, lnw, lnb));
+    CG_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<MT, LNF>, A, lda, B, ldb, M, N, K, epi, lnw, lnb, lns));
     ++g_launch_count;
     return OK;
 }
 
 template <bool LNF>
 int dispatch_gemv(const float *A, long lda, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi,
-                  const float *lnw, const float *lnb, cudaStream_t s) {
-    if (M <= 1) return launch_gemv<1, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, s);
-    if (M <= 2) return launch_gemv<2, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, s);
-    if (M <= 4) return launch_gemv<4, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, s);
-    return launch_gemv<8, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, s);
+                  const float *lnw, const float *lnb, const float *lns, cudaStream_t s) {
+    if (M <= 1) return launch_gemv<1, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, lns, s);
+    if (M <= 2) return launch_gemv<2, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, lns, s);
+    if (M <= 4) return launch_gemv<4, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, lns, s);
+    return launch_gemv<8, LNF>(A, lda, B, ldb, M, N, K, epi, lnw, lnb, lns, s);
 }
 
-bool gemv_ok(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_mn, int M, int K,
+// LayerNorm statistics (mean, rstd) of M rows, one block per row: the
+// stand-alone form of the GEMV's last-block statistics
+__global__ void __launch_bounds__(GV_THREADS) ln_stats_kernel(const float *__restrict__ X, long ldx, int K,
+                                                              float *__restrict__ out) {
+    __shared__ float lnred[GV_THREADS / 32][1], lnstat[2][1];
+    float mu[1], rs[1];
+    block_row_stats<1, true>(X + (long)blockIdx.x * ldx, ldx, 1, K >> 2, mu, rs, lnred, lnstat);
+    if (threadIdx.x == 0) {
+        out[2 * blockIdx.x] = mu[0];
+        out[2 * blockIdx.x + 1] = rs[0];
+    }
+}
+
+bool gemv_ok(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_mn, int M, int N, int K,
              const GemmEpi &epi) {
     auto al = [](const void *p) { return ((uintptr_t)p % 16) == 0; };
     return M <= 8 && !a_mn && !b_mn && K % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 && al(A) && al(B) &&
-           (!epi.kc || epi.mode == EPI_STORE);
+           (!epi.kc || epi.mode == EPI_STORE) &&
+           (!epi.ln_stats_out || (epi.mode == EPI_RESID && N % 4 == 0 && epi.ldd2 % 4 == 0 && al(epi.D2)));
 }
 
 // ------------------------------------------------------- tensor maps
@@ -1012,26 +1064,41 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ ws, int S, long s
     }
 }
 
-// Number of K splits for a GEMM with `tiles` output tiles: more work units
-// fill the last wave of the persistent grid, each extra split costs a write
-// and a read of an M x N partial. Modelled time, realistic rates.
-int choose_ksplit(int tiles, int kblocks, int M, int N, long K, bool split3, int workers = 0) {
-    const double sms = workers > 0 ? workers / 2 : num_sms();  // pair kernels: one worker per pair
-    const double flops = 2.0 * M * (double)N * K * (split3 ? 3.0 : 1.0);
-    const double peak = 450e12, hbm = 6e12;
-    auto cost = [&](int k) {
-        const double units = (double)tiles * k, waves = std::ceil(units / sms);
-        return flops / (peak * units / (waves * sms)) + (k > 1 ? 2.0 * k * M * (double)N * 4 / hbm : 0.0);
-    };
+// Modelled time of a GEMM run as `units` persistent work units on `workers`
+// (SMs, or CTA pairs): the slower of the tensor rate and the L2-to-SM operand
+// stream (bytes per FLOP of the CTA tile: (rows + loaded B rows) x 128 B per
+// 2 x rows x BN x 32 FLOP per k-block), both scaled by the last wave's fill,
+// plus the split-K partial sums (written and read once each).
+struct GemmModel {
+    static constexpr double kTensor = 745e12;  // TF32 sustained, this kernel
+    static constexpr double kL2 = 11.5e12;     // measured L2 -> SM operand stream
+    static constexpr double kHbm = 6e12;
+    static double time(double flops, double bpf, long units, long workers, int ks, long MN, bool split3) {
+        const double waves = std::ceil((double)units / workers);
+        const double eff = (double)units / (waves * workers);
+        const double t_mma = flops * (split3 ? 3.0 : 1.0) / (kTensor * eff);
+        const double t_l2 = flops * bpf / (kL2 * eff);
+        return std::max(t_mma, t_l2) + (ks > 1 ? 2.0 * ks * MN * 4 / kHbm : 0.0);
+    }
+};
+
+// Number of K splits for a GEMM with `tiles` output tiles of width bn (rows
+// per CTA 128; pair kernels load bn / 2 B rows per CTA).
+int choose_ksplit(int tiles, int kblocks, int M, int N, long K, bool split3, int workers = 0, int bn = 128,
+                  bool pair = false, double *t_out = nullptr) {
+    const long w = workers > 0 ? workers : num_sms();
+    const double flops = 2.0 * M * (double)N * K;
+    const double bpf = (128.0 + (pair ? bn / 2 : bn)) * 128.0 / (2.0 * 128 * bn * 32);
     int best = 1;
-    double bt = cost(1);
+    double bt = GemmModel::time(flops, bpf, tiles, w, 1, (long)M * N, split3);
     for (int k = 2; k <= 8 && kblocks / k >= 4; ++k) {
-        const double t = cost(k);
+        const double t = GemmModel::time(flops, bpf, (long)tiles * k, w, k, (long)M * N, split3);
         if (t < 0.97 * bt) {
             bt = t;
             best = k;
         }
     }
+    if (t_out) *t_out = bt;
     return best;
 }
 
@@ -1053,7 +1120,7 @@ int launch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, 
     const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n;
     const int kblocks = (K + BK - 1) / BK;
-    int ks = choose_ksplit(tiles, kblocks, M, N, K, SPLIT);
+    int ks = choose_ksplit(tiles, kblocks, M, N, K, SPLIT, 0, BN, false);
     int kb_per = (kblocks + ks - 1) / ks;
     ks = (kblocks + kb_per - 1) / kb_per;  // every split non-empty
     float *ws = ks > 1 ? splitk_workspace((size_t)ks * M * N, s) : nullptr;
@@ -1088,7 +1155,7 @@ bool pair_gemm_enabled() {
     static int on = -1;
     if (on < 0) {
         const char *e = getenv("CNGPT_CUDA_GEMM_PAIR");
-        on = (e && e[0] == '1') ? 1 : 0;
+        on = (e && e[0] == '0') ? 0 : 1;
     }
     return on == 1;
 }
@@ -1131,7 +1198,7 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     const int tiles = tiles_m * tiles_n;
     const int kblocks = (K + BK - 1) / BK;
     const int slots = pair_slots(kern, C::THREADS, C::SMEM);
-    int ks = choose_ksplit(tiles, kblocks, M, N, K, false, slots * 2);
+    int ks = choose_ksplit(tiles, kblocks, M, N, K, false, slots, BN, true);
     int kb_per = (kblocks + ks - 1) / ks;
     ks = (kblocks + kb_per - 1) / kb_per;
     float *ws = ks > 1 ? splitk_workspace((size_t)ks * M * N, s) : nullptr;
@@ -1162,18 +1229,27 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     return OK;
 }
 
+// Tile width for the pair kernel: the modelled-faster of 256 and 128 (each
+// with its best K split).
+int pair_tile_width(int M, int N, int K) {
+    const int pairs = num_sms() / 2, tm = (M + 2 * BM - 1) / (2 * BM), kblocks = (K + BK - 1) / BK;
+    if (N <= 128) return 128;
+    double t256 = 0, t128 = 0;
+    choose_ksplit(tm * ((N + 255) / 256), kblocks, M, N, K, false, pairs, 256, true, &t256);
+    choose_ksplit(tm * ((N + 127) / 128), kblocks, M, N, K, false, pairs, 128, true, &t128);
+    return t256 <= t128 ? 256 : 128;
+}
+
 template <bool A_MN, bool B_MN>
 int dispatch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, int K,
                 const GemmEpi &epi, cudaStream_t s, bool split) {
     if (split) return launch_tc<128, A_MN, B_MN, true>(A, lda, B, ldb, M, N, K, epi, s);
     if (pair_gemm_enabled() && M > BM) {
-        // CTA pairs, 256 x 256 tiles unless their last wave leaves the pairs
-        // much emptier than 256 x 128 tiles would
-        const long pairs = num_sms() / 2, tm2 = (M + 2 * BM - 1) / (2 * BM);
-        const long t256 = tm2 * ((N + 255) / 256);
-        auto eff2 = [&](long t) { return (double)t / (double)(((t + pairs - 1) / pairs) * pairs); };
-        if (N > 128 && eff2(t256) >= 0.8)
-            return launch_tc2<256, A_MN, B_MN>(A, lda, B, ldb, M, N, K, epi, s);
+        // CTA pairs with 256 x 256 or 256 x 128 tiles, whichever the model
+        // below times faster (tile width trades wave fill against the
+        // L2-to-SM bytes per FLOP)
+        const int bn = pair_tile_width(M, N, K);
+        if (bn == 256) return launch_tc2<256, A_MN, B_MN>(A, lda, B, ldb, M, N, K, epi, s);
         return launch_tc2<128, A_MN, B_MN>(A, lda, B, ldb, M, N, K, epi, s);
     }
     // 128 x 256 tiles halve the A traffic per FLOP; take them unless their
@@ -1192,11 +1268,11 @@ bool tma_ok(const float *p, long ld) {
 
 }  // namespace
 
-int gemm_ln(const float *X, long ldx, const float *ln_w, const float *ln_b, float *ln_out, const float *B,
-            long ldb, int M, int N, int K, const GemmEpi &epi, cudaStream_t s) {
+int gemm_ln(const float *X, long ldx, const float *ln_w, const float *ln_b, const float *ln_stats,
+            float *ln_out, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi, cudaStream_t s) {
     auto al = [](const void *p) { return ((uintptr_t)p % 16) == 0; };
-    if (M > 0 && N > 0 && gemv_ok(X, ldx, false, B, ldb, false, M, K, epi) && al(ln_w) && al(ln_b))
-        return dispatch_gemv<true>(X, ldx, B, ldb, M, N, K, epi, ln_w, ln_b, s);
+    if (M > 0 && N > 0 && gemv_ok(X, ldx, false, B, ldb, false, M, N, K, epi) && al(ln_w) && al(ln_b))
+        return dispatch_gemv<true>(X, ldx, B, ldb, M, N, K, epi, ln_w, ln_b, ln_stats, s);
     CG_TRY(layernorm_fwd(X, ldx, ln_w, ln_b, ln_out, K, nullptr, nullptr, M, K, s));
     return gemm(ln_out, K, false, B, ldb, false, M, N, K, epi, s);
 }
@@ -1216,8 +1292,23 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
                   (!epi.R || epi.ldr % 4 == 0) && (!epi.G || epi.ldg % 4 == 0);
     }
     const int prec = precision();
-    if (gemv_ok(A, lda, a_mn, B, ldb, b_mn, M, K, epi) && ((long)N * K >= (1L << 16) || epi.kc))
-        return dispatch_gemv<false>(A, lda, B, ldb, M, N, K, epi, nullptr, nullptr, s);
+    if (gemv_ok(A, lda, a_mn, B, ldb, b_mn, M, N, K, epi) &&
+        ((long)N * K >= (1L << 16) || epi.kc || epi.ln_stats_out))
+        return dispatch_gemv<false>(A, lda, B, ldb, M, N, K, epi, nullptr, nullptr, nullptr, s);
+    if (epi.ln_stats_out) {  // statistics requested outside the GEMV path: a separate pass
+        GemmEpi e3 = epi;
+        e3.ln_stats_out = nullptr;
+        e3.ln_ticket = nullptr;
+        CG_TRY(gemm(A, lda, a_mn, B, ldb, b_mn, M, N, K, e3, s));
+        if (epi.mode != EPI_RESID || N % 4 != 0 || epi.ldd2 % 4 != 0 || ((uintptr_t)epi.D2 % 16) != 0) {
+            set_last_error(ERR_ARG, "gemm: LayerNorm statistics need an aligned RESID output");
+            return ERR_ARG;
+        }
+        ln_stats_kernel<<<M, GV_THREADS, 0, s>>>(epi.D2, epi.ldd2, N, epi.ln_stats_out);
+        ++g_launch_count;
+        CG_CUDA(cudaGetLastError());
+        return OK;
+    }
     if (epi.kc) {  // KV-cache columns: the GEMM, then the cache append
         GemmEpi e3 = epi;
         e3.kc = e3.vc = nullptr;

@@ -84,6 +84,11 @@ struct GemmEpi {
     long kv_ld = 0;
     const int *kv_pos = nullptr;
     int kv_C = 0;
+    // decode (RESID mode): LayerNorm statistics (mean, rstd) of each finished
+    // D2 row into ln_stats_out[2m], [2m+1], for the next LayerNorm-fused GEMV;
+    // ln_ticket: one int, zero before the call and left at zero after it
+    float *ln_stats_out = nullptr;
+    int *ln_ticket = nullptr;
 };
 
 // out[M,N] = op(A)[M,K] * op(B)[N,K]^T, with the epilogue applied per element.
@@ -101,9 +106,11 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 // y = LayerNorm(X) (eps 1e-5, weights ln_w / ln_b) then the GEMM above with
 // A = y (K-major, M x K). For M <= 8 the normalisation is fused into the GEMV
-// (no y is written); otherwise y goes to ln_out [M, K] first.
-int gemm_ln(const float *X, long ldx, const float *ln_w, const float *ln_b, float *ln_out,
-            const float *B, long ldb, int M, int N, int K, const GemmEpi &epi, cudaStream_t s);
+// (no y is written), with the row statistics taken from ln_stats (mean, rstd
+// per row, e.g. written by the producer's ln_stats_out) when given, else
+// computed in every block; otherwise y goes to ln_out [M, K] first.
+int gemm_ln(const float *X, long ldx, const float *ln_w, const float *ln_b, const float *ln_stats,
+            float *ln_out, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi, cudaStream_t s);
 
 // Counts of kernel launches issued by this library (for benchmarks).
 extern unsigned long long g_launch_count;

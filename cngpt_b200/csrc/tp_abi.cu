@@ -288,7 +288,7 @@ int decode_step(const GPT *m, TpState *t, int B, cudaStream_t s) {
         eq.kv_ld = (long)t->kv_T * Cl;
         eq.kv_pos = t->ctr;
         eq.kv_C = Cl;
-        CG_TRY(gemm_ln(x, C, w->ln1_w[l], w->ln1_b[l], t->ln, t->qkv_w(l), C, B, 3 * Cl, C, eq, s));
+        CG_TRY(gemm_ln(x, C, w->ln1_w[l], w->ln1_b[l], nullptr, t->ln, t->qkv_w(l), C, B, 3 * Cl, C, eq, s));
         CG_TRY(attention_decode_at(t->qkv, 3L * Cl, t->kc + l * per, t->vc + l * per, t->kv_T, t->ctr,
                                    t->al, B, Cl, t->p.nh, t->dec_part, s));
         CG_TRY(gemm(t->al, Cl, false, w->c_proj_w[l] + (size_t)t->p.h0 * t->hs, C, false, B, C, Cl,
@@ -299,13 +299,13 @@ int decode_step(const GPT *m, TpState *t, int B, cudaStream_t s) {
         g.bias = w->mlp_fc_b[l] + t->p.f0;
         g.D2 = t->hid;
         g.ldd2 = nf;
-        CG_TRY(gemm_ln(x, C, w->ln2_w[l], w->ln2_b[l], t->ln, w->mlp_fc_w[l] + (size_t)t->p.f0 * C, C, B, nf,
+        CG_TRY(gemm_ln(x, C, w->ln2_w[l], w->ln2_b[l], nullptr, t->ln, w->mlp_fc_w[l] + (size_t)t->p.f0 * C, C, B, nf,
                        C, g, s));
         CG_TRY(gemm(t->hid, nf, false, w->mlp_proj_w[l] + t->p.f0, 4L * C, false, B, C, nf,
                     epi_partial(t, x, C, w->mlp_proj_b[l]), s));
         CG_TRY(allreduce(t, x, (size_t)B * C, s));
     }
-    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, t->ln, w->wte + (size_t)t->p.v0 * C, C, B, t->p.nv, C,
+    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, nullptr, t->ln, w->wte + (size_t)t->p.v0 * C, C, B, t->p.nv, C,
                    epi_store(t->logits, t->ldlog, nullptr), s));
     CG_TRY(greedy(t, B, s));
     return decode_advance(t->ctr, s);
