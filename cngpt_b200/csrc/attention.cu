@@ -14,6 +14,7 @@
 // hs = 8) take a CUDA-core kernel with one warp per query row.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -830,11 +831,23 @@ bool mma_ok(int C, std::initializer_list<const void *> ptrs) {
 }
 }  // namespace
 
+// CNGPT_CUDA_ATTN_TC=0 keeps the TF32 forward on the mma.sync kernel
+bool tc_attention_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("CNGPT_CUDA_ATTN_TC");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 int attention_fwd(const float *qkv, float *out, float *lse, int B, int T, int C, int H,
                   cudaStream_t s) {
     if (B <= 0 || T <= 0) return OK;
     const int hs = C / H;
     const float scale = 1.0f / sqrtf((float)hs);
+    if (precision() == PREC_TF32 && tc_attention_enabled() && attention_fwd_tc(qkv, out, lse, B, T, C, H, s) == OK)
+        return OK;
     if (hs == HS && precision() != PREC_FP32 && mma_ok(C, {qkv, out})) {
         const int smem = (FQ + 4 * TK) * LDS * sizeof(float);
         dim3 grid((T + FQ - 1) / FQ, B * H);

@@ -188,9 +188,14 @@ int decode_step(const GPT *m, FastCtx *f, FastDev *d, int B, cudaStream_t s) {
         CG_TRY(gemm(f->hid, 4 * C, false, w->mlp_proj_w[l], 4 * C, false, B, C, 4 * C,
                     resid(x, w->mlp_proj_b[l], st_mlp, d->ln_ticket + 1), s));
     }
-    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, (st && L > 0) ? st_mlp : nullptr, f->ln, w->wte, C, B, V, C,
-                   epi_store(f->logits, V, nullptr), s));
-    CG_TRY(argmax_log(f->logits, V, B, V, d->next, d->gen, d->ctr + 1, s));
+    // LM head with the greedy argmax folded into its epilogue
+    GemmEpi eh = epi_store(f->logits, V, nullptr);
+    eh.argmax_key = d->am_key;
+    eh.argmax_out = d->next;
+    eh.argmax_log = d->gen;
+    eh.argmax_step = d->ctr + 1;
+    eh.argmax_ticket = d->ln_ticket + 2;
+    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, (st && L > 0) ? st_mlp : nullptr, f->ln, w->wte, C, B, V, C, eh, s));
     return decode_advance(d->ctr, s);
 }
 
@@ -255,6 +260,7 @@ extern "C" void fast_free(FastCtx *f) {
         dev_free(d->ctr);
         dev_free(d->ln_stats);
         dev_free(d->ln_ticket);
+        dev_free(d->am_key);
         drop_graph(d);
         if (d->ev_a) cudaEventDestroy(d->ev_a);
         if (d->ev_b) cudaEventDestroy(d->ev_b);
@@ -305,8 +311,10 @@ extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B,
         CG_CUDA(cudaEventCreateWithFlags(&d->ev_b, cudaEventDisableTiming));
         CG_TRY(dev_alloc((void **)&d->ctr, 2 * sizeof(int), false));
         CG_TRY(dev_alloc((void **)&d->ln_stats, 32 * sizeof(float), false));
-        CG_TRY(dev_alloc((void **)&d->ln_ticket, 2 * sizeof(int), false));
-        CG_CUDA(cudaMemsetAsync(d->ln_ticket, 0, 2 * sizeof(int), s));
+        CG_TRY(dev_alloc((void **)&d->ln_ticket, 4 * sizeof(int), false));
+        CG_CUDA(cudaMemsetAsync(d->ln_ticket, 0, 4 * sizeof(int), s));
+        CG_TRY(dev_alloc((void **)&d->am_key, 8 * sizeof(unsigned long long), false));
+        CG_CUDA(cudaMemsetAsync(d->am_key, 0, 8 * sizeof(unsigned long long), s));
     }
     if (d->kv_B != B || d->kv_T < Tmax) {
         CG_CUDA(cudaStreamSynchronize(s));

@@ -869,22 +869,71 @@ gemv_kernel(const float *__restrict__ X, long ldx, const float *__restrict__ W, 
     for (; o > 0; o >>= 1) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], o);
     if ((lane & (32 / NV - 1)) == 0) red[warp][idx] = acc[0];
     __syncthreads();
+    unsigned long long amkey = 0;  // greedy key of this thread's (m, n), 0 = none
     if (t < NV) {
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < GV_THREADS / 32; ++w) v += red[w][t];
         const int r = t / MT, m = t % MT, n = n0 + r;
+        if (epi.argmax_key && m < M && n < N) {
+            const uint32_t u = __float_as_uint(v * epi.alpha + (epi.bias ? epi.bias[n] : 0.0f));
+            const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            amkey = ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+        }
         if (m < M && n < N) {
             long ld = 0;
             const float *ax = epi_aux(epi, ld);
             const float bias = epi.bias ? epi.bias[n] : 0.0f;
-            epi_apply(epi, m, n, v, bias, ax ? ax[(long)m * ld + n] : 0.0f);
+            if (epi.push_bufs) {
+                // tensor-parallel partial: to every rank's receive slot
+                const float a = v * epi.alpha + bias;
+                const float val = epi.mode == EPI_RESID ? (ax ? ax[(long)m * ld + n] : 0.0f) + a : a;
+                const unsigned long long ep =
+                    (unsigned long long)(*epi.push_step) * epi.push_nk + epi.push_k + 1;
+                for (int r = 0; r < epi.push_world; ++r)
+                    tp_slot(epi.push_bufs[r], epi.push_world, epi.push_ld, (int)(ep & 1), epi.push_rank)
+                        [(long)m * epi.push_ld + n] = val;
+            } else {
+                epi_apply(epi, m, n, v, bias, ax ? ax[(long)m * ld + n] : 0.0f);
+            }
             if (epi.kc && n >= epi.kv_C) {  // STORE mode: the K / V value just stored
                 const float val = v * epi.alpha + bias;
                 const long at = (long)m * epi.kv_ld + (long)(*epi.kv_pos) * epi.kv_C;
                 if (n < 2 * epi.kv_C) epi.kc[at + (n - epi.kv_C)] = val;
                 else epi.vc[at + (n - 2 * epi.kv_C)] = val;
             }
+        }
+    }
+    if (epi.argmax_key) {
+        // rows m of this block's NV values sit in lanes t = r * MT + m of warp 0
+        __shared__ int alast;
+        if (warp == 0) {
+#pragma unroll
+            for (int o = MT; o < 32; o <<= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, amkey, o);
+                amkey = other > amkey ? other : amkey;
+            }
+            if (t < MT && t < M && amkey) atomicMax(epi.argmax_key + t, amkey);
+        }
+        __threadfence();
+        __syncthreads();
+        if (t == 0) alast = atomicAdd(epi.argmax_ticket, 1) == (int)gridDim.x - 1;
+        __syncthreads();
+        if (alast) {
+            __threadfence();
+            if (t < M) {
+                const unsigned long long k = atomicExch(epi.argmax_key + t, 0ull);
+                const uint32_t ord = (uint32_t)(k >> 32);
+                const int col = (int)(0xFFFFFFFFu - (uint32_t)k);
+                const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
+                if (epi.argmax_out) epi.argmax_out[t] = col;
+                if (epi.argmax_log) epi.argmax_log[(long)(*epi.argmax_step) * M + t] = col;
+                if (epi.argmax_pair) {
+                    epi.argmax_pair[t] = (int)u;
+                    epi.argmax_pair[M + t] = col;
+                }
+            }
+            if (t == 0) *epi.argmax_ticket = 0;
         }
     }
     if (epi.ln_stats_out) {
@@ -905,6 +954,26 @@ gemv_kernel(const float *__restrict__ X, long ldx, const float *__restrict__ W, 
                 epi.ln_stats_out[2 * t + 1] = 1.0f / sqrtf(lnstat[1][t] + 1e-5f);
             }
             if (t == 0) *epi.ln_ticket = 0;
+        }
+    }
+    if (epi.push_bufs) {
+        // every block's pushes are fenced at system scope before its ticket;
+        // the last block then publishes the epoch on every rank's flag
+        // (the CTA barrier makes the block's pushes visible to thread 0, whose
+        // system-scope fence is cumulative over them)
+        __shared__ int plast;
+        __syncthreads();
+        if (t == 0) {
+            __threadfence_system();
+            plast = atomicAdd(epi.push_ticket, 1) == (int)gridDim.x - 1;
+        }
+        __syncthreads();
+        if (plast && t < epi.push_world) {
+            __threadfence_system();
+            const unsigned long long ep = (unsigned long long)(*epi.push_step) * epi.push_nk + epi.push_k + 1;
+            unsigned long long *flag = (unsigned long long *)epi.push_bufs[t] + epi.push_rank;
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(ep) : "memory");
+            if (t == 0) *epi.push_ticket = 0;
         }
     }
 }
@@ -953,7 +1022,9 @@ bool gemv_ok(const float *A, long lda, bool a_mn, const float *B, long ldb, bool
     auto al = [](const void *p) { return ((uintptr_t)p % 16) == 0; };
     return M <= 8 && !a_mn && !b_mn && K % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 && al(A) && al(B) &&
            (!epi.kc || epi.mode == EPI_STORE) &&
-           (!epi.ln_stats_out || (epi.mode == EPI_RESID && N % 4 == 0 && epi.ldd2 % 4 == 0 && al(epi.D2)));
+           (!epi.ln_stats_out || (epi.mode == EPI_RESID && N % 4 == 0 && epi.ldd2 % 4 == 0 && al(epi.D2))) &&
+           (!epi.push_bufs || ((epi.mode == EPI_RESID || epi.mode == EPI_STORE) && !epi.ln_stats_out && !epi.kc)) &&
+           (!epi.argmax_key || (epi.mode == EPI_STORE && !epi.push_bufs && !epi.kc));
 }
 
 // ------------------------------------------------------- tensor maps
@@ -1049,11 +1120,36 @@ float *splitk_workspace(size_t floats, cudaStream_t s) {
     return g_splitk_ws;
 }
 
-// out = epilogue(sum over splits of ws[s]) in split order (deterministic)
+// out = epilogue(sum over splits of ws[s]) in split order (deterministic).
+// Vector form: 4 consecutive columns per thread (N % 4 == 0, 16-byte aligned
+// partials); the epilogue is applied per element.
 __global__ void splitk_reduce_kernel(const float *__restrict__ ws, int S, long stride, int M, int N,
                                      GemmEpi epi) {
     long ld = 0;
     const float *aux = epi_aux(epi, ld);
+    if ((N & 3) == 0) {
+        const int N4 = N >> 2;
+        const int total = M * N4;
+        const float4 *w4 = (const float4 *)ws;
+        const long s4 = stride >> 2;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+            float4 a = w4[i];
+            for (int k = 1; k < S; ++k) {
+                const float4 b = w4[k * s4 + i];
+                a.x += b.x;
+                a.y += b.y;
+                a.z += b.z;
+                a.w += b.w;
+            }
+            const int m = i / N4, n = (i - m * N4) * 4;
+            const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                epi_apply(epi, m, n + j, av[j], epi.bias ? epi.bias[n + j] : 0.0f,
+                          aux ? aux[(long)m * ld + n + j] : 0.0f);
+        }
+        return;
+    }
     const long total = (long)M * N;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         float a = ws[i];
@@ -1144,7 +1240,7 @@ int launch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, 
     kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, ks, kb_per, stride, pe);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
-    const int rgrid = (int)std::min<long>((stride + 255) / 256, (long)num_sms() * 8);
+    const int rgrid = (int)std::min<long>((stride / 4 + 255) / 256, (long)num_sms() * 16);
     splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(ws, ks, stride, M, N, epi);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
@@ -1222,7 +1318,7 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, ks, kb_per, stride, pe);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
-    const int rgrid = (int)std::min<long>((stride + 255) / 256, (long)num_sms() * 8);
+    const int rgrid = (int)std::min<long>((stride / 4 + 255) / 256, (long)num_sms() * 16);
     splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(ws, ks, stride, M, N, epi);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
@@ -1293,8 +1389,24 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
     }
     const int prec = precision();
     if (gemv_ok(A, lda, a_mn, B, ldb, b_mn, M, N, K, epi) &&
-        ((long)N * K >= (1L << 16) || epi.kc || epi.ln_stats_out))
+        ((long)N * K >= (1L << 16) || epi.kc || epi.ln_stats_out || epi.push_bufs))
         return dispatch_gemv<false>(A, lda, B, ldb, M, N, K, epi, nullptr, nullptr, nullptr, s);
+    if (epi.push_bufs) {
+        set_last_error(ERR_ARG, "gemm: peer push needs the GEMV path (M <= 8, aligned K-major operands)");
+        return ERR_ARG;
+    }
+    if (epi.argmax_key) {  // greedy step outside the GEMV path: the GEMM, then an argmax pass
+        GemmEpi e3 = epi;
+        e3.argmax_key = nullptr;
+        CG_TRY(gemm(A, lda, a_mn, B, ldb, b_mn, M, N, K, e3, s));
+        if (epi.mode != EPI_STORE) {
+            set_last_error(ERR_ARG, "gemm: the fused argmax needs STORE mode");
+            return ERR_ARG;
+        }
+        if (epi.argmax_pair) CG_TRY(argmax_rows(epi.D, epi.ldd, M, N, epi.argmax_pair + M, (float *)epi.argmax_pair, s));
+        if (epi.argmax_out) CG_TRY(argmax_log(epi.D, epi.ldd, M, N, epi.argmax_out, epi.argmax_log, epi.argmax_step, s));
+        return OK;
+    }
     if (epi.ln_stats_out) {  // statistics requested outside the GEMV path: a separate pass
         GemmEpi e3 = epi;
         e3.ln_stats_out = nullptr;
@@ -1334,6 +1446,11 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
     return OK;
+}
+
+int make_tensor_map(CUtensorMap_st *out, const float *p, long inner, long outer, long ld, int box0, int box1,
+                    bool mn_major) {
+    return make_map(out, p, inner, outer, ld, box0, box1, mn_major);
 }
 
 }  // namespace cg

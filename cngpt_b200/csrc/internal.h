@@ -5,6 +5,8 @@
 #include <cstdint>
 #include <cstdio>
 
+struct CUtensorMap_st;
+
 namespace cg {
 
 // ---------------------------------------------------------------- errors
@@ -25,6 +27,7 @@ enum DevError : int {
     DEV_ERR_GEMM_MMA = 102,
     DEV_ERR_GEMM_EPILOGUE = 103,
     DEV_ERR_GEMM_TRANSFORM = 104,
+    DEV_ERR_TP_FLAG = 201,  // a peer's partial sum did not arrive in time
 };
 
 void set_last_error(int status, const char *fmt, ...);
@@ -33,6 +36,8 @@ const char *last_message();
 int check_device_error();  // reads and clears the device error words
 int gemm_take_dev_error();
 int attn_take_dev_error();
+int tp_take_dev_error();
+int attn_tc_take_dev_error();
 
 #define CG_CUDA(call)                                                                 \
     do {                                                                              \
@@ -89,7 +94,37 @@ struct GemmEpi {
     // ln_ticket: one int, zero before the call and left at zero after it
     float *ln_stats_out = nullptr;
     int *ln_ticket = nullptr;
+    // tensor-parallel decode (GEMV path, STORE or RESID): instead of writing
+    // D / D2, every value is pushed into the receive buffer of every rank
+    // (peer memory over NVLink, slot = epoch & 1, source = push_rank), and the
+    // last block raises this rank's flag on every rank to the epoch
+    // (*push_step * push_nk + push_k + 1). Layout of each rank's buffer:
+    // uint64 flags[TP_MAX_WORLD] (256 B), then float data[2][world][8][push_ld].
+    char *const *push_bufs = nullptr;
+    int push_world = 0, push_rank = 0, push_ld = 0, push_k = 0, push_nk = 0;
+    const int *push_step = nullptr;
+    int *push_ticket = nullptr;
+    // greedy decode (STORE mode, D = logits rows): each row's largest value
+    // (lowest column on ties) is folded into argmax_key[m] by atomicMax on an
+    // order-preserving 64-bit key; the last block turns the keys into the
+    // column (argmax_out[m], and argmax_log[*argmax_step * M + m] when set)
+    // and/or the (value bits, column) pair (argmax_pair[m], [M + m]), then
+    // clears the keys. Keys and ticket start at zero and end at zero.
+    unsigned long long *argmax_key = nullptr;
+    int *argmax_out = nullptr, *argmax_log = nullptr, *argmax_pair = nullptr;
+    const int *argmax_step = nullptr;
+    int *argmax_ticket = nullptr;
 };
+
+constexpr int TP_MAX_WORLD = 8;
+constexpr int TP_MAX_ROWS = 8;
+constexpr int TP_FLAG_BYTES = 256;
+__host__ __device__ inline size_t tp_buf_bytes(int world, int ld) {
+    return TP_FLAG_BYTES + (size_t)2 * world * TP_MAX_ROWS * ld * sizeof(float);
+}
+__host__ __device__ inline float *tp_slot(char *buf, int world, int ld, int slot, int src) {
+    return (float *)(buf + TP_FLAG_BYTES) + ((size_t)slot * world + src) * TP_MAX_ROWS * ld;
+}
 
 // out[M,N] = op(A)[M,K] * op(B)[N,K]^T, with the epilogue applied per element.
 // A element (m,k) is A[m*lda+k] (a_mn=false, K-major) or A[k*lda+m] (a_mn=true).
@@ -111,6 +146,14 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 // computed in every block; otherwise y goes to ln_out [M, K] first.
 int gemm_ln(const float *X, long ldx, const float *ln_w, const float *ln_b, const float *ln_stats,
             float *ln_out, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi, cudaStream_t s);
+
+// 2-D fp32 TMA descriptor (cached): inner x outer elements, row pitch ld;
+// box0 x box1; K-major operands use the 128B swizzle, MN-major (mn_major)
+// the 128B swizzle with 32-byte atoms. CUtensorMap_st is the driver API's
+// struct, forward-declared at global scope so that files without <cuda.h>
+// can include this header.
+int make_tensor_map(CUtensorMap_st *out, const float *p, long inner, long outer, long ld, int box0, int box1,
+                    bool mn_major);
 
 // Counts of kernel launches issued by this library (for benchmarks).
 extern unsigned long long g_launch_count;

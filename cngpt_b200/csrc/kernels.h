@@ -61,6 +61,9 @@ int decode_advance(int *ctr, cudaStream_t s);
 // when non-null.
 int attention_fwd(const float *qkv, float *out, float *lse, int B, int T, int C, int H,
                   cudaStream_t s);
+// TF32 tcgen05 version (head size 64): ERR_ARG without launching anything
+// when the shapes or alignment do not fit
+int attention_fwd_tc(const float *qkv, float *out, float *lse, int B, int T, int C, int H, cudaStream_t s);
 // dqkv [B, T, 3C] is overwritten with dQ, dK, dV. dout/out are [B, T, C].
 size_t attention_bwd_scratch_bytes(int B, int T, int H);
 int attention_bwd(const float *qkv, const float *out, const float *dout, const float *lse,

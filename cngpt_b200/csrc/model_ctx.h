@@ -54,7 +54,8 @@ struct FastDev {
     size_t gen_cap = 0;
     int *ctr = nullptr;    // [0] position of the incoming token, [1] step index
     float *ln_stats = nullptr;  // [2][8][2] LayerNorm statistics handed between decode GEMVs
-    int *ln_ticket = nullptr;   // [2] last-block tickets of the GEMVs that write them
+    int *ln_ticket = nullptr;   // [4] last-block tickets: [0..1] statistics, [2] greedy argmax
+    unsigned long long *am_key = nullptr;  // [8] greedy argmax keys of the LM-head GEMV
     // one decode step captured as a CUDA graph, reused while the key matches
     cudaStream_t cap_stream = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;

@@ -36,7 +36,8 @@ int last_status() { return g_status; }
 const char *last_message() { return g_msg; }
 
 int check_device_error() {
-    int (*readers[])() = {gemm_take_dev_error, attn_take_dev_error};
+    int (*readers[])() = {gemm_take_dev_error, attn_take_dev_error, tp_take_dev_error,
+                            attn_tc_take_dev_error};
     for (auto rd : readers) {
         int code = rd();
         if (code < 0) {

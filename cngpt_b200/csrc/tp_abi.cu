@@ -21,12 +21,14 @@
 // ranks go to the lower vocabulary index, as in the one-GPU argmax.
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <vector>
 
 #include "abi_common.h"
+#include "common.cuh"
 #include "kernels.h"
 #include "model_ctx.h"
 
@@ -35,6 +37,9 @@ extern "C" {
 }
 
 namespace cg {
+
+CG_DEV_ERROR_READER(tp_take_dev_error)
+
 namespace {
 
 struct TpPlan {
@@ -94,6 +99,16 @@ struct TpState {
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
     cudaGraphExec_t graph = nullptr;
     int graph_B = 0, graph_T = 0, graph_prec = -1;
+    // peer memory for the decode all-reduce: this rank's receive buffer
+    // (tp_buf_bytes), every rank's buffer mapped here (IPC), a device copy of
+    // those pointers, the step counter that numbers the exchanges, tickets
+    char *pbuf = nullptr;
+    char *peer[TP_MAX_WORLD] = {};
+    char **d_peers = nullptr;
+    int *d_step = nullptr, *d_ticket = nullptr;
+    float *d_stats = nullptr;  // [8][2] LayerNorm statistics of x after each exchange
+    unsigned long long *am_key = nullptr;  // [8] greedy keys of the LM-head GEMV
+    int *am_ticket = nullptr;
 
     const float *qkv_w(int l) const { return wbuf + (size_t)l * 3 * Cl * C; }
     const float *qkv_b(int l) const { return wbuf + (size_t)L * 3 * Cl * C + (size_t)l * 3 * Cl; }
@@ -132,6 +147,79 @@ __global__ void tp_argmax_merge_kernel(const int *__restrict__ gath, int B, int 
     }
     next[b] = bi;
     if (log) log[(size_t)(*step_dev) * B + b] = bi;
+}
+
+// x[m, :] = sum over ranks r, in rank order, of the partial row rank r pushed
+// into this rank's receive slot (identical on every rank), then the LayerNorm
+// statistics of x for the next LayerNorm-fused GEMV. One block per row. The
+// peers' flags are awaited with a bounded spin (2 s of %globaltimer); on
+// expiry the block records DEV_ERR_TP_FLAG and leaves x unchanged.
+__global__ void __launch_bounds__(256)
+tp_reduce_kernel(char *__restrict__ buf, int world, int C, const int *__restrict__ step, int nk, int k,
+                 float *__restrict__ x, float *__restrict__ stats) {
+    pdl_trigger();
+    pdl_wait();
+    const unsigned long long ep = (unsigned long long)(*step) * nk + k + 1;
+    __shared__ int ok;
+    __shared__ float red[8][2];
+    if (threadIdx.x == 0) ok = 1;
+    __syncthreads();
+    if ((int)threadIdx.x < world) {
+        const unsigned long long *flag = (const unsigned long long *)buf + threadIdx.x;
+        const uint64_t t0 = globaltimer_ns();
+        for (unsigned it = 0;; ++it) {
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+            if (v >= ep) break;
+            if ((it & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) {
+                record_error(DEV_ERR_TP_FLAG);
+                ok = 0;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (!ok) return;
+    const int m = blockIdx.x, slot = (int)(ep & 1), lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float v[8];
+    float s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int n = threadIdx.x + i * 256;
+        v[i] = 0.f;
+        if (n < C) {
+            float a = 0.f;
+            for (int r = 0; r < world; ++r) a += __ldcg(tp_slot(buf, world, C, slot, r) + (long)m * C + n);
+            v[i] = a;
+            x[(long)m * C + n] = a;
+            s1 += a;
+        }
+    }
+    s1 = warp_sum(s1);
+    if (lane == 0) red[warp][0] = s1;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < 8; ++w) tot += red[w][0];
+    const float mean = tot / (float)C;
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int n = threadIdx.x + i * 256;
+        if (n < C) s2 += (v[i] - mean) * (v[i] - mean);
+    }
+    s2 = warp_sum(s2);
+    if (lane == 0) red[warp][1] = s2;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float var = 0.f;
+        for (int w = 0; w < 8; ++w) var += red[w][1];
+        stats[2 * m] = mean;
+        stats[2 * m + 1] = 1.0f / sqrtf(var / (float)C + 1e-5f);
+    }
+}
+
+__global__ void step_advance_kernel(int *step) {
+    if (threadIdx.x == 0) *step += 1;
 }
 
 void drop_graph(TpState *t) {
@@ -233,8 +321,9 @@ int lm_head(const GPT *m, TpState *t, int B, cudaStream_t s) {
 }
 
 // greedy token of the local logits, merged over ranks -> t->next, t->gen[step]
-int greedy(TpState *t, int B, cudaStream_t s) {
-    CG_TRY(argmax_rows(t->logits, t->ldlog, B, t->p.nv, t->pairs + B, (float *)t->pairs, s));
+// (pairs_ready: the LM-head GEMV already left the local (max, index) pairs)
+int greedy(TpState *t, int B, cudaStream_t s, bool pairs_ready = false) {
+    if (!pairs_ready) CG_TRY(argmax_rows(t->logits, t->ldlog, B, t->p.nv, t->pairs + B, (float *)t->pairs, s));
     const int *g = t->pairs;
     if (t->world > 1) {
         CG_TRY(nccl_allgather_words(t->pairs, t->gath, (size_t)2 * B, t->comm, s));
@@ -277,38 +366,83 @@ int prefill(const GPT *m, TpState *t, const int *tok, int B, int T, bool kv, cud
 // epilogue appends K and V to the cache
 int decode_step(const GPT *m, TpState *t, int B, cudaStream_t s) {
     const GPTWeights *w = &m->params;
-    const int C = t->C, Cl = t->Cl, nf = t->p.nf;
+    const int C = t->C, Cl = t->Cl, nf = t->p.nf, L = t->L;
     float *x = t->xl;
     CG_TRY(embed_fwd_at(t->next, w->wte, w->wpe, x, B, C, t->ctr, s));
     const size_t per = (size_t)t->kv_B * t->kv_T * Cl;
-    for (int l = 0; l < t->L; ++l) {
+    // with peer memory, each row-split GEMV pushes its partial sums to every
+    // rank and tp_reduce_kernel adds them (and the LayerNorm statistics for
+    // the next GEMV); otherwise the partials go through ncclAllReduce
+    const bool push = t->d_peers && B <= TP_MAX_ROWS;
+    auto partial = [&](int k, const float *bias) {
+        GemmEpi e = epi_partial(t, x, C, bias);
+        if (push) {
+            e.push_bufs = t->d_peers;
+            e.push_world = t->world;
+            e.push_rank = t->rank;
+            e.push_ld = C;
+            e.push_k = k;
+            e.push_nk = 2 * L;
+            e.push_step = t->d_step;
+            e.push_ticket = t->d_ticket;
+        }
+        return e;
+    };
+    auto exchange = [&](int k) -> int {
+        if (!push) return allreduce(t, x, (size_t)B * C, s);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(B);
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        CG_CUDA(cudaLaunchKernelEx(&cfg, tp_reduce_kernel, t->pbuf, t->world, C, (const int *)t->d_step, 2 * L, k,
+                                   x, t->d_stats));
+        ++g_launch_count;
+        return OK;
+    };
+    for (int l = 0; l < L; ++l) {
         GemmEpi eq = epi_store(t->qkv, 3 * Cl, t->qkv_b(l));
         eq.kc = t->kc + l * per;
         eq.vc = t->vc + l * per;
         eq.kv_ld = (long)t->kv_T * Cl;
         eq.kv_pos = t->ctr;
         eq.kv_C = Cl;
-        CG_TRY(gemm_ln(x, C, w->ln1_w[l], w->ln1_b[l], nullptr, t->ln, t->qkv_w(l), C, B, 3 * Cl, C, eq, s));
+        CG_TRY(gemm_ln(x, C, w->ln1_w[l], w->ln1_b[l], (push && l > 0) ? t->d_stats : nullptr, t->ln,
+                       t->qkv_w(l), C, B, 3 * Cl, C, eq, s));
         CG_TRY(attention_decode_at(t->qkv, 3L * Cl, t->kc + l * per, t->vc + l * per, t->kv_T, t->ctr,
                                    t->al, B, Cl, t->p.nh, t->dec_part, s));
         CG_TRY(gemm(t->al, Cl, false, w->c_proj_w[l] + (size_t)t->p.h0 * t->hs, C, false, B, C, Cl,
-                    epi_partial(t, x, C, w->c_proj_b[l]), s));
-        CG_TRY(allreduce(t, x, (size_t)B * C, s));
+                    partial(2 * l, w->c_proj_b[l]), s));
+        CG_TRY(exchange(2 * l));
         GemmEpi g;
         g.mode = EPI_GELU;
         g.bias = w->mlp_fc_b[l] + t->p.f0;
         g.D2 = t->hid;
         g.ldd2 = nf;
-        CG_TRY(gemm_ln(x, C, w->ln2_w[l], w->ln2_b[l], nullptr, t->ln, w->mlp_fc_w[l] + (size_t)t->p.f0 * C, C, B, nf,
-                       C, g, s));
+        CG_TRY(gemm_ln(x, C, w->ln2_w[l], w->ln2_b[l], push ? t->d_stats : nullptr, t->ln,
+                       w->mlp_fc_w[l] + (size_t)t->p.f0 * C, C, B, nf, C, g, s));
         CG_TRY(gemm(t->hid, nf, false, w->mlp_proj_w[l] + t->p.f0, 4L * C, false, B, C, nf,
-                    epi_partial(t, x, C, w->mlp_proj_b[l]), s));
-        CG_TRY(allreduce(t, x, (size_t)B * C, s));
+                    partial(2 * l + 1, w->mlp_proj_b[l]), s));
+        CG_TRY(exchange(2 * l + 1));
     }
-    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, nullptr, t->ln, w->wte + (size_t)t->p.v0 * C, C, B, t->p.nv, C,
-                   epi_store(t->logits, t->ldlog, nullptr), s));
-    CG_TRY(greedy(t, B, s));
-    return decode_advance(t->ctr, s);
+    GemmEpi eh = epi_store(t->logits, t->ldlog, nullptr);
+    eh.argmax_key = t->am_key;
+    eh.argmax_pair = t->pairs;
+    eh.argmax_ticket = t->am_ticket;
+    CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, (push && L > 0) ? t->d_stats : nullptr, t->ln,
+                   w->wte + (size_t)t->p.v0 * C, C, B, t->p.nv, C, eh, s));
+    CG_TRY(greedy(t, B, s, true));
+    CG_TRY(decode_advance(t->ctr, s));
+    if (push) {  // the exchange numbering advances once per step
+        step_advance_kernel<<<1, 32, 0, s>>>(t->d_step);
+        ++g_launch_count;
+        CG_CUDA(cudaGetLastError());
+    }
+    return OK;
 }
 
 int capture_step(const GPT *m, TpState *t, int B) {
@@ -343,6 +477,25 @@ void release(TpState *t) {
     cudaStreamSynchronize(g_stream);
     if (t->cap_stream) cudaStreamSynchronize(t->cap_stream);
     drop_graph(t);  // before the communicator its NCCL nodes use
+    if (t->pbuf && t->comm) {
+        // no rank unmaps or frees its receive buffer while a peer may still
+        // write into it: one all-reduce as a barrier first
+        float *one = nullptr;
+        if (dev_alloc((void **)&one, sizeof(float), false) == OK) {
+            nccl_allreduce_sum(one, 1, t->comm, g_stream);
+            cudaStreamSynchronize(g_stream);
+            dev_free(one);
+        }
+    }
+    for (int r = 0; r < TP_MAX_WORLD; ++r)
+        if (t->peer[r] && t->peer[r] != t->pbuf) cudaIpcCloseMemHandle(t->peer[r]);
+    dev_free(t->pbuf);
+    dev_free(t->d_peers);
+    dev_free(t->d_step);
+    dev_free(t->d_ticket);
+    dev_free(t->d_stats);
+    dev_free(t->am_key);
+    dev_free(t->am_ticket);
     float *bufs[] = {t->wbuf, t->x,  t->ln,     t->qkv, t->aout, t->hid, t->mean, t->rstd,
                      t->xl,   t->al, t->logits, t->lgath, t->kc,  t->vc, t->dec_part};
     for (auto b : bufs) dev_free(b);
@@ -353,6 +506,59 @@ void release(TpState *t) {
     if (t->cap_stream) cudaStreamDestroy(t->cap_stream);
     nccl_comm_destroy(t->comm);
     delete t;
+}
+
+// Peer memory for the decode exchange: every rank allocates its receive
+// buffer, the IPC handles are all-gathered over NCCL, and each rank maps the
+// others' buffers (NVLink peer access). Plain loads and stores only.
+int setup_peers(TpState *t) {
+    const size_t bytes = tp_buf_bytes(t->world, t->C);
+    CG_TRY(dev_alloc((void **)&t->pbuf, bytes, false));
+    CG_CUDA(cudaMemset(t->pbuf, 0, bytes));
+    cudaIpcMemHandle_t h;
+    CG_CUDA(cudaIpcGetMemHandle(&h, t->pbuf));
+    static_assert(sizeof(cudaIpcMemHandle_t) % 4 == 0, "handle size");
+    const size_t words = sizeof(cudaIpcMemHandle_t) / 4;
+    int *dh = nullptr;
+    CG_TRY(dev_alloc((void **)&dh, (t->world + 1) * sizeof(cudaIpcMemHandle_t), false));
+    CG_CUDA(cudaMemcpy(dh, &h, sizeof(h), cudaMemcpyHostToDevice));
+    int st = nccl_allgather_words(dh, dh + words, words, t->comm, g_stream);
+    std::vector<cudaIpcMemHandle_t> all(t->world);
+    if (st == OK && cudaStreamSynchronize(g_stream) == cudaSuccess &&
+        cudaMemcpy(all.data(), dh + words, t->world * sizeof(h), cudaMemcpyDeviceToHost) == cudaSuccess) {
+        for (int r = 0; r < t->world && st == OK; ++r) {
+            if (r == t->rank) {
+                t->peer[r] = t->pbuf;
+                continue;
+            }
+            void *p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                set_last_error(ERR_CUDA, "tp_init: mapping rank %d's buffer failed: %s", r,
+                               cudaGetErrorString(cudaGetLastError()));
+                st = ERR_CUDA;
+            }
+            t->peer[r] = (char *)p;
+        }
+    } else if (st == OK) {
+        set_last_error(ERR_CUDA, "tp_init: exchanging buffer handles failed");
+        st = ERR_CUDA;
+    }
+    dev_free(dh);
+    if (st != OK) return st;
+    CG_TRY(dev_alloc((void **)&t->d_peers, TP_MAX_WORLD * sizeof(char *), false));
+    CG_CUDA(cudaMemcpy(t->d_peers, t->peer, TP_MAX_WORLD * sizeof(char *), cudaMemcpyHostToDevice));
+    CG_TRY(dev_alloc((void **)&t->d_step, sizeof(int), false));
+    CG_TRY(dev_alloc((void **)&t->d_ticket, sizeof(int), false));
+    CG_TRY(dev_alloc((void **)&t->d_stats, 2 * TP_MAX_ROWS * sizeof(float), false));
+    CG_CUDA(cudaMemset(t->d_step, 0, sizeof(int)));
+    CG_CUDA(cudaMemset(t->d_ticket, 0, sizeof(int)));
+    // every rank's buffer is zeroed before any rank may push into it
+    float *one = nullptr;
+    CG_TRY(dev_alloc((void **)&one, sizeof(float), false));
+    st = nccl_allreduce_sum(one, 1, t->comm, g_stream);
+    cudaStreamSynchronize(g_stream);
+    dev_free(one);
+    return st;
 }
 
 }  // namespace
@@ -434,6 +640,18 @@ extern "C" int cngpt_cuda_tp_init(GPT *m, const unsigned char id[128], int world
     }
     st = dev_alloc((void **)&t->ctr, 2 * sizeof(int), false);
     if (st != OK) return fail(st);
+    if ((st = dev_alloc((void **)&t->am_key, 8 * sizeof(unsigned long long), false)) != OK ||
+        (st = dev_alloc((void **)&t->am_ticket, sizeof(int), false)) != OK)
+        return fail(st);
+    if (cudaMemset(t->am_key, 0, 8 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(t->am_ticket, 0, sizeof(int)) != cudaSuccess) {
+        set_last_error(ERR_CUDA, "tp_init: clearing the argmax keys failed");
+        return fail(ERR_CUDA);
+    }
+    if (world > 1 && world <= TP_MAX_WORLD && t->C <= 8 * 256 && !getenv("CNGPT_CUDA_TP_NCCL_ONLY")) {
+        st = setup_peers(t);
+        if (st != OK) return fail(st);
+    }
     if (cudaStreamSynchronize(g_stream) != cudaSuccess) {
         set_last_error(ERR_CUDA, "tp_init: %s", cudaGetErrorString(cudaGetLastError()));
         return fail(ERR_CUDA);

@@ -4,6 +4,7 @@ for profilers (ncu) and quick timing.
     python -m cngpt_b200.profile_step [--B 8] [--T 1024] [--layers 12] [--steps 1]
                                       [--warmup 3] [--prec tf32|3xtf32|fp32]
     python -m cngpt_b200.profile_step --gemm M N K [--a-mn] [--b-mn] [--reps 3]
+    python -m cngpt_b200.profile_step --decode xl|small [--B 1] [--T 128] [--new 8]
 
 Token ids live on the device before the first step; nothing else runs.
 """
@@ -39,6 +40,9 @@ def main() -> None:
     ap.add_argument("--b-mn", action="store_true")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--epi", choices=["store", "gelu", "resid", "accum", "gelu_bwd"], default="store")
+    ap.add_argument("--decode", choices=["xl", "small"], help="greedy KV-cache decode of GPT-2 XL / small "
+                    "(device-random weights): prefill B x T, then --new tokens")
+    ap.add_argument("--new", type=int, default=8)
     a = ap.parse_args()
     import torch
     torch.cuda.set_device(0)
@@ -54,13 +58,43 @@ def main() -> None:
         bias = torch.zeros(N, device="cuda")
         mode = {"store": abi.EPI_STORE, "gelu": abi.EPI_GELU, "resid": abi.EPI_RESID,
                 "accum": abi.EPI_ACCUM, "gelu_bwd": abi.EPI_GELU_BWD}[a.epi]
-        for _ in range(a.reps):
+        def one():
             abi.check(lib, lib.cngpt_cuda_gemm(A.data_ptr(), A.shape[1], int(a.a_mn), B.data_ptr(), B.shape[1],
                                                int(a.b_mn), M, N, K, mode, 1.0, D.data_ptr(), N,
                                                bias.data_ptr(), D2.data_ptr(), N, R.data_ptr(), N,
                                                R.data_ptr(), N), "gemm")
+        one()
         abi.check(lib, lib.cngpt_cuda_check(), "sync")
-        print(f"gemm {M}x{N}x{K} done")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(max(a.reps - 1, 1)):
+            one()
+        e1.record()
+        abi.check(lib, lib.cngpt_cuda_check(), "sync")
+        us = e0.elapsed_time(e1) * 1e3 / max(a.reps - 1, 1)
+        print(f"gemm {M}x{N}x{K} a_mn={int(a.a_mn)} b_mn={int(a.b_mn)} epi={a.epi}: {us:.1f} us "
+              f"({2.0 * M * N * K / us / 1e6:.1f} TFLOP/s, CUDA events, back to back)")
+        return
+    if a.decode:
+        L, H, Cm = (48, 25, 1600) if a.decode == "xl" else (12, 12, 768)
+        m = abi.GPT()
+        assert lib.gpt_init(C.byref(m), abi.GPTConfig(L, H, Cm, 50257, 1024, 0.0)) == 0
+        w = torch.randn(m.n_params, device="cuda", generator=torch.Generator("cuda").manual_seed(0)) * 0.02
+        abi.check(lib, lib.cngpt_cuda_copy(C.cast(m.param_buf, C.c_void_p), C.c_void_p(w.data_ptr()),
+                                           m.n_params * 4), "weights")
+        del w
+        prompt = np.arange(a.B * a.T, dtype=np.int32) % 50257
+        out = np.zeros(a.B * a.new, np.int32)
+        fc = abi.FastCtx()
+        lib.fast_init(C.byref(fc))
+        for _ in range(a.reps):
+            t0 = time.perf_counter()
+            abi.check(lib, lib.cngpt_cuda_generate(C.byref(m), C.byref(fc), prompt.ctypes.data, a.B, a.T, a.new,
+                                                   out.ctypes.data), "generate")
+            dt = time.perf_counter() - t0
+        print(f"decode {a.decode} B={a.B} T={a.T} new={a.new}: {dt * 1e3:.2f} ms per generate call")
+        lib.fast_free(C.byref(fc))
+        lib.gpt_free(C.byref(m))
         return
     m = abi.GPT()
     assert lib.gpt_init(C.byref(m), abi.GPTConfig(a.layers, 12, 768, 50257, 1024, 0.0)) == 0

@@ -4,9 +4,12 @@ gathered final-position logits against the reference's gpt_forward_fast
 and the split greedy decode against the one-GPU cngpt_cuda_generate.
 
 Cases: 5 heads at n_embd 320 (uneven 3/2 head split, ragged vocabulary 1001),
-3 heads of size 32 (CUDA-core attention path), and two layers of GPT-2 XL's
-shape (25 heads: 13/12 over two ranks). world = 1 runs on any GPU; world = 2
-needs two GPUs and is skipped on a one-GPU box."""
+3 heads of size 32 (CUDA-core attention path), two layers of GPT-2 XL's
+shape (25 heads: 13/12 over two ranks), and a decode batch of 10 (above the
+8 rows the peer-memory exchange takes, so its partial sums go through
+ncclAllReduce). world = 1 runs on any GPU; world = 2 needs two GPUs and is
+skipped on a one-GPU box. At world = 2 the decode exchanges of batches up to
+8 run through the GEMV's peer-memory push and tp_reduce_kernel."""
 import ctypes as C
 import os
 import subprocess

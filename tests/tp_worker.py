@@ -23,6 +23,8 @@ CASES = {
     "tp5": ((2, 5, 320, 1001, 64, 11), (3, 40), (2, 12, 20)),
     "tp3": ((3, 3, 96, 77, 32, 5), (2, 17), (3, 5, 9)),
     "xl2": ((2, 25, 1600, 50257, 1024, 3), (2, 48), (2, 16, 8)),
+    # batch above the peer-exchange row limit: the decode exchanges go through NCCL
+    "tp5w": ((2, 5, 320, 1001, 64, 11), (3, 40), (10, 6, 5)),
 }
 
 
