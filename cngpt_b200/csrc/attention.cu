@@ -901,6 +901,9 @@ int attention_bwd(const float *qkv, const float *out, const float *dout, const f
     attn_bwd_dot_kernel<<<(int)std::min<long>((rows + 7) / 8, 148L * 64), 256, 0, s>>>(out, dout, D, B,
                                                                                       T, C, H, hs);
     LAUNCH_CHECK();
+    if (precision() == PREC_TF32 && tc_attention_enabled() &&
+        attention_bwd_tc(qkv, dout, lse, D, dqkv, B, T, C, H, s) == OK)
+        return OK;
     if (hs == HS && precision() != PREC_FP32 && mma_ok(C, {qkv, out, dout, dqkv})) {
         const int nt = (T + 63) / 64;
         const int smem_kv = ((2 * TK + 4 * TQ) * LDS + 4 * TQ) * sizeof(float);

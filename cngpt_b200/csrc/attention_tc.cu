@@ -4,15 +4,19 @@
 //
 // One CTA per (query tile of 128 rows, sequence * head), heaviest tiles
 // first. Warp roles:
-//   warp 4  TMA producer: Q once, then K and V tiles of 128 keys into a
-//           two-stage ring (K K-major, V MN-major: V^T is the B operand);
-//   warp 5  MMA issuer (one thread): S = Q K^T into one of two TMEM score
-//           buffers (128 x 128 fp32), and O_t = P V into one of two TMEM
-//           output buffers (128 x 64);
-//   warps 0-3  softmax, one thread per query row (TMEM lane = row): row max
-//           over the scores (pass 1), then P = exp2(S - m) written to shared
-//           memory in the 128B-swizzled K-major layout the MMA reads (pass 2),
-//           and the running output O = O * alpha + O_t kept in registers.
+//   warp 16  TMA producer: Q once, then K and V tiles of 128 keys into a
+//            two-stage ring (K K-major, V MN-major: V^T is the B operand);
+//   warp 17  MMA issuer (one thread): S = Q K^T into one of two TMEM score
+//            buffers (128 x 128 fp32), and O_t = P V into one of two TMEM
+//            output buffers (128 x 64);
+//   warps 0-15  softmax: warp w reads TMEM lane quarter w % 4 (thread = query
+//            row). Every thread takes the row max over all 128 scores of the
+//            tile (TMEM reads are cheap; no exchange between warps), then
+//            writes P = exp2(S - m) for its own 32 keys (columns
+//            32 * (w / 4) .. +31) straight into the 128B-swizzled K-major
+//            layout the MMA reads, and keeps 16 columns of the running output
+//            O = O * alpha + O_t in registers; the four partial row sums of a
+//            row are added in column order at the end.
 // The next tile's S runs on the tensor cores while a tile's softmax runs on
 // the CUDA cores, and each P V product overlaps the next tile's first pass.
 // Every mbarrier wait is bounded (common.cuh); on expiry the CTA records a
@@ -34,8 +38,10 @@ constexpr int V_BYTES = AK * AHS * 4;  // 4 key blocks x 2 dim atoms (32 x 32 ea
 constexpr int P_BYTES = AQ * AK * 4;   // 4 key blocks of 128 rows x 128 B
 constexpr int SM_Q = 0, SM_K = SM_Q + Q_BYTES, SM_V = SM_K + 2 * K_BYTES, SM_P = SM_V + 2 * V_BYTES;
 constexpr int SM_CTL = SM_P + P_BYTES;
-constexpr int ATT_SMEM = SM_CTL + 256 + 1024;
-constexpr int ATT_THREADS = 192;
+constexpr int ATT_SMEM = SM_CTL + 128 + 1024;
+constexpr int SOFT_WARPS = 16;                       // 4 per TMEM lane quarter, 32 key columns each
+constexpr int TMA_WARP = SOFT_WARPS, MMA_WARP = SOFT_WARPS + 1;
+constexpr int ATT_THREADS = (SOFT_WARPS + 2) * 32;
 constexpr int ATT_TMEM_COLS = 512;  // S[2] at columns 0 / 128, O[2] at 256 / 320
 constexpr float LN2f = 0.6931471805599453f;
 
@@ -71,7 +77,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
 
     if (threadIdx.x == 0) {
         mbar_init(&ctl->q_full, 1);
-        mbar_init(&ctl->p_full, 4);
+        mbar_init(&ctl->p_full, SOFT_WARPS);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&ctl->kv_full[s], 1);
             mbar_init(&ctl->kv_empty[s], 1);
@@ -81,7 +87,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
         ctl->abort = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == MMA_WARP) {
         tmem_alloc(&ctl->tmem_base, ATT_TMEM_COLS);
         tmem_relinquish();
     }
@@ -90,7 +96,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
     tc_fence_after();
     const uint32_t tmem = ctl->tmem_base;
 
-    if (warp == 4) {
+    if (warp == TMA_WARP) {
         // ------------------------------------------------------------ TMA
         if (lane == 0) {
             tma_prefetch_desc(&tmQK);
@@ -113,7 +119,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
                                     2 * C + h * AHS + 32 * d, k0 + 32 * kb);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == MMA_WARP) {
         // ------------------------------------------------------------ MMA
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_tf32(AQ, AK, false, false);
@@ -160,24 +166,27 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
             }
         }
     } else {
-        // --------------------------------------------- softmax, row = thread
-        const int r = warp * 32 + lane, q = q0 + r;
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        uint8_t *prow = base + SM_P + (r >> 3) * 1024 + (r & 7) * 128;
-        float o[AHS];
+        // -------------------------- softmax: row = thread, 32 key columns per warp
+        const int quarter = warp & 3, cs = warp >> 2;
+        const int r = quarter * 32 + lane, q = q0 + r;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        uint8_t *pblk = base + SM_P + cs * (P_BYTES / 4) + (r >> 3) * 1024 + (r & 7) * 128;
+        float o[16];
 #pragma unroll
-        for (int d = 0; d < AHS; ++d) o[d] = 0.f;
+        for (int d = 0; d < 16; ++d) o[d] = 0.f;
         float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
         bool ok = true;
-        auto fold = [&](int j) -> bool {  // O = O * alpha_prev + O_t(j)
+        auto fold = [&](int j) -> bool {  // O = O * alpha_prev + O_t(j), this warp's 16 columns
             if (!mbar_wait(&ctl->o_full[j & 1], (j >> 1) & 1, DEV_ERR_ATT_SOFTMAX, abort)) return false;
             tc_fence_after();
+            float v[32];
+            tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(2 * AK + (j & 1) * AHS + (cs >> 1) * 32), v);
+            if (cs & 1) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float v[32];
-                tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(2 * AK + (j & 1) * AHS + c * 32), v);
+                for (int i = 0; i < 16; ++i) o[i] = o[i] * alpha_prev + v[16 + i];
+            } else {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + v[i];
+                for (int i = 0; i < 16; ++i) o[i] = o[i] * alpha_prev + v[i];
             }
             return true;
         };
@@ -187,45 +196,46 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
                 break;
             }
             tc_fence_after();
-            const uint32_t sb = tmem + lane_off + (uint32_t)((j & 1) * AK);
             const bool diag = (j == qt);
-            const int kbase = j * AK;
-            float mx = -INFINITY;
-#pragma unroll 1
+            const int kb0 = j * AK;
+            float own[32];
+            float mraw = -INFINITY;  // max of the unscaled, unmasked scores
+#pragma unroll
             for (int c = 0; c < 4; ++c) {
                 float v[32];
-                tmem_ld_32x32b_x32(sb + c * 32, v);
+                tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((j & 1) * AK + c * 32), v);
+                if (diag) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const bool masked = diag && (kbase + c * 32 + i > q);
-                    mx = fmaxf(mx, masked ? -INFINITY : v[i] * sl2);
+                    for (int i = 0; i < 32; ++i)
+                        if (kb0 + c * 32 + i <= q) mraw = fmaxf(mraw, v[i]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, v[i]);
+                }
+                if (c == cs) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) own[i] = v[i];
                 }
             }
-            const float m_new = fmaxf(m, mx);
+            const float m_new = fmaxf(m, mraw * sl2);  // sl2 > 0: max commutes with the scale
             const float alpha = ex2f(m - m_new);
             // P(j) may only be written once P V of tile j - 1 has read P
             if (j > 0 && !fold(j - 1)) {
                 ok = false;
                 break;
             }
+            const int kfirst = kb0 + cs * 32;
             float rs = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                float v[32];
-                tmem_ld_32x32b_x32(sb + c * 32, v);
-                uint8_t *pblk = prow + c * (P_BYTES / 4);
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {
-                    float p4[4];
+            for (int ch = 0; ch < 8; ++ch) {
+                float p4[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int i = ch * 4 + e;
-                        const bool masked = diag && (kbase + c * 32 + i > q);
-                        p4[e] = masked ? 0.f : ex2f(v[i] * sl2 - m_new);
-                        rs += p4[e];
-                    }
-                    *(float4 *)(pblk + ((ch ^ (r & 7)) << 4)) = make_float4(p4[0], p4[1], p4[2], p4[3]);
+                for (int e = 0; e < 4; ++e) {
+                    const int i = ch * 4 + e;
+                    p4[e] = (diag && kfirst + i > q) ? 0.f : ex2f(own[i] * sl2 - m_new);
+                    rs += p4[e];
                 }
+                *(float4 *)(pblk + ((ch ^ (r & 7)) << 4)) = make_float4(p4[0], p4[1], p4[2], p4[3]);
             }
             l = l * alpha + rs;
             m = m_new;
@@ -236,20 +246,402 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
             __syncwarp();
             if (lane == 0) mbar_arrive(&ctl->p_full);
         }
-        if (ok && fold(nkv - 1) && q < T) {
-            const float inv = 1.0f / l;
-            float *orow = out + (long)(row_base + q) * C + h * AHS;
+        ok = ok && fold(nkv - 1);
+        // row sums: the four column slices of each row, added in slice order,
+        // exchanged through the P buffer (free once the last P V completed)
+        float *lsum = (float *)(base + SM_P);
+        lsum[cs * AQ + r] = l;
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + quarter) : "memory");
+        if (ok && q < T) {
+            const float lt = ((lsum[r] + lsum[AQ + r]) + lsum[2 * AQ + r]) + lsum[3 * AQ + r];
+            const float inv = 1.0f / lt;
+            float *orow = out + (long)(row_base + q) * C + h * AHS + cs * 16;
 #pragma unroll
-            for (int d = 0; d < AHS; d += 4)
+            for (int d = 0; d < 16; d += 4)
                 *(float4 *)(orow + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
-            if (lse) lse[(long)bh * T + q] = m * LN2f + logf(l);
+            if (lse && cs == 0) lse[(long)bh * T + q] = m * LN2f + logf(lt);
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, ATT_TMEM_COLS);
+    }
+}
+
+
+// ================================================================ backward
+// Both passes recompute P = exp2(S * scale * log2e - lse * log2e) from the
+// saved row log-sum-exp, form dS = P (dP - D) with D = rowsum(dO * O), and
+// accumulate in TMEM across their loop - no atomics, deterministic:
+//   attn_bwd_dkdv_tc_kernel  one CTA per (128-key tile, sequence * head),
+//     steps of 64 queries q >= first key: S^T = K Q^T and dP^T = V dO^T
+//     (keys on the TMEM lanes), then dV += P^T dO and dK += dS^T Q with P^T /
+//     dS^T written by the compute warps into shared memory (K-major) and Q,
+//     dO read a second time in the MN-major layout as the B operands;
+//   attn_bwd_dq_tc_kernel  one CTA per (128-query tile, sequence * head),
+//     steps of 64 keys <= the tile's last query: S = Q K^T, dP = dO V^T, then
+//     dQ += dS K (K read MN-major).
+// 16 compute warps (thread = TMEM lane row, 16 of the 64 step columns per
+// warp), one TMA warp, one MMA warp; every wait bounded.
+constexpr int BQS = 64;                               // step width (queries or keys)
+constexpr int BT_HALF = BQS * 64 * 4;                 // 16 KB: a 64-row x 64-dim operand
+constexpr int BT_FULL = 128 * 64 * 4;                 // 32 KB: a 128-row operand
+constexpr int BT_DS = 128 * BQS * 4;                  // 32 KB: P^T / dS^T or dS tile
+// dK/dV: K, V resident; stages of {Q, dO} K-major + {Q, dO} MN-major
+constexpr int KV_SM_K = 0, KV_SM_V = BT_FULL, KV_SM_STAGE = 2 * BT_FULL, KV_STAGE = 4 * BT_HALF;
+constexpr int KV_SM_DS = KV_SM_STAGE + 2 * KV_STAGE, KV_SM_CTL = KV_SM_DS + BT_DS;
+constexpr int KV_SMEM = KV_SM_CTL + 128 + 1024;
+// dQ: Q, dO resident; stages of {K, V} K-major + K MN-major
+constexpr int DQ_SM_Q = 0, DQ_SM_DO = BT_FULL, DQ_SM_STAGE = 2 * BT_FULL, DQ_STAGE = 3 * BT_HALF;
+constexpr int DQ_SM_DS = DQ_SM_STAGE + 2 * DQ_STAGE, DQ_SM_CTL = DQ_SM_DS + BT_DS;
+constexpr int DQ_SMEM = DQ_SM_CTL + 128 + 1024;
+constexpr int BWD_WARPS = 16, BWD_TMA = 16, BWD_MMA = 17, BWD_THREADS = 18 * 32;
+constexpr float LOG2Ef = 1.4426950408889634f;
+
+struct BwdCtl {
+    uint64_t in_full, st_full[2], st_empty[2], sp_full[2], a_full, a_done, b_full, b_done, acc_done;
+    uint32_t tmem_base;
+    int abort;
+};
+
+enum : int { DEV_ERR_ATTB_TMA = 311, DEV_ERR_ATTB_MMA = 312, DEV_ERR_ATTB_CMP = 313 };
+
+__device__ __forceinline__ void bwd_init(BwdCtl *ctl) {
+    mbar_init(&ctl->in_full, 1);
+    for (int s = 0; s < 2; ++s) {
+        mbar_init(&ctl->st_full[s], 1);
+        mbar_init(&ctl->st_empty[s], 1);
+        mbar_init(&ctl->sp_full[s], 1);
+    }
+    mbar_init(&ctl->a_full, BWD_WARPS);
+    mbar_init(&ctl->a_done, 1);
+    mbar_init(&ctl->b_full, BWD_WARPS);
+    mbar_init(&ctl->b_done, 1);
+    mbar_init(&ctl->acc_done, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+}
+
+// 16 values of one row into the K-major 128B-swizzled tile (rows of 128 B =
+// 32 floats; this writes floats [col0, col0 + 16) of row r, col0 % 16 == 0)
+__device__ __forceinline__ void put_row16(uint8_t *tile, int r, int col0, const float (&v)[16]) {
+    uint8_t *row = tile + (col0 >> 5) * (128 * 128) + (r >> 3) * 1024 + (r & 7) * 128;
+    const int ch0 = (col0 & 31) >> 2;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *(float4 *)(row + (((ch0 + c) ^ (r & 7)) << 4)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
+// D (+)= A B^T over K = 64 (two 32-wide k-blocks, four tf32 MMAs each)
+// A: 128 rows K-major at a (k-block stride a_kb); B: K-major rows at b
+// (k-block stride b_kb) or MN-major at b (k-block stride 8192, dim atoms 4096)
+__device__ __forceinline__ void mma_k64(uint32_t d, uint32_t a, int a_kb, uint32_t b, int b_kb, bool b_mn,
+                                        uint32_t idesc, bool acc) {
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t da = smem_desc(a + kb * a_kb + kk * 32, 16, 1024, 2);
+            const uint64_t db = b_mn ? smem_desc(b + kb * 8192 + kk * 1024, 4096, 512, 1)
+                                     : smem_desc(b + kb * b_kb + kk * 32, 16, 1024, 2);
+            mma_tf32(d, da, db, idesc, (acc || kb || kk) ? 1u : 0u);
+        }
+}
+
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_constant__ CUtensorMap tmQK64,
+                        const __grid_constant__ CUtensorMap tmMN, const __grid_constant__ CUtensorMap tmDO64,
+                        const __grid_constant__ CUtensorMap tmDOMN, const float *__restrict__ lse,
+                        const float *__restrict__ Dd, float *__restrict__ dqkv, int T, int C, int H, float sl2,
+                        float scale) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    BwdCtl *ctl = (BwdCtl *)(base + KV_SM_CTL);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nkt = (T + 127) / 128, BH = gridDim.x / nkt;
+    const int kt = (int)(blockIdx.x / BH), bh = blockIdx.x % BH;  // light tiles (late keys) last
+    const int b = bh / H, h = bh % H, row_base = b * T, k0 = kt * 128;
+    const int ns = (T - k0 + BQS - 1) / BQS;  // query steps q0 = k0 + 64 s
+    volatile int *abort = &ctl->abort;
+    auto stage = [&](int st) { return base + KV_SM_STAGE + st * KV_STAGE; };  // Qk, dOk, Qmn, dOmn
+    if (threadIdx.x == 0) bwd_init(ctl);
+    if (warp == BWD_MMA) {
+        tmem_alloc(&ctl->tmem_base, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+    // TMEM: S^T[2] at 0 / 64, dP^T[2] at 128 / 192, dV at 256, dK at 320
+    if (warp == BWD_TMA) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&ctl->in_full, 2 * BT_FULL);
+            for (int kb = 0; kb < 2; ++kb) {
+                tma_load_2d(base + KV_SM_K + kb * (BT_FULL / 2), &tmQK128, &ctl->in_full, C + h * 64 + 32 * kb,
+                            row_base + k0);
+                tma_load_2d(base + KV_SM_V + kb * (BT_FULL / 2), &tmQK128, &ctl->in_full, 2 * C + h * 64 + 32 * kb,
+                            row_base + k0);
+            }
+            for (int s = 0; s < ns; ++s) {
+                const int st = s & 1;
+                if (!mbar_wait(&ctl->st_empty[st], ((s >> 1) & 1) ^ 1u, DEV_ERR_ATTB_TMA, abort)) break;
+                mbar_arrive_expect_tx(&ctl->st_full[st], KV_STAGE);
+                const int q0 = row_base + k0 + s * BQS;
+                uint8_t *sg = stage(st);
+                for (int kb = 0; kb < 2; ++kb) {
+                    tma_load_2d(sg + kb * (BT_HALF / 2), &tmQK64, &ctl->st_full[st], h * 64 + 32 * kb, q0);
+                    tma_load_2d(sg + BT_HALF + kb * (BT_HALF / 2), &tmDO64, &ctl->st_full[st], h * 64 + 32 * kb, q0);
+                    for (int d = 0; d < 2; ++d) {
+                        tma_load_2d(sg + 2 * BT_HALF + kb * 8192 + d * 4096, &tmMN, &ctl->st_full[st],
+                                    h * 64 + 32 * d, q0 + 32 * kb);
+                        tma_load_2d(sg + 3 * BT_HALF + kb * 8192 + d * 4096, &tmDOMN, &ctl->st_full[st],
+                                    h * 64 + 32 * d, q0 + 32 * kb);
+                    }
+                }
+            }
+        }
+    } else if (warp == BWD_MMA) {
+        if (lane == 0) {
+            constexpr uint32_t id_sp = idesc_tf32(128, BQS, false, false);
+            constexpr uint32_t id_acc = idesc_tf32(128, 64, false, true);
+            const uint32_t ka = smem_u32(base + KV_SM_K), va = smem_u32(base + KV_SM_V), dsa = smem_u32(base + KV_SM_DS);
+            auto issue_sp = [&](int s) {
+                const uint32_t sg = smem_u32(stage(s & 1));
+                mma_k64(tmem + (s & 1) * 64, ka, BT_FULL / 2, sg, BT_HALF / 2, false, id_sp, false);
+                mma_k64(tmem + 128 + (s & 1) * 64, va, BT_FULL / 2, sg + BT_HALF, BT_HALF / 2, false, id_sp, false);
+                mma_commit(&ctl->sp_full[s & 1]);
+            };
+            bool ok = mbar_wait(&ctl->in_full, 0, DEV_ERR_ATTB_MMA, abort) &&
+                      mbar_wait(&ctl->st_full[0], 0, DEV_ERR_ATTB_MMA, abort);
+            if (ok) {
+                tc_fence_after();
+                issue_sp(0);
+            }
+            for (int s = 0; ok && s < ns; ++s) {
+                if (s + 1 < ns) {
+                    if (!mbar_wait(&ctl->st_full[(s + 1) & 1], ((s + 1) >> 1) & 1, DEV_ERR_ATTB_MMA, abort)) break;
+                    tc_fence_after();
+                    issue_sp(s + 1);
+                }
+                const uint32_t sg = smem_u32(stage(s & 1));
+                if (!mbar_wait(&ctl->a_full, s & 1, DEV_ERR_ATTB_MMA, abort)) break;  // P^T written
+                tc_fence_after();
+                mma_k64(tmem + 256, dsa, BT_DS / 2, sg + 3 * BT_HALF, 0, true, id_acc, s > 0);  // dV += P^T dO
+                mma_commit(&ctl->a_done);
+                if (!mbar_wait(&ctl->b_full, s & 1, DEV_ERR_ATTB_MMA, abort)) break;  // dS^T written
+                tc_fence_after();
+                mma_k64(tmem + 320, dsa, BT_DS / 2, sg + 2 * BT_HALF, 0, true, id_acc, s > 0);  // dK += dS^T Q
+                mma_commit(&ctl->b_done);
+                mma_commit(&ctl->st_empty[s & 1]);
+            }
+            mma_commit(&ctl->acc_done);
+        }
+    } else {
+        const int quarter = warp & 3, cq = warp >> 2;
+        const int r = quarter * 32 + lane, key = k0 + r;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        uint8_t *ds = base + KV_SM_DS;
+        const float *lse_bh = lse + (long)bh * T, *D_bh = Dd + (long)bh * T;
+        bool ok = true;
+        for (int s = 0; s < ns; ++s) {
+            if (!mbar_wait(&ctl->sp_full[s & 1], (s >> 1) & 1, DEV_ERR_ATTB_CMP, abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sv[16], dp[16], pv[16], dsv[16];
+            tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)((s & 1) * 64 + cq * 16), sv);
+            tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)(128 + (s & 1) * 64 + cq * 16), dp);
+            const int qf = k0 + s * BQS + cq * 16;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const int q = qf + c;
+                const bool valid = key <= q && q < T;
+                const float l2 = valid ? lse_bh[q] * LOG2Ef : 0.f, dd = valid ? D_bh[q] : 0.f;
+                pv[c] = valid ? ex2f(sv[c] * sl2 - l2) : 0.f;
+                dsv[c] = pv[c] * (dp[c] - dd);
+            }
+            // the dS^T of the previous step must have been read (dK MMA done)
+            if (s > 0 && !mbar_wait(&ctl->b_done, (s - 1) & 1, DEV_ERR_ATTB_CMP, abort)) {
+                ok = false;
+                break;
+            }
+            put_row16(ds, r, cq * 16, pv);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->a_full);
+            if (!mbar_wait(&ctl->a_done, s & 1, DEV_ERR_ATTB_CMP, abort)) {  // dV MMA read P^T
+                ok = false;
+                break;
+            }
+            put_row16(ds, r, cq * 16, dsv);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->b_full);
+        }
+        if (ok && mbar_wait(&ctl->acc_done, 0, DEV_ERR_ATTB_CMP, abort)) {
+            tc_fence_after();
+            float dv[16], dk[16];
+            tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)(256 + cq * 16), dv);
+            tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)(320 + cq * 16), dk);
+            if (key < T) {
+                float *row = dqkv + (long)(row_base + key) * 3 * C + h * 64 + cq * 16;
+#pragma unroll
+                for (int c = 0; c < 16; c += 4) {
+                    *(float4 *)(row + C + c) = make_float4(dk[c] * scale, dk[c + 1] * scale, dk[c + 2] * scale,
+                                                           dk[c + 3] * scale);
+                    *(float4 *)(row + 2 * C + c) = make_float4(dv[c], dv[c + 1], dv[c + 2], dv[c + 3]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == BWD_MMA) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_constant__ CUtensorMap tmQK64,
+                      const __grid_constant__ CUtensorMap tmMN, const __grid_constant__ CUtensorMap tmDO128,
+                      const float *__restrict__ lse, const float *__restrict__ Dd, float *__restrict__ dqkv, int T,
+                      int C, int H, float sl2, float scale) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    BwdCtl *ctl = (BwdCtl *)(base + DQ_SM_CTL);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nqt = (T + 127) / 128, BH = gridDim.x / nqt;
+    const int qt = nqt - 1 - (int)(blockIdx.x / BH), bh = blockIdx.x % BH;  // heavy tiles first
+    const int b = bh / H, h = bh % H, row_base = b * T, q0 = qt * 128;
+    const int ns = (min(T, q0 + 128) + BQS - 1) / BQS;  // key steps k0 = 64 s
+    volatile int *abort = &ctl->abort;
+    auto stage = [&](int st) { return base + DQ_SM_STAGE + st * DQ_STAGE; };  // Kk, Vk, Kmn
+    if (threadIdx.x == 0) bwd_init(ctl);
+    if (warp == BWD_MMA) {
+        tmem_alloc(&ctl->tmem_base, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ctl->tmem_base;
+    // TMEM: S[2] at 0 / 64, dP[2] at 128 / 192, dQ at 256
+    if (warp == BWD_TMA) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&ctl->in_full, 2 * BT_FULL);
+            for (int kb = 0; kb < 2; ++kb) {
+                tma_load_2d(base + DQ_SM_Q + kb * (BT_FULL / 2), &tmQK128, &ctl->in_full, h * 64 + 32 * kb,
+                            row_base + q0);
+                tma_load_2d(base + DQ_SM_DO + kb * (BT_FULL / 2), &tmDO128, &ctl->in_full, h * 64 + 32 * kb,
+                            row_base + q0);
+            }
+            for (int s = 0; s < ns; ++s) {
+                const int st = s & 1;
+                if (!mbar_wait(&ctl->st_empty[st], ((s >> 1) & 1) ^ 1u, DEV_ERR_ATTB_TMA, abort)) break;
+                mbar_arrive_expect_tx(&ctl->st_full[st], DQ_STAGE);
+                const int k0 = row_base + s * BQS;
+                uint8_t *sg = stage(st);
+                for (int kb = 0; kb < 2; ++kb) {
+                    tma_load_2d(sg + kb * (BT_HALF / 2), &tmQK64, &ctl->st_full[st], C + h * 64 + 32 * kb, k0);
+                    tma_load_2d(sg + BT_HALF + kb * (BT_HALF / 2), &tmQK64, &ctl->st_full[st],
+                                2 * C + h * 64 + 32 * kb, k0);
+                    for (int d = 0; d < 2; ++d)
+                        tma_load_2d(sg + 2 * BT_HALF + kb * 8192 + d * 4096, &tmMN, &ctl->st_full[st],
+                                    C + h * 64 + 32 * d, k0 + 32 * kb);
+                }
+            }
+        }
+    } else if (warp == BWD_MMA) {
+        if (lane == 0) {
+            constexpr uint32_t id_sp = idesc_tf32(128, BQS, false, false);
+            constexpr uint32_t id_acc = idesc_tf32(128, 64, false, true);
+            const uint32_t qa = smem_u32(base + DQ_SM_Q), doa = smem_u32(base + DQ_SM_DO);
+            const uint32_t dsa = smem_u32(base + DQ_SM_DS);
+            auto issue_sp = [&](int s) {
+                const uint32_t sg = smem_u32(stage(s & 1));
+                mma_k64(tmem + (s & 1) * 64, qa, BT_FULL / 2, sg, BT_HALF / 2, false, id_sp, false);
+                mma_k64(tmem + 128 + (s & 1) * 64, doa, BT_FULL / 2, sg + BT_HALF, BT_HALF / 2, false, id_sp, false);
+                mma_commit(&ctl->sp_full[s & 1]);
+            };
+            bool ok = mbar_wait(&ctl->in_full, 0, DEV_ERR_ATTB_MMA, abort) &&
+                      mbar_wait(&ctl->st_full[0], 0, DEV_ERR_ATTB_MMA, abort);
+            if (ok) {
+                tc_fence_after();
+                issue_sp(0);
+            }
+            for (int s = 0; ok && s < ns; ++s) {
+                if (s + 1 < ns) {
+                    if (!mbar_wait(&ctl->st_full[(s + 1) & 1], ((s + 1) >> 1) & 1, DEV_ERR_ATTB_MMA, abort)) break;
+                    tc_fence_after();
+                    issue_sp(s + 1);
+                }
+                if (!mbar_wait(&ctl->a_full, s & 1, DEV_ERR_ATTB_MMA, abort)) break;  // dS written
+                tc_fence_after();
+                mma_k64(tmem + 256, dsa, BT_DS / 2, smem_u32(stage(s & 1)) + 2 * BT_HALF, 0, true, id_acc, s > 0);
+                mma_commit(&ctl->a_done);
+                mma_commit(&ctl->st_empty[s & 1]);
+            }
+            mma_commit(&ctl->acc_done);
+        }
+    } else {
+        const int quarter = warp & 3, cq = warp >> 2;
+        const int r = quarter * 32 + lane, q = q0 + r;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        uint8_t *ds = base + DQ_SM_DS;
+        const bool qv = q < T;
+        const float l2 = qv ? lse[(long)bh * T + q] * LOG2Ef : 0.f, dd = qv ? Dd[(long)bh * T + q] : 0.f;
+        bool ok = true;
+        for (int s = 0; s < ns; ++s) {
+            if (!mbar_wait(&ctl->sp_full[s & 1], (s >> 1) & 1, DEV_ERR_ATTB_CMP, abort)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float sv[16], dp[16], dsv[16];
+            tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)((s & 1) * 64 + cq * 16), sv);
+            tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)(128 + (s & 1) * 64 + cq * 16), dp);
+            const int kf = s * BQS + cq * 16;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const bool valid = qv && kf + c <= q;
+                const float p = valid ? ex2f(sv[c] * sl2 - l2) : 0.f;
+                dsv[c] = p * (dp[c] - dd);
+            }
+            if (s > 0 && !mbar_wait(&ctl->a_done, (s - 1) & 1, DEV_ERR_ATTB_CMP, abort)) {  // dQ MMA read dS
+                ok = false;
+                break;
+            }
+            put_row16(ds, r, cq * 16, dsv);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->a_full);
+        }
+        if (ok && mbar_wait(&ctl->acc_done, 0, DEV_ERR_ATTB_CMP, abort)) {
+            tc_fence_after();
+            float dq[16];
+            tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)(256 + cq * 16), dq);
+            if (qv) {
+                float *row = dqkv + (long)(row_base + q) * 3 * C + h * 64 + cq * 16;
+#pragma unroll
+                for (int c = 0; c < 16; c += 4)
+                    *(float4 *)(row + c) = make_float4(dq[c] * scale, dq[c + 1] * scale, dq[c + 2] * scale,
+                                                       dq[c + 3] * scale);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == BWD_MMA) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
     }
 }
 
@@ -275,6 +667,40 @@ int attention_fwd_tc(const float *qkv, float *out, float *lse, int B, int T, int
     const int nqt = (T + AQ - 1) / AQ;
     const float sl2 = (1.0f / sqrtf((float)AHS)) * 1.4426950408889634f;
     attn_fwd_tc_kernel<<<nqt * B * H, ATT_THREADS, ATT_SMEM, s>>>(tqk, tv, out, lse, T, C, H, sl2);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    return OK;
+}
+
+// TF32 causal attention backward on tcgen05 (head size 64): D must already
+// hold rowsum(dO * O) per (sequence * head, row). ERR_ARG without launching
+// when the shapes or alignment do not fit.
+int attention_bwd_tc(const float *qkv, const float *dout, const float *lse, const float *D, float *dqkv, int B,
+                     int T, int C, int H, cudaStream_t s) {
+    auto al = [](const void *p) { return ((uintptr_t)p % 16) == 0; };
+    if (C / H != 64 || C % H != 0 || C % 4 != 0 || !al(qkv) || !al(dout) || !al(dqkv)) return ERR_ARG;
+    CUtensorMap qk128, qk64, mn, do128, do64, domn;
+    const long rows = (long)B * T;
+    CG_TRY(make_tensor_map(&qk128, qkv, 3L * C, rows, 3L * C, 32, 128, false));
+    CG_TRY(make_tensor_map(&qk64, qkv, 3L * C, rows, 3L * C, 32, 64, false));
+    CG_TRY(make_tensor_map(&mn, qkv, 3L * C, rows, 3L * C, 32, 32, true));
+    CG_TRY(make_tensor_map(&do128, dout, C, rows, C, 32, 128, false));
+    CG_TRY(make_tensor_map(&do64, dout, C, rows, C, 32, 64, false));
+    CG_TRY(make_tensor_map(&domn, dout, C, rows, C, 32, 32, true));
+    static bool attr = false;
+    if (!attr) {
+        CG_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KV_SMEM));
+        CG_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM));
+        attr = true;
+    }
+    const int nt = (T + 127) / 128;
+    const float scale = 0.125f, sl2 = scale * LOG2Ef;  // 1 / sqrt(64)
+    attn_bwd_dkdv_tc_kernel<<<nt * B * H, BWD_THREADS, KV_SMEM, s>>>(qk128, qk64, mn, do64, domn, lse, D, dqkv, T,
+                                                                     C, H, sl2, scale);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    attn_bwd_dq_tc_kernel<<<nt * B * H, BWD_THREADS, DQ_SMEM, s>>>(qk128, qk64, mn, do128, lse, D, dqkv, T, C, H,
+                                                                   sl2, scale);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
     return OK;

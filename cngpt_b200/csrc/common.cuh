@@ -171,6 +171,21 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 16 consecutive fp32 columns
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Shared-memory matrix descriptor (tcgen05 "version 1": start address, leading
 // and stride byte offsets, all >> 4; layout type in bits 61-63).
 //   layout 2 = 128B swizzle (16B chunks; K-major operands: 8-row atoms of
@@ -269,14 +284,26 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
         ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-    const float k = 0.7978845608028654f, c = 0.044715f;
-    return 0.5f * x * (1.0f + tanhf(k * (x + c * x * x * x)));
+// tanh-GELU (src/ops.c:357-415): y = 0.5 x (1 + tanh(k (x + c x^3))).
+// `fast` selects tanh(u) = 1 - 2 / (2^(2u log2 e) + 1) on ex2.approx and a
+// fast reciprocal (absolute error ~1e-7, enough for the TF32 mode whose GEMM
+// inputs already carry 1e-3); otherwise the accurate tanhf.
+__device__ __forceinline__ float tanh_fast(float u) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * 2.885390081777927f));
+    return 1.0f - __fdividef(2.0f, e + 1.0f);
 }
 
-__device__ __forceinline__ float gelu_tanh_grad(float x) {
+__device__ __forceinline__ float gelu_tanh(float x, bool fast = false) {
     const float k = 0.7978845608028654f, c = 0.044715f;
-    float th = tanhf(k * (x + c * x * x * x));
+    const float u = k * (x + c * x * x * x);
+    return 0.5f * x * (1.0f + (fast ? tanh_fast(u) : tanhf(u)));
+}
+
+__device__ __forceinline__ float gelu_tanh_grad(float x, bool fast = false) {
+    const float k = 0.7978845608028654f, c = 0.044715f;
+    const float u = k * (x + c * x * x * x);
+    const float th = fast ? tanh_fast(u) : tanhf(u);
     return 0.5f * (1.0f + th) + 0.5f * x * (1.0f - th * th) * k * (1.0f + 3.0f * c * x * x);
 }
 

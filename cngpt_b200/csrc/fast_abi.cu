@@ -191,12 +191,9 @@ int decode_step(const GPT *m, FastCtx *f, FastDev *d, int B, cudaStream_t s) {
     // LM head with the greedy argmax folded into its epilogue
     GemmEpi eh = epi_store(f->logits, V, nullptr);
     eh.argmax_key = d->am_key;
-    eh.argmax_out = d->next;
-    eh.argmax_log = d->gen;
-    eh.argmax_step = d->ctr + 1;
-    eh.argmax_ticket = d->ln_ticket + 2;
     CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, (st && L > 0) ? st_mlp : nullptr, f->ln, w->wte, C, B, V, C, eh, s));
-    return decode_advance(d->ctr, s);
+    // tokens of this step -> next input and the log; counters advance
+    return greedy_finalize(d->am_key, B, d->next, d->gen, d->ctr + 1, nullptr, d->ctr, s);
 }
 
 // Capture one decode step on the FastDev's own stream (reused while the model,

@@ -90,7 +90,7 @@ __device__ __forceinline__ void epi_apply(const GemmEpi &e, long m, int n, float
         case EPI_GELU:
             a += bias;
             if (e.D) e.D[m * e.ldd + n] = a;
-            e.D2[m * e.ldd2 + n] = gelu_tanh(a);
+            e.D2[m * e.ldd2 + n] = gelu_tanh(a, e.fast_act);
             break;
         case EPI_RESID:
             a += bias;
@@ -98,7 +98,7 @@ __device__ __forceinline__ void epi_apply(const GemmEpi &e, long m, int n, float
             e.D2[m * e.ldd2 + n] = aux + a;
             break;
         case EPI_GELU_BWD:
-            e.D[m * e.ldd + n] = a * gelu_tanh_grad(aux);
+            e.D[m * e.ldd + n] = a * gelu_tanh_grad(aux, e.fast_act);
             break;
     }
 }
@@ -127,6 +127,7 @@ __device__ __forceinline__ void store_block(const GemmEpi &ep, float *stile, int
     if (ep.vec4 && n + 3 < N) {
         const float4 b4 = ep.bias ? *(const float4 *)(ep.bias + n) : make_float4(0.f, 0.f, 0.f, 0.f);
         const float al = ep.alpha;
+        const bool fa = ep.fast_act != 0;
         auto run = [&](auto op) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -158,7 +159,7 @@ __device__ __forceinline__ void store_block(const GemmEpi &ep, float *stile, int
                     a = make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
                     if (ep.D) *(float4 *)(ep.D + m * ep.ldd + n) = a;
                     *(float4 *)(ep.D2 + m * ep.ldd2 + n) =
-                        make_float4(gelu_tanh(a.x), gelu_tanh(a.y), gelu_tanh(a.z), gelu_tanh(a.w));
+                        make_float4(gelu_tanh(a.x, fa), gelu_tanh(a.y, fa), gelu_tanh(a.z, fa), gelu_tanh(a.w, fa));
                 });
                 break;
             case EPI_RESID:
@@ -174,8 +175,8 @@ __device__ __forceinline__ void store_block(const GemmEpi &ep, float *stile, int
                 run([&](long m, float4 a) {
                     const float4 g = *(const float4 *)(ep.G + m * ep.ldg + n);
                     *(float4 *)(ep.D + m * ep.ldd + n) =
-                        make_float4(a.x * gelu_tanh_grad(g.x), a.y * gelu_tanh_grad(g.y),
-                                    a.z * gelu_tanh_grad(g.z), a.w * gelu_tanh_grad(g.w));
+                        make_float4(a.x * gelu_tanh_grad(g.x, fa), a.y * gelu_tanh_grad(g.y, fa),
+                                    a.z * gelu_tanh_grad(g.z, fa), a.w * gelu_tanh_grad(g.w, fa));
                 });
                 break;
         }
@@ -905,35 +906,16 @@ gemv_kernel(const float *__restrict__ X, long ldx, const float *__restrict__ W, 
         }
     }
     if (epi.argmax_key) {
-        // rows m of this block's NV values sit in lanes t = r * MT + m of warp 0
-        __shared__ int alast;
+        // rows m of this block's NV values sit in lanes t = r * MT + m of warp
+        // 0; a block only issues the atomic when it beats the current key
         if (warp == 0) {
 #pragma unroll
             for (int o = MT; o < 32; o <<= 1) {
                 const unsigned long long other = __shfl_xor_sync(0xffffffffu, amkey, o);
                 amkey = other > amkey ? other : amkey;
             }
-            if (t < MT && t < M && amkey) atomicMax(epi.argmax_key + t, amkey);
-        }
-        __threadfence();
-        __syncthreads();
-        if (t == 0) alast = atomicAdd(epi.argmax_ticket, 1) == (int)gridDim.x - 1;
-        __syncthreads();
-        if (alast) {
-            __threadfence();
-            if (t < M) {
-                const unsigned long long k = atomicExch(epi.argmax_key + t, 0ull);
-                const uint32_t ord = (uint32_t)(k >> 32);
-                const int col = (int)(0xFFFFFFFFu - (uint32_t)k);
-                const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
-                if (epi.argmax_out) epi.argmax_out[t] = col;
-                if (epi.argmax_log) epi.argmax_log[(long)(*epi.argmax_step) * M + t] = col;
-                if (epi.argmax_pair) {
-                    epi.argmax_pair[t] = (int)u;
-                    epi.argmax_pair[M + t] = col;
-                }
-            }
-            if (t == 0) *epi.argmax_ticket = 0;
+            if (t < MT && t < M && amkey > *(volatile unsigned long long *)(epi.argmax_key + t))
+                atomicMax(epi.argmax_key + t, amkey);
         }
     }
     if (epi.ln_stats_out) {
@@ -1388,14 +1370,15 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
                   (!epi.R || epi.ldr % 4 == 0) && (!epi.G || epi.ldg % 4 == 0);
     }
     const int prec = precision();
+    e2.fast_act = prec == PREC_TF32;
     if (gemv_ok(A, lda, a_mn, B, ldb, b_mn, M, N, K, epi) &&
-        ((long)N * K >= (1L << 16) || epi.kc || epi.ln_stats_out || epi.push_bufs))
+        ((long)N * K >= (1L << 16) || epi.kc || epi.ln_stats_out || epi.push_bufs || epi.argmax_key))
         return dispatch_gemv<false>(A, lda, B, ldb, M, N, K, epi, nullptr, nullptr, nullptr, s);
     if (epi.push_bufs) {
         set_last_error(ERR_ARG, "gemm: peer push needs the GEMV path (M <= 8, aligned K-major operands)");
         return ERR_ARG;
     }
-    if (epi.argmax_key) {  // greedy step outside the GEMV path: the GEMM, then an argmax pass
+    if (epi.argmax_key) {  // greedy step outside the GEMV path: the GEMM, then the row keys
         GemmEpi e3 = epi;
         e3.argmax_key = nullptr;
         CG_TRY(gemm(A, lda, a_mn, B, ldb, b_mn, M, N, K, e3, s));
@@ -1403,9 +1386,7 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
             set_last_error(ERR_ARG, "gemm: the fused argmax needs STORE mode");
             return ERR_ARG;
         }
-        if (epi.argmax_pair) CG_TRY(argmax_rows(epi.D, epi.ldd, M, N, epi.argmax_pair + M, (float *)epi.argmax_pair, s));
-        if (epi.argmax_out) CG_TRY(argmax_log(epi.D, epi.ldd, M, N, epi.argmax_out, epi.argmax_log, epi.argmax_step, s));
-        return OK;
+        return argmax_keys(epi.D, epi.ldd, M, N, epi.argmax_key, s);
     }
     if (epi.ln_stats_out) {  // statistics requested outside the GEMV path: a separate pass
         GemmEpi e3 = epi;

@@ -82,6 +82,7 @@ struct GemmEpi {
     const float *G = nullptr;
     long ldg = 0;
     int vec4 = 0;  // set by gemm(): every pointer 16B-aligned and every pitch % 4 == 0
+    int fast_act = 0;  // set by gemm() in TF32 mode: GELU epilogues use tanh_fast
     // KV-cache decode (STORE mode, D = packed qkv rows): the K and V columns
     // [kv_C, 3 kv_C) are also written to kc / vc at position *kv_pos:
     // kc[m * kv_ld + pos * kv_C + (n - kv_C)], vc likewise for n >= 2 kv_C
@@ -106,14 +107,9 @@ struct GemmEpi {
     int *push_ticket = nullptr;
     // greedy decode (STORE mode, D = logits rows): each row's largest value
     // (lowest column on ties) is folded into argmax_key[m] by atomicMax on an
-    // order-preserving 64-bit key; the last block turns the keys into the
-    // column (argmax_out[m], and argmax_log[*argmax_step * M + m] when set)
-    // and/or the (value bits, column) pair (argmax_pair[m], [M + m]), then
-    // clears the keys. Keys and ticket start at zero and end at zero.
+    // order-preserving 64-bit key (keys start at zero); greedy_finalize()
+    // turns the keys into tokens and clears them
     unsigned long long *argmax_key = nullptr;
-    int *argmax_out = nullptr, *argmax_log = nullptr, *argmax_pair = nullptr;
-    const int *argmax_step = nullptr;
-    int *argmax_ticket = nullptr;
 };
 
 constexpr int TP_MAX_WORLD = 8;

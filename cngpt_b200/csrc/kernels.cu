@@ -523,6 +523,56 @@ __global__ void argmax_kernel(const float *__restrict__ x, long ldx, int V, int 
     }
 }
 
+__device__ __forceinline__ unsigned long long greedy_key(float v, int col) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)col);
+}
+
+__global__ void argmax_keys_kernel(const float *__restrict__ x, long ldx, int V, unsigned long long *keys) {
+    __shared__ unsigned long long sk[32];
+    const float *row = x + (long)blockIdx.x * ldx;
+    unsigned long long best = 0;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const unsigned long long k = greedy_key(row[v], v);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = sk[w] > best ? sk[w] : best;
+        atomicMax(keys + blockIdx.x, best);
+    }
+}
+
+__global__ void greedy_finalize_kernel(unsigned long long *keys, int rows, int *next, int *log, const int *step,
+                                       int *pair, int *ctr) {
+    const int t = threadIdx.x;
+    if (t < rows) {
+        const unsigned long long k = keys[t];
+        keys[t] = 0ull;
+        const uint32_t ord = (uint32_t)(k >> 32);
+        const int col = (int)(0xFFFFFFFFu - (uint32_t)k);
+        const uint32_t u = (ord & 0x80000000u) ? (ord & 0x7FFFFFFFu) : ~ord;
+        if (next) next[t] = col;
+        if (log) log[(long)(*step) * rows + t] = col;
+        if (pair) {
+            pair[t] = (int)u;
+            pair[rows + t] = col;
+        }
+    }
+    __syncthreads();
+    if (ctr && t == 0) {
+        ctr[0] += 1;
+        ctr[1] += 1;
+    }
+}
+
 }  // namespace
 
 // ========================================================== launchers
@@ -795,6 +845,25 @@ int decode_advance(int *ctr, cudaStream_t s) {
 int argmax_rows(const float *x, long ldx, int rows, int V, int *out, float *outval, cudaStream_t s) {
     if (rows <= 0) return OK;
     argmax_kernel<<<rows, 512, 0, s>>>(x, ldx, V, out, outval, nullptr, nullptr);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int argmax_keys(const float *x, long ldx, int rows, int V, unsigned long long *keys, cudaStream_t s) {
+    if (rows <= 0) return OK;
+    argmax_keys_kernel<<<rows, 512, 0, s>>>(x, ldx, V, keys);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int greedy_finalize(unsigned long long *keys, int rows, int *next, int *log, const int *step, int *pair,
+                    int *ctr, cudaStream_t s) {
+    if (rows > 1024) {
+        set_last_error(ERR_ARG, "greedy_finalize: %d rows", rows);
+        return ERR_ARG;
+    }
+    greedy_finalize_kernel<<<1, rows < 32 ? 32 : ((rows + 31) / 32) * 32, 0, s>>>(keys, rows, next, log, step,
+                                                                                   pair, ctr);
     LAUNCH_CHECK();
     return OK;
 }

@@ -53,6 +53,14 @@ int kv_append_at(const float *qkv, float *kc, float *vc, int B, long Tmax, int C
 int argmax_log(const float *x, long ldx, int rows, int V, int *cur, int *log, const int *step_dev,
                cudaStream_t s);
 int decode_advance(int *ctr, cudaStream_t s);
+// greedy keys: key = (order-preserving bits of the value) << 32 | ~column, so
+// the largest key is the largest value with the lowest column
+int argmax_keys(const float *x, long ldx, int rows, int V, unsigned long long *keys, cudaStream_t s);
+// keys[m] -> token column: next[m], log[*step * rows + m] (log optional) and
+// the (value bits, column) pair pair[m], pair[rows + m] (optional); clears
+// the keys; then, when ctr is given, advances the decode counters
+int greedy_finalize(unsigned long long *keys, int rows, int *next, int *log, const int *step, int *pair,
+                    int *ctr, cudaStream_t s);
 
 // ---------------------------------------------------------------- attention
 // Causal self-attention over packed qkv rows [B, T, 3C] (head h: columns
@@ -64,6 +72,10 @@ int attention_fwd(const float *qkv, float *out, float *lse, int B, int T, int C,
 // TF32 tcgen05 version (head size 64): ERR_ARG without launching anything
 // when the shapes or alignment do not fit
 int attention_fwd_tc(const float *qkv, float *out, float *lse, int B, int T, int C, int H, cudaStream_t s);
+// TF32 tcgen05 backward (head size 64), D = rowsum(dO * O) already computed;
+// ERR_ARG without launching when the shapes or alignment do not fit
+int attention_bwd_tc(const float *qkv, const float *dout, const float *lse, const float *D, float *dqkv, int B,
+                     int T, int C, int H, cudaStream_t s);
 // dqkv [B, T, 3C] is overwritten with dQ, dK, dV. dout/out are [B, T, C].
 size_t attention_bwd_scratch_bytes(int B, int T, int H);
 int attention_bwd(const float *qkv, const float *out, const float *dout, const float *lse,

@@ -54,7 +54,7 @@ struct FastDev {
     size_t gen_cap = 0;
     int *ctr = nullptr;    // [0] position of the incoming token, [1] step index
     float *ln_stats = nullptr;  // [2][8][2] LayerNorm statistics handed between decode GEMVs
-    int *ln_ticket = nullptr;   // [4] last-block tickets: [0..1] statistics, [2] greedy argmax
+    int *ln_ticket = nullptr;   // [4] last-block tickets of the statistics GEMVs ([0..1] used)
     unsigned long long *am_key = nullptr;  // [8] greedy argmax keys of the LM-head GEMV
     // one decode step captured as a CUDA graph, reused while the key matches
     cudaStream_t cap_stream = nullptr;

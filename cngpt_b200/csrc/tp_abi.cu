@@ -108,7 +108,6 @@ struct TpState {
     int *d_step = nullptr, *d_ticket = nullptr;
     float *d_stats = nullptr;  // [8][2] LayerNorm statistics of x after each exchange
     unsigned long long *am_key = nullptr;  // [8] greedy keys of the LM-head GEMV
-    int *am_ticket = nullptr;
 
     const float *qkv_w(int l) const { return wbuf + (size_t)l * 3 * Cl * C; }
     const float *qkv_b(int l) const { return wbuf + (size_t)L * 3 * Cl * C + (size_t)l * 3 * Cl; }
@@ -431,10 +430,9 @@ int decode_step(const GPT *m, TpState *t, int B, cudaStream_t s) {
     }
     GemmEpi eh = epi_store(t->logits, t->ldlog, nullptr);
     eh.argmax_key = t->am_key;
-    eh.argmax_pair = t->pairs;
-    eh.argmax_ticket = t->am_ticket;
     CG_TRY(gemm_ln(x, C, w->ln_f_w, w->ln_f_b, (push && L > 0) ? t->d_stats : nullptr, t->ln,
                    w->wte + (size_t)t->p.v0 * C, C, B, t->p.nv, C, eh, s));
+    CG_TRY(greedy_finalize(t->am_key, B, nullptr, nullptr, nullptr, t->pairs, nullptr, s));
     CG_TRY(greedy(t, B, s, true));
     CG_TRY(decode_advance(t->ctr, s));
     if (push) {  // the exchange numbering advances once per step
@@ -495,7 +493,6 @@ void release(TpState *t) {
     dev_free(t->d_ticket);
     dev_free(t->d_stats);
     dev_free(t->am_key);
-    dev_free(t->am_ticket);
     float *bufs[] = {t->wbuf, t->x,  t->ln,     t->qkv, t->aout, t->hid, t->mean, t->rstd,
                      t->xl,   t->al, t->logits, t->lgath, t->kc,  t->vc, t->dec_part};
     for (auto b : bufs) dev_free(b);
@@ -640,11 +637,8 @@ extern "C" int cngpt_cuda_tp_init(GPT *m, const unsigned char id[128], int world
     }
     st = dev_alloc((void **)&t->ctr, 2 * sizeof(int), false);
     if (st != OK) return fail(st);
-    if ((st = dev_alloc((void **)&t->am_key, 8 * sizeof(unsigned long long), false)) != OK ||
-        (st = dev_alloc((void **)&t->am_ticket, sizeof(int), false)) != OK)
-        return fail(st);
-    if (cudaMemset(t->am_key, 0, 8 * sizeof(unsigned long long)) != cudaSuccess ||
-        cudaMemset(t->am_ticket, 0, sizeof(int)) != cudaSuccess) {
+    if ((st = dev_alloc((void **)&t->am_key, 8 * sizeof(unsigned long long), false)) != OK) return fail(st);
+    if (cudaMemset(t->am_key, 0, 8 * sizeof(unsigned long long)) != cudaSuccess) {
         set_last_error(ERR_CUDA, "tp_init: clearing the argmax keys failed");
         return fail(ERR_CUDA);
     }

@@ -4,7 +4,8 @@ against a float64 PyTorch restatement of the reference's per-head loop
 mask, row softmax, O = PV, lse = log-sum-exp of the scaled scores.
 
 Tolerances (normwise max|err| / max|ref|): TF32 2e-3 (the tensor cores read
-tf32 operands; forward on tcgen05 for head size 64), 3xTF32 2e-5, FP32 1e-5.
+tf32 operands; forward and backward on tcgen05 for head size 64), 3xTF32
+2e-5, FP32 1e-5 (backward: 5x).
 Shapes: GPT-2 small heads (hs 64) at T = 1024 and ragged T, head size 32
 (CUDA-core path), and an odd B*T whose rows are not 16-byte aligned."""
 import numpy as np
@@ -75,7 +76,7 @@ def test_attention_forward_unaligned_rows(lib, cuda):
         lib.cngpt_cuda_set_precision(abi.PREC_3XTF32)
 
 
-@pytest.mark.parametrize("B,T,C,H", [(2, 512, 768, 12), (1, 300, 96, 3)])
+@pytest.mark.parametrize("B,T,C,H", [(2, 512, 768, 12), (1, 1000, 768, 12), (3, 77, 128, 2), (1, 300, 96, 3)])
 def test_attention_backward(lib, cuda, prec, B, T, C, H):
     g = torch.Generator(device=cuda).manual_seed(T)
     qkv = torch.randn(B, T, 3 * C, device=cuda, generator=g)
