@@ -48,7 +48,9 @@ constexpr float LN2f = 0.6931471805599453f;
 enum : int { DEV_ERR_ATT_TMA = 301, DEV_ERR_ATT_MMA = 302, DEV_ERR_ATT_SOFTMAX = 303 };
 
 struct AttCtl {
-    uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full, o_full[2];
+    // kv_full / kv_empty guard the K stages (released once S = Q K^T is done),
+    // v_full / v_empty the V stages (released once P V is done)
+    uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full, o_full[2], v_full[2], v_empty[2];
     uint32_t tmem_base;
     int abort;
 };
@@ -83,6 +85,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
             mbar_init(&ctl->kv_empty[s], 1);
             mbar_init(&ctl->s_full[s], 1);
             mbar_init(&ctl->o_full[s], 1);
+            mbar_init(&ctl->v_full[s], 1);
+            mbar_init(&ctl->v_empty[s], 1);
         }
         ctl->abort = 0;
         fence_mbar_init();
@@ -97,7 +101,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
     const uint32_t tmem = ctl->tmem_base;
 
     if (warp == TMA_WARP) {
-        // ------------------------------------------------------------ TMA
+        // --------------------------------------------------------------- TMA
+        // lane 0 loads Q and the K ring, lane 1 the V ring: K(j) is free once
+        // S(j) is done, V(j) only once P V(j) is, so K runs ahead of V
         if (lane == 0) {
             tma_prefetch_desc(&tmQK);
             tma_prefetch_desc(&tmV);
@@ -107,16 +113,21 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
             for (int j = 0; j < nkv; ++j) {
                 const int st = j & 1;
                 if (!mbar_wait(&ctl->kv_empty[st], ((j >> 1) & 1) ^ 1u, DEV_ERR_ATT_TMA, abort)) break;
-                mbar_arrive_expect_tx(&ctl->kv_full[st], K_BYTES + V_BYTES);
-                const int k0 = row_base + j * AK;
-                tma_load_2d(sK(st), &tmQK, &ctl->kv_full[st], C + h * AHS, k0);
-                tma_load_2d(sK(st) + K_BYTES / 2, &tmQK, &ctl->kv_full[st], C + h * AHS + 32, k0);
+                mbar_arrive_expect_tx(&ctl->kv_full[st], K_BYTES);
+                tma_load_2d(sK(st), &tmQK, &ctl->kv_full[st], C + h * AHS, row_base + j * AK);
+                tma_load_2d(sK(st) + K_BYTES / 2, &tmQK, &ctl->kv_full[st], C + h * AHS + 32, row_base + j * AK);
+            }
+        } else if (lane == 1) {
+            for (int j = 0; j < nkv; ++j) {
+                const int st = j & 1;
+                if (!mbar_wait(&ctl->v_empty[st], ((j >> 1) & 1) ^ 1u, DEV_ERR_ATT_TMA, abort)) break;
+                mbar_arrive_expect_tx(&ctl->v_full[st], V_BYTES);
 #pragma unroll
                 for (int kb = 0; kb < 4; ++kb)
 #pragma unroll
                     for (int d = 0; d < 2; ++d)
-                        tma_load_2d(sV(st) + kb * 8192 + d * 4096, &tmV, &ctl->kv_full[st],
-                                    2 * C + h * AHS + 32 * d, k0 + 32 * kb);
+                        tma_load_2d(sV(st) + kb * 8192 + d * 4096, &tmV, &ctl->v_full[st],
+                                    2 * C + h * AHS + 32 * d, row_base + j * AK + 32 * kb);
             }
         }
     } else if (warp == MMA_WARP) {
@@ -136,6 +147,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
                                  smem_desc(k_addr + kb * (K_BYTES / 2) + kk * 32, 16, 1024, 2), idesc_s,
                                  (kb | kk) != 0);
                 mma_commit(&ctl->s_full[j & 1]);
+                mma_commit(&ctl->kv_empty[j & 1]);  // K(j) may be overwritten once S(j) is done
             };
             bool ok = mbar_wait(&ctl->q_full, 0, DEV_ERR_ATT_MMA, abort) &&
                       mbar_wait(&ctl->kv_full[0], 0, DEV_ERR_ATT_MMA, abort);
@@ -151,6 +163,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
                 }
                 // P(j) written by the softmax warps (and O(j - 2) already folded)
                 if (!mbar_wait(&ctl->p_full, j & 1, DEV_ERR_ATT_MMA, abort)) break;
+                if (!mbar_wait(&ctl->v_full[j & 1], (j >> 1) & 1, DEV_ERR_ATT_MMA, abort)) break;
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(sV(j & 1));
 #pragma unroll
@@ -162,7 +175,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
                                  smem_desc(v_addr + kb * 8192 + kk * 1024, 4096, 512, 1), idesc_o,
                                  (kb | kk) != 0);
                 mma_commit(&ctl->o_full[j & 1]);
-                mma_commit(&ctl->kv_empty[j & 1]);
+                mma_commit(&ctl->v_empty[j & 1]);
             }
         }
     } else {
@@ -301,7 +314,11 @@ constexpr int BWD_WARPS = 16, BWD_TMA = 16, BWD_MMA = 17, BWD_THREADS = 18 * 32;
 constexpr float LOG2Ef = 1.4426950408889634f;
 
 struct BwdCtl {
-    uint64_t in_full, st_full[2], st_empty[2], sp_full[2], a_full, a_done, b_full, b_done, acc_done;
+    // st_*: ring of the K-major step operands (free once S / dP are done);
+    // mn_*: ring of the MN-major step operands (free once the accumulating
+    // MMAs that read them are done)
+    uint64_t in_full, st_full[2], st_empty[2], mn_full[2], mn_empty[2], sp_full[2], a_full, a_done, b_full,
+        b_done, acc_done;
     uint32_t tmem_base;
     int abort;
 };
@@ -313,6 +330,8 @@ __device__ __forceinline__ void bwd_init(BwdCtl *ctl) {
     for (int s = 0; s < 2; ++s) {
         mbar_init(&ctl->st_full[s], 1);
         mbar_init(&ctl->st_empty[s], 1);
+        mbar_init(&ctl->mn_full[s], 1);
+        mbar_init(&ctl->mn_empty[s], 1);
         mbar_init(&ctl->sp_full[s], 1);
     }
     mbar_init(&ctl->a_full, BWD_WARPS);
@@ -388,19 +407,28 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
             for (int s = 0; s < ns; ++s) {
                 const int st = s & 1;
                 if (!mbar_wait(&ctl->st_empty[st], ((s >> 1) & 1) ^ 1u, DEV_ERR_ATTB_TMA, abort)) break;
-                mbar_arrive_expect_tx(&ctl->st_full[st], KV_STAGE);
+                mbar_arrive_expect_tx(&ctl->st_full[st], 2 * BT_HALF);
                 const int q0 = row_base + k0 + s * BQS;
                 uint8_t *sg = stage(st);
                 for (int kb = 0; kb < 2; ++kb) {
                     tma_load_2d(sg + kb * (BT_HALF / 2), &tmQK64, &ctl->st_full[st], h * 64 + 32 * kb, q0);
                     tma_load_2d(sg + BT_HALF + kb * (BT_HALF / 2), &tmDO64, &ctl->st_full[st], h * 64 + 32 * kb, q0);
+                }
+            }
+        } else if (lane == 1) {
+            for (int s = 0; s < ns; ++s) {
+                const int st = s & 1;
+                if (!mbar_wait(&ctl->mn_empty[st], ((s >> 1) & 1) ^ 1u, DEV_ERR_ATTB_TMA, abort)) break;
+                mbar_arrive_expect_tx(&ctl->mn_full[st], 2 * BT_HALF);
+                const int q0 = row_base + k0 + s * BQS;
+                uint8_t *sg = stage(st);
+                for (int kb = 0; kb < 2; ++kb)
                     for (int d = 0; d < 2; ++d) {
-                        tma_load_2d(sg + 2 * BT_HALF + kb * 8192 + d * 4096, &tmMN, &ctl->st_full[st],
+                        tma_load_2d(sg + 2 * BT_HALF + kb * 8192 + d * 4096, &tmMN, &ctl->mn_full[st],
                                     h * 64 + 32 * d, q0 + 32 * kb);
-                        tma_load_2d(sg + 3 * BT_HALF + kb * 8192 + d * 4096, &tmDOMN, &ctl->st_full[st],
+                        tma_load_2d(sg + 3 * BT_HALF + kb * 8192 + d * 4096, &tmDOMN, &ctl->mn_full[st],
                                     h * 64 + 32 * d, q0 + 32 * kb);
                     }
-                }
             }
         }
     } else if (warp == BWD_MMA) {
@@ -413,6 +441,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
                 mma_k64(tmem + (s & 1) * 64, ka, BT_FULL / 2, sg, BT_HALF / 2, false, id_sp, false);
                 mma_k64(tmem + 128 + (s & 1) * 64, va, BT_FULL / 2, sg + BT_HALF, BT_HALF / 2, false, id_sp, false);
                 mma_commit(&ctl->sp_full[s & 1]);
+                mma_commit(&ctl->st_empty[s & 1]);
             };
             bool ok = mbar_wait(&ctl->in_full, 0, DEV_ERR_ATTB_MMA, abort) &&
                       mbar_wait(&ctl->st_full[0], 0, DEV_ERR_ATTB_MMA, abort);
@@ -428,6 +457,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
                 }
                 const uint32_t sg = smem_u32(stage(s & 1));
                 if (!mbar_wait(&ctl->a_full, s & 1, DEV_ERR_ATTB_MMA, abort)) break;  // P^T written
+                if (!mbar_wait(&ctl->mn_full[s & 1], (s >> 1) & 1, DEV_ERR_ATTB_MMA, abort)) break;
                 tc_fence_after();
                 mma_k64(tmem + 256, dsa, BT_DS / 2, sg + 3 * BT_HALF, 0, true, id_acc, s > 0);  // dV += P^T dO
                 mma_commit(&ctl->a_done);
@@ -435,7 +465,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
                 tc_fence_after();
                 mma_k64(tmem + 320, dsa, BT_DS / 2, sg + 2 * BT_HALF, 0, true, id_acc, s > 0);  // dK += dS^T Q
                 mma_commit(&ctl->b_done);
-                mma_commit(&ctl->st_empty[s & 1]);
+                mma_commit(&ctl->mn_empty[s & 1]);
             }
             mma_commit(&ctl->acc_done);
         }
@@ -545,17 +575,26 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_
             for (int s = 0; s < ns; ++s) {
                 const int st = s & 1;
                 if (!mbar_wait(&ctl->st_empty[st], ((s >> 1) & 1) ^ 1u, DEV_ERR_ATTB_TMA, abort)) break;
-                mbar_arrive_expect_tx(&ctl->st_full[st], DQ_STAGE);
+                mbar_arrive_expect_tx(&ctl->st_full[st], 2 * BT_HALF);
                 const int k0 = row_base + s * BQS;
                 uint8_t *sg = stage(st);
                 for (int kb = 0; kb < 2; ++kb) {
                     tma_load_2d(sg + kb * (BT_HALF / 2), &tmQK64, &ctl->st_full[st], C + h * 64 + 32 * kb, k0);
                     tma_load_2d(sg + BT_HALF + kb * (BT_HALF / 2), &tmQK64, &ctl->st_full[st],
                                 2 * C + h * 64 + 32 * kb, k0);
-                    for (int d = 0; d < 2; ++d)
-                        tma_load_2d(sg + 2 * BT_HALF + kb * 8192 + d * 4096, &tmMN, &ctl->st_full[st],
-                                    C + h * 64 + 32 * d, k0 + 32 * kb);
                 }
+            }
+        } else if (lane == 1) {
+            for (int s = 0; s < ns; ++s) {
+                const int st = s & 1;
+                if (!mbar_wait(&ctl->mn_empty[st], ((s >> 1) & 1) ^ 1u, DEV_ERR_ATTB_TMA, abort)) break;
+                mbar_arrive_expect_tx(&ctl->mn_full[st], BT_HALF);
+                const int k0 = row_base + s * BQS;
+                uint8_t *sg = stage(st);
+                for (int kb = 0; kb < 2; ++kb)
+                    for (int d = 0; d < 2; ++d)
+                        tma_load_2d(sg + 2 * BT_HALF + kb * 8192 + d * 4096, &tmMN, &ctl->mn_full[st],
+                                    C + h * 64 + 32 * d, k0 + 32 * kb);
             }
         }
     } else if (warp == BWD_MMA) {
@@ -569,6 +608,7 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_
                 mma_k64(tmem + (s & 1) * 64, qa, BT_FULL / 2, sg, BT_HALF / 2, false, id_sp, false);
                 mma_k64(tmem + 128 + (s & 1) * 64, doa, BT_FULL / 2, sg + BT_HALF, BT_HALF / 2, false, id_sp, false);
                 mma_commit(&ctl->sp_full[s & 1]);
+                mma_commit(&ctl->st_empty[s & 1]);
             };
             bool ok = mbar_wait(&ctl->in_full, 0, DEV_ERR_ATTB_MMA, abort) &&
                       mbar_wait(&ctl->st_full[0], 0, DEV_ERR_ATTB_MMA, abort);
@@ -583,10 +623,11 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_
                     issue_sp(s + 1);
                 }
                 if (!mbar_wait(&ctl->a_full, s & 1, DEV_ERR_ATTB_MMA, abort)) break;  // dS written
+                if (!mbar_wait(&ctl->mn_full[s & 1], (s >> 1) & 1, DEV_ERR_ATTB_MMA, abort)) break;
                 tc_fence_after();
                 mma_k64(tmem + 256, dsa, BT_DS / 2, smem_u32(stage(s & 1)) + 2 * BT_HALF, 0, true, id_acc, s > 0);
                 mma_commit(&ctl->a_done);
-                mma_commit(&ctl->st_empty[s & 1]);
+                mma_commit(&ctl->mn_empty[s & 1]);
             }
             mma_commit(&ctl->acc_done);
         }

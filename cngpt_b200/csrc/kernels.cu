@@ -196,14 +196,31 @@ __global__ void __launch_bounds__(512)
 ce_fwd_kernel(const float *__restrict__ logits, long ldl, const int *__restrict__ targets,
               float *__restrict__ probs, long ldp, float *__restrict__ dlogits, long ldd,
               float scale, float *__restrict__ rowterm, int V) {
+    // Each thread handles columns v = tid + 512 u in groups of CE_U, loading a
+    // whole group before using it so that CE_U loads per thread are in flight
+    // (the rows are HBM-resident and their pitch V is odd, so no float4).
+    constexpr int CE_U = 8, NT = 512;
     __shared__ float shm[16], shs[16];
     const long r = blockIdx.x;
     const float *lg = logits + r * ldl;
     float m = -INFINITY, sum = 0.f;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        const float x = lg[v];
-        if (x > m) { sum = (m == -INFINITY ? 0.f : sum * expf(m - x)) + 1.0f; m = x; }
-        else sum += expf(x - m);
+    for (int v0 = threadIdx.x; v0 < V; v0 += NT * CE_U) {
+        float x[CE_U];
+#pragma unroll
+        for (int u = 0; u < CE_U; ++u) {
+            const int v = v0 + u * NT;
+            x[u] = v < V ? __ldcs(lg + v) : -INFINITY;
+        }
+        float mx = x[0];
+#pragma unroll
+        for (int u = 1; u < CE_U; ++u) mx = fmaxf(mx, x[u]);
+        if (mx == -INFINITY) continue;
+        const float mn = fmaxf(m, mx);
+        float add = 0.f;
+#pragma unroll
+        for (int u = 0; u < CE_U; ++u) add += expf(x[u] - mn);
+        sum = (m == -INFINITY ? 0.f : sum * expf(m - mn)) + add;
+        m = mn;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -221,10 +238,22 @@ ce_fwd_kernel(const float *__restrict__ logits, long ldl, const int *__restrict_
     if (probs || dlogits) {
         float *pr = probs ? probs + r * ldp : nullptr;
         float *dl = dlogits ? dlogits + r * ldd : nullptr;
-        for (int v = threadIdx.x; v < V; v += blockDim.x) {
-            const float p = expf(lg[v] - m) * inv;
-            if (pr) pr[v] = p;
-            if (dl) dl[v] = scale * (p - (v == tgt ? 1.0f : 0.0f));
+        for (int v0 = threadIdx.x; v0 < V; v0 += NT * CE_U) {
+            float x[CE_U];
+#pragma unroll
+            for (int u = 0; u < CE_U; ++u) {
+                const int v = v0 + u * NT;
+                x[u] = v < V ? __ldcs(lg + v) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < CE_U; ++u) {
+                const int v = v0 + u * NT;
+                if (v < V) {
+                    const float p = expf(x[u] - m) * inv;
+                    if (pr) __stcs(pr + v, p);
+                    if (dl) __stcs(dl + v, scale * (p - (v == tgt ? 1.0f : 0.0f)));
+                }
+            }
         }
         if (dl)
             for (long v = V + threadIdx.x; v < ldd; v += blockDim.x) dl[v] = 0.f;
