@@ -1102,6 +1102,7 @@ float *splitk_workspace(size_t floats, cudaStream_t s) {
     return g_splitk_ws;
 }
 
+
 // out = epilogue(sum over splits of ws[s]) in split order (deterministic).
 // Vector form: 4 consecutive columns per thread (N % 4 == 0, 16-byte aligned
 // partials); the epilogue is applied per element.

@@ -506,17 +506,29 @@ __global__ void colsum_partial_kernel(const float *__restrict__ y, long ldy, int
     const long r0 = (long)blockIdx.y * rows_per_chunk;
     const long r1 = std::min<long>(M, r0 + rows_per_chunk);
     float s = 0.f;
+#pragma unroll 8
     for (long r = r0; r < r1; ++r) s += y[r * ldy + n];
     part[(long)blockIdx.y * N + n] = s;
 }
 
-__global__ void colsum_final_kernel(const float *__restrict__ part, int chunks, int N,
-                                    float *__restrict__ db) {
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
-    if (n >= N) return;
+// db[n] += sum of the chunk partials, in chunk order per warp: one block per
+// 32 columns, warp w sums chunks k = w, w+8, ... and the 8 warp sums are
+// added in warp order (fixed shape, deterministic)
+__global__ void __launch_bounds__(256) colsum_final_kernel(const float *__restrict__ part, int chunks, int N,
+                                                           float *__restrict__ db) {
+    __shared__ float red[8][32];
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, n = blockIdx.x * 32 + lane;
     float s = 0.f;
-    for (int k = 0; k < chunks; ++k) s += part[(long)k * N + n];
-    db[n] += s;
+    if (n < N)
+        for (int k = wid; k < chunks; k += 8) s += part[(long)k * N + n];
+    red[wid][lane] = s;
+    __syncthreads();
+    if (wid == 0 && n < N) {
+        float t = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) t += red[k][lane];
+        db[n] += t;
+    }
 }
 
 // ---------------------------------------------------------------- argmax
@@ -620,24 +632,33 @@ int layernorm_fwd(const float *x, long ldx, const float *w, const float *b, floa
 
 constexpr int kLnBwdRowsPerChunk = 128;
 
-size_t layernorm_bwd_scratch_bytes(int T, int C) {
-    const long chunks = (T + kLnBwdRowsPerChunk - 1) / kLnBwdRowsPerChunk;
+size_t layernorm_bwd_scratch_bytes(int T, int C, int rows_per_chunk) {
+    const long chunks = (T + rows_per_chunk - 1) / rows_per_chunk;
     return (size_t)chunks * 2 * C * sizeof(float);
+}
+
+size_t layernorm_bwd_scratch_bytes(int T, int C) { return layernorm_bwd_scratch_bytes(T, C, kLnBwdRowsPerChunk); }
+
+int layernorm_bwd(const float *dout, const float *x, const float *w, const float *mean, const float *rstd,
+                  float *dx, float *dw, float *db, int T, int C, float *scratch, cudaStream_t s,
+                  int rows_per_chunk) {
+    if (T <= 0) return OK;
+    if (rows_per_chunk <= 0) rows_per_chunk = kLnBwdRowsPerChunk;
+    layernorm_bwd_dx_kernel<<<grid_for(T, 8, 148 * 16), 256, 0, s>>>(dout, x, w, mean, rstd, dx, T, C);
+    LAUNCH_CHECK();
+    const int chunks = (T + rows_per_chunk - 1) / rows_per_chunk;
+    dim3 g((C + 255) / 256, chunks);
+    layernorm_bwd_dwdb_kernel<<<g, 256, 0, s>>>(dout, x, mean, rstd, scratch, T, C, rows_per_chunk);
+    LAUNCH_CHECK();
+    layernorm_bwd_reduce<<<(C + 31) / 32, 256, 0, s>>>(scratch, chunks, C, dw, db);
+    LAUNCH_CHECK();
+    return OK;
 }
 
 int layernorm_bwd(const float *dout, const float *x, const float *w, const float *mean,
                   const float *rstd, float *dx, float *dw, float *db, int T, int C, float *scratch,
                   cudaStream_t s) {
-    if (T <= 0) return OK;
-    layernorm_bwd_dx_kernel<<<grid_for(T, 8, 148 * 16), 256, 0, s>>>(dout, x, w, mean, rstd, dx, T, C);
-    LAUNCH_CHECK();
-    const int chunks = (T + kLnBwdRowsPerChunk - 1) / kLnBwdRowsPerChunk;
-    dim3 g((C + 255) / 256, chunks);
-    layernorm_bwd_dwdb_kernel<<<g, 256, 0, s>>>(dout, x, mean, rstd, scratch, T, C, kLnBwdRowsPerChunk);
-    LAUNCH_CHECK();
-    layernorm_bwd_reduce<<<(C + 31) / 32, 256, 0, s>>>(scratch, chunks, C, dw, db);
-    LAUNCH_CHECK();
-    return OK;
+    return layernorm_bwd(dout, x, w, mean, rstd, dx, dw, db, T, C, scratch, s, kLnBwdRowsPerChunk);
 }
 
 int gelu_fwd(const float *x, float *out, long n, cudaStream_t s) {
@@ -793,19 +814,21 @@ int adamw(float *p, float *g, float *m, float *v, const unsigned char *decay, lo
     return OK;
 }
 
+// 32-row chunks (at most 256): enough blocks to keep every SM's loads in
+// flight; the chunk sums are added in chunk order
 size_t colsum_scratch_bytes(int M, int N) {
-    const int chunks = std::max(1, std::min(64, (M + 127) / 128));
+    const int chunks = std::max(1, std::min(256, (M + 31) / 32));
     return (size_t)chunks * N * sizeof(float);
 }
 
 int colsum_add(const float *y, long ldy, int M, int N, float *db, float *scratch, cudaStream_t s) {
     if (M <= 0 || N <= 0) return OK;
-    const int chunks = std::max(1, std::min(64, (M + 127) / 128));
+    const int chunks = std::max(1, std::min(256, (M + 31) / 32));
     const int rpc = (M + chunks - 1) / chunks;
     dim3 g((N + 255) / 256, chunks);
     colsum_partial_kernel<<<g, 256, 0, s>>>(y, ldy, M, N, rpc, scratch);
     LAUNCH_CHECK();
-    colsum_final_kernel<<<(N + 255) / 256, 256, 0, s>>>(scratch, chunks, N, db);
+    colsum_final_kernel<<<(N + 31) / 32, 256, 0, s>>>(scratch, chunks, N, db);
     LAUNCH_CHECK();
     return OK;
 }

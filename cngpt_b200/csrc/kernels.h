@@ -12,6 +12,13 @@ size_t layernorm_bwd_scratch_bytes(int T, int C);
 int layernorm_bwd(const float *dout, const float *x, const float *w, const float *mean,
                   const float *rstd, float *dx, float *dw, float *db, int T, int C, float *scratch,
                   cudaStream_t s);
+// same with dw/db partials over chunks of rows_per_chunk rows (the form
+// above uses 128; the training step uses finer chunks for more parallelism)
+size_t layernorm_bwd_scratch_bytes(int T, int C, int rows_per_chunk);
+int layernorm_bwd(const float *dout, const float *x, const float *w, const float *mean, const float *rstd,
+                  float *dx, float *dw, float *db, int T, int C, float *scratch, cudaStream_t s,
+                  int rows_per_chunk);
+constexpr int kLnBwdTrainRows = 32;
 int gelu_fwd(const float *x, float *out, long n, cudaStream_t s);
 int gelu_bwd(const float *dout, const float *x, float *dx, long n, cudaStream_t s);
 int softmax_rows(float *x, int rows, int cols, cudaStream_t s);

@@ -202,7 +202,7 @@ int ensure_extras(GPT *m, ModelCtx *c, int B, int T) {
     CG_TRY(dev_alloc((void **)&c->d_mlp, BT * 4 * C * sizeof(float), false));
     CG_TRY(dev_alloc((void **)&c->d_ao, BT * C * sizeof(float), false));
     CG_TRY(dev_alloc((void **)&c->d_qkv, BT * 3 * C * sizeof(float), false));
-    size_t sb = layernorm_bwd_scratch_bytes((int)BT, (int)C);
+    size_t sb = layernorm_bwd_scratch_bytes((int)BT, (int)C, kLnBwdTrainRows);
     sb = std::max(sb, colsum_scratch_bytes((int)BT, (int)(4 * C)));
     sb = std::max(sb, attention_bwd_scratch_bytes(B, T, (int)H));
     sb = std::max(sb, BT * sizeof(float));  // CE row terms
@@ -408,7 +408,7 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
     // LN_f (src/model.c:680-685): d_x = 0 + LN_f backward
     CG_CUDA(cudaMemsetAsync(c->d_x, 0, (size_t)BT * C * sizeof(float), s));
     CG_TRY(layernorm_bwd(c->d_ln, L > 0 ? a->res2[L - 1] : a->emb, w->ln_f_w, a->ln_f_mean,
-                         a->ln_f_rstd, c->d_x, g->ln_f_w, g->ln_f_b, BT, C, scr, s));
+                         a->ln_f_rstd, c->d_x, g->ln_f_w, g->ln_f_b, BT, C, scr, s, kLnBwdTrainRows));
     for (int l = L - 1; l >= 0; l--) {
         const float *x_in = (l == 0) ? a->emb : a->res2[l - 1];
         if (m->cfg.dropout > 0.0f) dropout_bwd(c->d_x, a->res2_mask[l], BT * C, m->cfg.dropout);
@@ -440,7 +440,7 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
         CG_TRY(colsum_add(c->d_mlp, 4 * C, BT, 4 * C, g->mlp_fc_b[l], scr, s));
         // LN2 accumulates into the residual gradient: d_x becomes d_res1
         CG_TRY(layernorm_bwd(c->d_ln, a->res1[l], w->ln2_w[l], a->ln2_mean[l], a->ln2_rstd[l], c->d_x,
-                             g->ln2_w[l], g->ln2_b[l], BT, C, scr, s));
+                             g->ln2_w[l], g->ln2_b[l], BT, C, scr, s, kLnBwdTrainRows));
         if (m->cfg.dropout > 0.0f) dropout_bwd(c->d_x, a->res1_mask[l], BT * C, m->cfg.dropout);
         // c_proj (src/model.c:736-740)
         e = GemmEpi();
@@ -471,7 +471,7 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
         CG_TRY(colsum_add(c->d_qkv, 3 * C, BT, 3 * C, g->c_attn_b[l], scr, s));
         // LN1 accumulates into d_x (= d_res1 + LN1 backward, src/model.c:833-840)
         CG_TRY(layernorm_bwd(c->d_ln, x_in, w->ln1_w[l], a->ln1_mean[l], a->ln1_rstd[l], c->d_x,
-                             g->ln1_w[l], g->ln1_b[l], BT, C, scr, s));
+                             g->ln1_w[l], g->ln1_b[l], BT, C, scr, s, kLnBwdTrainRows));
     }
     if (m->cfg.dropout > 0.0f) dropout_bwd(c->d_x, a->emb_mask, BT * C, m->cfg.dropout);
     // embeddings (src/model.c:852-867)
