@@ -133,6 +133,8 @@ EXT_SIGNATURES = {
     "cngpt_cuda_dp_init": (I, [C.POINTER(GPT), VP, I, I]),
     "cngpt_cuda_dp_allreduce_grads": (I, [C.POINTER(GPT)]),
     "cngpt_cuda_dp_free": (I, [C.POINTER(GPT)]),
+    "cngpt_cuda_save_checkpoint": (I, [C.POINTER(GPT), C.c_char_p]),
+    "cngpt_cuda_load_checkpoint": (I, [C.POINTER(GPT), C.c_char_p]),
     "cngpt_cuda_tp_plan": (I, [I, I, I, I, I, VP]),
     "cngpt_cuda_tp_init": (I, [C.POINTER(GPT), VP, I, I]),
     "cngpt_cuda_tp_forward_last": (I, [C.POINTER(GPT), VP, I, I, VP]),

@@ -647,6 +647,104 @@ extern "C" int gpt_save(GPT *m, const char *path) {
     return 0;
 }
 
+// ------------------------------------------------------- training checkpoints
+// gpt_save's file (header + parameters, readable by any gpt_load) followed by
+// an optimizer trailer the reference never writes: magic, AdamW step count,
+// then the first and second moments (n_params floats each).
+namespace {
+constexpr uint32_t kOptMagic = 0x4F50544Du;  // "MTPO"
+
+int write_all(FILE *f, const void *p, size_t bytes) { return fwrite(p, 1, bytes, f) == bytes ? 0 : -1; }
+int read_all(FILE *f, void *p, size_t bytes) { return fread(p, 1, bytes, f) == bytes ? 0 : -1; }
+}  // namespace
+
+extern "C" int cngpt_cuda_save_checkpoint(GPT *m, const char *path) {
+    if (!model_ctx(m)) return ERR_STATE;
+    const size_t n = (size_t)m->n_params;
+    std::vector<float> h(n);
+    cudaStreamSynchronize(g_stream);
+    FILE *f = fopen(path, "wb");
+    if (!f) {
+        set_last_error(ERR_ARG, "save_checkpoint: cannot open %s", path);
+        return ERR_ARG;
+    }
+    GPTHeader hdr = {CNGPT_MAGIC, CNGPT_VERSION, m->cfg.n_layer, m->cfg.n_head, m->cfg.n_embd,
+                     m->cfg.vocab_size, m->cfg.block_size};
+    int st = write_all(f, &hdr, sizeof(hdr));
+    const float *bufs[3] = {m->param_buf, m->m_buf, m->v_buf};
+    for (int i = 0; i < 3 && st == 0; ++i) {
+        if (i == 1) {
+            const uint32_t magic = kOptMagic;
+            const int32_t step = m->step;
+            st = write_all(f, &magic, 4) | write_all(f, &step, 4);
+        }
+        if (cudaMemcpy(h.data(), bufs[i], n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            fclose(f);
+            set_last_error(ERR_CUDA, "save_checkpoint: download failed");
+            return ERR_CUDA;
+        }
+        if (st == 0) st = write_all(f, h.data(), n * 4);
+    }
+    if (fclose(f) != 0 || st != 0) {
+        set_last_error(ERR_ARG, "save_checkpoint: writing %s failed", path);
+        return ERR_ARG;
+    }
+    return OK;
+}
+
+extern "C" int cngpt_cuda_load_checkpoint(GPT *m, const char *path) {
+    FILE *f = fopen(path, "rb");
+    if (!f) {
+        set_last_error(ERR_ARG, "load_checkpoint: cannot open %s", path);
+        return ERR_ARG;
+    }
+    GPTHeader hdr;
+    if (read_all(f, &hdr, sizeof(hdr)) != 0 || hdr.magic != CNGPT_MAGIC) {
+        fclose(f);
+        set_last_error(ERR_ARG, "load_checkpoint: %s is not a cngpt model file", path);
+        return ERR_ARG;
+    }
+    if (!m->param_buf) {
+        GPTConfig cfg = {hdr.n_layer, hdr.n_head, hdr.n_embd, hdr.vocab_size, hdr.block_size, 0.0f};
+        if (gpt_init(m, cfg) != 0) {
+            fclose(f);
+            return ERR_ALLOC;
+        }
+    } else if (hdr.n_layer != m->cfg.n_layer || hdr.n_head != m->cfg.n_head || hdr.n_embd != m->cfg.n_embd ||
+               hdr.vocab_size != m->cfg.vocab_size || hdr.block_size != m->cfg.block_size) {
+        fclose(f);
+        set_last_error(ERR_ARG, "load_checkpoint: %s holds a different configuration", path);
+        return ERR_ARG;
+    }
+    const size_t n = (size_t)m->n_params;
+    std::vector<float> h(n);
+    uint32_t magic = 0;
+    int32_t step = 0;
+    int st = read_all(f, h.data(), n * 4);
+    if (st == 0 && cudaMemcpy(m->param_buf, h.data(), n * 4, cudaMemcpyHostToDevice) != cudaSuccess) st = -2;
+    const bool has_opt = st == 0 && read_all(f, &magic, 4) == 0 && magic == kOptMagic && read_all(f, &step, 4) == 0;
+    if (st == 0) {
+        if (has_opt) {
+            float *dst[2] = {m->m_buf, m->v_buf};
+            for (int i = 0; i < 2 && st == 0; ++i) {
+                st = read_all(f, h.data(), n * 4);
+                if (st == 0 && cudaMemcpy(dst[i], h.data(), n * 4, cudaMemcpyHostToDevice) != cudaSuccess) st = -2;
+            }
+            if (st == 0) m->step = step;
+        } else if (cudaMemset(m->m_buf, 0, n * 4) != cudaSuccess || cudaMemset(m->v_buf, 0, n * 4) != cudaSuccess) {
+            st = -2;
+        } else {
+            m->step = 0;  // a plain gpt_save file: fresh optimizer state
+        }
+    }
+    fclose(f);
+    if (st != 0) {
+        set_last_error(st == -2 ? ERR_CUDA : ERR_ARG, "load_checkpoint: reading %s failed", path);
+        return st == -2 ? ERR_CUDA : ERR_ARG;
+    }
+    return OK;
+}
+
 extern "C" int cngpt_cuda_dp_free(GPT *m);
 
 extern "C" void gpt_free(GPT *m) {

@@ -113,6 +113,17 @@ int cngpt_cuda_params_from_host(GPT *m, const float *src);
 int cngpt_cuda_grads_to_host(GPT *m, float *dst);
 int cngpt_cuda_copy(void *dst, const void *src, size_t bytes); /* any direction, synchronous */
 
+/* ---- training checkpoints -------------------------------------------------
+ * The reference saves only the parameters (gpt_save, src/model.c:177-231)
+ * and restarts AdamW from zero moments. save_checkpoint writes gpt_save's
+ * file followed by an optimizer trailer (step count, first and second
+ * moments), so any gpt_load still reads it as a model file; load_checkpoint
+ * restores parameters, moments and step (a file without the trailer loads
+ * with fresh optimizer state). A model with no arena is created from the
+ * file's configuration; otherwise the configurations must match. */
+int cngpt_cuda_save_checkpoint(GPT *m, const char *path);
+int cngpt_cuda_load_checkpoint(GPT *m, const char *path);
+
 /* ---- greedy decode with a KV cache ---------------------------------------
  * The reference recomputes the whole prefix per token (src/model.c:991-1016);
  * this keeps K and V per layer and runs one row per sequence per step. The
