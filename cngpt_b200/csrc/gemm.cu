@@ -1163,6 +1163,16 @@ struct GemmModel {
 
 // Number of K splits for a GEMM with `tiles` output tiles of width bn (rows
 // per CTA 128; pair kernels load bn / 2 B rows per CTA).
+// CNGPT_CUDA_SPLITK=<n>: at most n K splits (1 disables split-K; default 8)
+int max_ksplit() {
+    static int mx = 0;
+    if (mx == 0) {
+        const char *e = getenv("CNGPT_CUDA_SPLITK");
+        mx = e ? std::max(1, std::min(8, atoi(e))) : 8;
+    }
+    return mx;
+}
+
 int choose_ksplit(int tiles, int kblocks, int M, int N, long K, bool split3, int workers = 0, int bn = 128,
                   bool pair = false, double *t_out = nullptr) {
     const long w = workers > 0 ? workers : num_sms();
@@ -1170,7 +1180,7 @@ int choose_ksplit(int tiles, int kblocks, int M, int N, long K, bool split3, int
     const double bpf = (128.0 + (pair ? bn / 2 : bn)) * 128.0 / (2.0 * 128 * bn * 32);
     int best = 1;
     double bt = GemmModel::time(flops, bpf, tiles, w, 1, (long)M * N, split3);
-    for (int k = 2; k <= 8 && kblocks / k >= 4; ++k) {
+    for (int k = 2; k <= max_ksplit() && kblocks / k >= 4; ++k) {
         const double t = GemmModel::time(flops, bpf, (long)tiles * k, w, k, (long)M * N, split3);
         if (t < 0.97 * bt) {
             bt = t;
