@@ -486,11 +486,15 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
             tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)((s & 1) * 64 + cq * 16), sv);
             tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)(128 + (s & 1) * 64 + cq * 16), dp);
             const int qf = k0 + s * BQS + cq * 16;
+            // lse and D of this warp's 16 queries: one load per lane (lanes
+            // 0-15 lse, 16-31 D), handed out by shuffles
+            const int ql = qf + (lane & 15);
+            const float ld_ = ql < T ? ((lane < 16) ? lse_bh[ql] * LOG2Ef : D_bh[ql]) : 0.f;
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
                 const int q = qf + c;
                 const bool valid = key <= q && q < T;
-                const float l2 = valid ? lse_bh[q] * LOG2Ef : 0.f, dd = valid ? D_bh[q] : 0.f;
+                const float l2 = __shfl_sync(0xffffffffu, ld_, c), dd = __shfl_sync(0xffffffffu, ld_, 16 + c);
                 pv[c] = valid ? ex2f(sv[c] * sl2 - l2) : 0.f;
                 dsv[c] = pv[c] * (dp[c] - dd);
             }
