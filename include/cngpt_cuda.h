@@ -152,9 +152,13 @@ int cngpt_cuda_dp_free(GPT *m);
  * width, the LM head by blocks of ceil(vocab / world) rows of the tied wte.
  * Every rank holds the full model (same weights on every rank: initialise
  * them from the same seed, or load the same file) and gets the id from
- * cngpt_cuda_dp_unique_id on rank 0. Each block ends in two sum-allreduces of
- * the [rows, n_embd] residual stream; the greedy token is merged from every
- * rank's (max, lowest index) pair. All ranks make the same calls in order.
+ * cngpt_cuda_dp_unique_id on rank 0. Each block ends in two sums of the
+ * ranks' partial [rows, n_embd] residual streams: ncclAllReduce for the
+ * prefill; for decode batches up to 8 rows the row-split GEMVs push their
+ * partials into every rank's receive buffer (CUDA IPC peer memory over
+ * NVLink, mapped at tp_init; CNGPT_CUDA_TP_NCCL_ONLY=1 keeps NCCL). The
+ * greedy token is merged from every rank's (max, lowest index) pair. All
+ * ranks make the same calls in order.
  * plan (host only, no GPU): h0, nh, f0, nf, v0, nv, vpad of `rank`. */
 int cngpt_cuda_tp_plan(int n_head, int n_embd, int vocab, int world, int rank, int plan[7]);
 int cngpt_cuda_tp_init(GPT *m, const unsigned char id[128], int world, int rank);
