@@ -381,6 +381,84 @@ def inference_bench(lib, torch, dev, world: int, rank: int, hbm_peak: float, bar
 
 
 
+def train_configs_bench(lib, torch, dev, world: int, rank: int, barrier, max_over_ranks, tf32_peak: float) -> dict:
+    """The other two training configs of BASELINE.json, data parallel over the
+    job's GPUs like the headline: configs[0] tiny (6L/384/6H, V=65, B=64,
+    T=256, lr 1e-3, betas 0.9/0.99) with the reference's rand() init, and
+    configs[3] GPT-2 medium (24L/1024/16H, B=16, T=1024 per GPU) with
+    device-random N(0, 0.02) weights (the host init of 355 M parameters would
+    dominate the run; step cost does not depend on the values). TF32, CUDA
+    events around the timed steps, max over ranks."""
+    from cngpt_b200 import abi
+    out = {}
+    for name, (L, H, Cm, V, blk, B, T, b2, lr, steps) in {
+            "tiny": (6, 6, 384, 65, 256, 64, 256, 0.99, 1e-3, 20),
+            "gpt2_medium": (24, 16, 1024, 50257, 1024, 16, 1024, 0.95, 3e-4, 5)}.items():
+        m = abi.GPT()
+        abi.check(lib, 0 if lib.gpt_init(C.byref(m), abi.GPTConfig(L, H, Cm, V, blk, 0.0)) == 0 else 3, "gpt_init")
+        if name == "tiny":
+            C.CDLL(None).srand(1)
+            lib.gpt_init_weights(C.byref(m))
+        else:
+            g = torch.Generator(device=dev).manual_seed(99)
+            w = torch.randn(m.n_params, generator=g, device=dev) * 0.02
+            abi.check(lib, lib.cngpt_cuda_copy(C.cast(m.param_buf, C.c_void_p), C.c_void_p(w.data_ptr()),
+                                               m.n_params * 4), "weights")
+            del w
+        if world > 1:
+            import torch.distributed as dist
+            uid = (C.c_ubyte * 128)()
+            if rank == 0:
+                abi.check(lib, lib.cngpt_cuda_dp_unique_id(uid), "dp id")
+            obj = [bytes(uid)]
+            dist.broadcast_object_list(obj, src=0)
+            uid = (C.c_ubyte * 128).from_buffer_copy(obj[0])
+            abi.check(lib, lib.cngpt_cuda_dp_init(C.byref(m), uid, world, rank), "dp init")
+        ids = lcg_tokens(B * T + 1, V, 12345 + rank)
+        tok = torch.from_numpy(ids[:-1].copy()).to(dev)
+        tgt = torch.from_numpy(ids[1:].copy()).to(dev)
+
+        def step():
+            st = lib.cngpt_cuda_train_step(C.byref(m), tok.data_ptr(), tgt.data_ptr(), B, T, lr, 0.9, b2, 1e-8,
+                                           0.1, 1.0, None)
+            if st:
+                raise RuntimeError(lib.cngpt_cuda_last_message().decode())
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1)) / steps
+        loss = C.c_float()
+        abi.check(lib, lib.cngpt_cuda_last_loss(C.byref(m), C.byref(loss)), "loss")
+        fl = step_flops_cfg(L, Cm, V, B, T)
+        out[name] = {"config": f"BASELINE configs[{0 if name == 'tiny' else 3}]: {L}L/{Cm}C/{H}H V={V}, "
+                               f"B={B} T={T} per GPU, dp{world}",
+                     "tokens_per_s": B * T * world / (ms * 1e-3), "ms_per_step": ms, "steps": steps,
+                     "step_tflops_per_gpu": fl / (ms * 1e-3) / 1e12,
+                     "step_frac_of_tf32_peak": fl / (ms * 1e-3) / 1e12 / tf32_peak, "loss": float(loss.value)}
+        if world > 1:
+            lib.cngpt_cuda_dp_free(C.byref(m))
+        lib.gpt_free(C.byref(m))
+    return out
+
+
+def step_flops_cfg(L: int, Cm: int, V: int, B: int, T: int) -> float:
+    """Algorithmic FLOP of one training step (3 x forward: linears, causal
+    attention over T(T+1)/2 pairs, LM head)."""
+    BT = B * T
+    lin = 2.0 * BT * L * (3 * Cm * Cm + Cm * Cm + 8 * Cm * Cm)
+    attn = 4.0 * B * L * Cm * (T * (T + 1) / 2)
+    head = 2.0 * BT * V * Cm
+    return 3.0 * (lin + attn + head)
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -513,6 +591,10 @@ def run_ours(args) -> None:
     if not args.no_inference:
         line["inference"] = inference_bench(lib, torch, dev, world, rank, peaks.get("hbm_gbs", 6650.0),
                                             barrier, max_over_ranks)
+    if not args.no_other_configs:
+        lib.cngpt_cuda_set_precision(abi.PREC_TF32)
+        line["other_train_configs"] = train_configs_bench(lib, torch, dev, world, rank, barrier, max_over_ranks,
+                                                          tf32_peak)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_reference_step_sample(1, 1, os.cpu_count() or 1)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -540,6 +622,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-inference", action="store_true", help="skip the decode / prefill figures")
+    ap.add_argument("--no-other-configs", action="store_true", help="skip the tiny and medium training figures")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
