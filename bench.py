@@ -350,7 +350,17 @@ def inference_bench(lib, torch, dev, world: int, rank: int, hbm_peak: float, bar
         obj = [bytes(uid)]
         dist.broadcast_object_list(obj, src=0)
         uid = (C.c_ubyte * 128).from_buffer_copy(obj[0])
-    abi.check(lib, lib.cngpt_cuda_tp_init(C.byref(m), uid, world, rank), "tp init")
+    st = lib.cngpt_cuda_tp_init(C.byref(m), uid, world, rank)
+    # every rank must have its tensor-parallel state before any rank issues a
+    # collective with it: agree on the outcome first
+    worst = max_over_ranks(float(st != 0))
+    if worst:
+        msg = lib.cngpt_cuda_last_message().decode() if st else "another rank failed tp_init"
+        if st == 0:
+            lib.cngpt_cuda_tp_free(C.byref(m))
+        lib.gpt_free(C.byref(m))
+        out["gpt2_xl"] = {"error": f"tp_init failed: {msg}"}
+        return out
     lib.cngpt_cuda_set_precision(abi.PREC_TF32)
     xl = {"config": "BASELINE configs[4]: prefill 8 x 1024; decode from a 896-token prompt for 128 "
                     "greedy steps (the cache ends at block_size 1024), tf32", "tp": world}

@@ -475,16 +475,10 @@ void release(TpState *t) {
     cudaStreamSynchronize(g_stream);
     if (t->cap_stream) cudaStreamSynchronize(t->cap_stream);
     drop_graph(t);  // before the communicator its NCCL nodes use
-    if (t->pbuf && t->comm) {
-        // no rank unmaps or frees its receive buffer while a peer may still
-        // write into it: one all-reduce as a barrier first
-        float *one = nullptr;
-        if (dev_alloc((void **)&one, sizeof(float), false) == OK) {
-            nccl_allreduce_sum(one, 1, t->comm, g_stream);
-            cudaStreamSynchronize(g_stream);
-            dev_free(one);
-        }
-    }
+    // No collective here: a peer pushes into this rank's buffer only before
+    // raising the flag this rank waited for, so once every call of this rank
+    // has completed no peer writes into it any more (all ranks make the same
+    // calls), and a rank whose tp_init failed must not wait for the others.
     for (int r = 0; r < TP_MAX_WORLD; ++r)
         if (t->peer[r] && t->peer[r] != t->pbuf) cudaIpcCloseMemHandle(t->peer[r]);
     dev_free(t->pbuf);
@@ -512,6 +506,7 @@ int setup_peers(TpState *t) {
     const size_t bytes = tp_buf_bytes(t->world, t->C);
     CG_TRY(dev_alloc((void **)&t->pbuf, bytes, false));
     CG_CUDA(cudaMemset(t->pbuf, 0, bytes));
+    CG_CUDA(cudaDeviceSynchronize());  // zeroed before the agreement below lets any peer push
     cudaIpcMemHandle_t h;
     CG_CUDA(cudaIpcGetMemHandle(&h, t->pbuf));
     static_assert(sizeof(cudaIpcMemHandle_t) % 4 == 0, "handle size");
@@ -541,7 +536,25 @@ int setup_peers(TpState *t) {
         st = ERR_CUDA;
     }
     dev_free(dh);
+    // every rank learns whether every rank mapped its peers (all ranks reach
+    // this collective, failed or not), so that either all ranks continue or
+    // all return the error; it also orders every buffer's zeroing before any
+    // rank can push into it
+    float *flag = nullptr;
+    CG_TRY(dev_alloc((void **)&flag, sizeof(float), false));
+    const float bad = st == OK ? 0.f : 1.f;
+    cudaMemcpy(flag, &bad, sizeof(float), cudaMemcpyHostToDevice);
+    const int st2 = nccl_allreduce_sum(flag, 1, t->comm, g_stream);
+    float nbad = 1.f;
+    cudaStreamSynchronize(g_stream);
+    cudaMemcpy(&nbad, flag, sizeof(float), cudaMemcpyDeviceToHost);
+    dev_free(flag);
     if (st != OK) return st;
+    if (st2 != OK) return st2;
+    if (nbad != 0.f) {
+        set_last_error(ERR_CUDA, "tp_init: another rank could not map the peer buffers");
+        return ERR_CUDA;
+    }
     CG_TRY(dev_alloc((void **)&t->d_peers, TP_MAX_WORLD * sizeof(char *), false));
     CG_CUDA(cudaMemcpy(t->d_peers, t->peer, TP_MAX_WORLD * sizeof(char *), cudaMemcpyHostToDevice));
     CG_TRY(dev_alloc((void **)&t->d_step, sizeof(int), false));
@@ -549,13 +562,7 @@ int setup_peers(TpState *t) {
     CG_TRY(dev_alloc((void **)&t->d_stats, 2 * TP_MAX_ROWS * sizeof(float), false));
     CG_CUDA(cudaMemset(t->d_step, 0, sizeof(int)));
     CG_CUDA(cudaMemset(t->d_ticket, 0, sizeof(int)));
-    // every rank's buffer is zeroed before any rank may push into it
-    float *one = nullptr;
-    CG_TRY(dev_alloc((void **)&one, sizeof(float), false));
-    st = nccl_allreduce_sum(one, 1, t->comm, g_stream);
-    cudaStreamSynchronize(g_stream);
-    dev_free(one);
-    return st;
+    return OK;
 }
 
 }  // namespace
