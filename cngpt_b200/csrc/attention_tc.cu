@@ -38,7 +38,7 @@ constexpr int V_BYTES = AK * AHS * 4;  // 4 key blocks x 2 dim atoms (32 x 32 ea
 constexpr int P_BYTES = AQ * AK * 4;   // 4 key blocks of 128 rows x 128 B
 constexpr int SM_Q = 0, SM_K = SM_Q + Q_BYTES, SM_V = SM_K + 2 * K_BYTES, SM_P = SM_V + 2 * V_BYTES;
 constexpr int SM_CTL = SM_P + P_BYTES;
-constexpr int ATT_SMEM = SM_CTL + 128 + 1024;
+constexpr int ATT_SMEM = SM_CTL + 256 + 1024;
 constexpr int SOFT_WARPS = 16;                       // 4 per TMEM lane quarter, 32 key columns each
 constexpr int TMA_WARP = SOFT_WARPS, MMA_WARP = SOFT_WARPS + 1;
 constexpr int ATT_THREADS = (SOFT_WARPS + 2) * 32;
@@ -49,11 +49,14 @@ enum : int { DEV_ERR_ATT_TMA = 301, DEV_ERR_ATT_MMA = 302, DEV_ERR_ATT_SOFTMAX =
 
 struct AttCtl {
     // kv_full / kv_empty guard the K stages (released once S = Q K^T is done),
-    // v_full / v_empty the V stages (released once P V is done)
-    uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full, o_full[2], v_full[2], v_empty[2];
+    // v_full / v_empty the V stages (released once P V is done); p_full[t]:
+    // the softmax warps' P of tiles j with j % 2 == t (P kept in shared
+    // memory uses p_full[0] for every tile)
+    uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], o_full[2], v_full[2], v_empty[2];
     uint32_t tmem_base;
     int abort;
 };
+static_assert(sizeof(AttCtl) <= 256, "control block");
 
 __device__ __forceinline__ float ex2f(float x) {
     float y;
@@ -61,6 +64,7 @@ __device__ __forceinline__ float ex2f(float x) {
     return y;
 }
 
+template <bool TS>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_constant__ CUtensorMap tmV,
                    float *__restrict__ out, float *__restrict__ lse, int T, int C, int H, float sl2) {
@@ -79,8 +83,8 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
 
     if (threadIdx.x == 0) {
         mbar_init(&ctl->q_full, 1);
-        mbar_init(&ctl->p_full, SOFT_WARPS);
         for (int s = 0; s < 2; ++s) {
+            mbar_init(&ctl->p_full[s], SOFT_WARPS);
             mbar_init(&ctl->kv_full[s], 1);
             mbar_init(&ctl->kv_empty[s], 1);
             mbar_init(&ctl->s_full[s], 1);
@@ -158,22 +162,39 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
             for (int j = 0; ok && j < nkv; ++j) {
                 if (j + 1 < nkv) {
                     if (!mbar_wait(&ctl->kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, DEV_ERR_ATT_MMA, abort)) break;
+                    // TS: S(j + 1) overwrites P(j - 1), the A operand of P V(j - 1);
+                    // MMAs into different accumulators are not ordered, so wait
+                    // for that product to complete
+                    if (TS && j >= 1 && !mbar_wait(&ctl->o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, DEV_ERR_ATT_MMA, abort))
+                        break;
                     tc_fence_after();
                     issue_s(j + 1);
                 }
-                // P(j) written by the softmax warps (and O(j - 2) already folded)
-                if (!mbar_wait(&ctl->p_full, j & 1, DEV_ERR_ATT_MMA, abort)) break;
+                // P(j) written by the softmax warps (and O(j - 2) already folded).
+                // TS: the softmax warps do not wait for P V(j) before writing
+                // P(j + 1), so the two tile parities arrive on separate barriers
+                // (a warp cannot run two tiles ahead: P(j + 2) follows its fold
+                // of O_t(j), which needs every warp's P(j))
+                if (!mbar_wait(TS ? &ctl->p_full[j & 1] : &ctl->p_full[0], TS ? (j >> 1) & 1 : j & 1, DEV_ERR_ATT_MMA,
+                               abort))
+                    break;
                 if (!mbar_wait(&ctl->v_full[j & 1], (j >> 1) & 1, DEV_ERR_ATT_MMA, abort)) break;
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(sV(j & 1));
 #pragma unroll
                 for (int kb = 0; kb < 4; ++kb)
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_tf32(tmem + (uint32_t)(2 * AK + (j & 1) * AHS),
-                                 smem_desc(p_addr + kb * (P_BYTES / 4) + kk * 32, 16, 1024, 2),
-                                 smem_desc(v_addr + kb * 8192 + kk * 1024, 4096, 512, 1), idesc_o,
-                                 (kb | kk) != 0);
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t vd = smem_desc(v_addr + kb * 8192 + kk * 1024, 4096, 512, 1);
+                        if constexpr (TS)  // P(j) in place of S(j): keys kb * 32 + kk * 8 .. + 7
+                            mma_tf32_ts(tmem + (uint32_t)(2 * AK + (j & 1) * AHS),
+                                        tmem + (uint32_t)((j & 1) * AK + kb * 32 + kk * 8), vd, idesc_o,
+                                        (kb | kk) != 0);
+                        else
+                            mma_tf32(tmem + (uint32_t)(2 * AK + (j & 1) * AHS),
+                                     smem_desc(p_addr + kb * (P_BYTES / 4) + kk * 32, 16, 1024, 2), vd, idesc_o,
+                                     (kb | kk) != 0);
+                    }
                 mma_commit(&ctl->o_full[j & 1]);
                 mma_commit(&ctl->v_empty[j & 1]);
             }
@@ -183,83 +204,147 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
         const int quarter = warp & 3, cs = warp >> 2;
         const int r = quarter * 32 + lane, q = q0 + r;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-        uint8_t *pblk = base + SM_P + cs * (P_BYTES / 4) + (r >> 3) * 1024 + (r & 7) * 128;
         float o[16];
 #pragma unroll
         for (int d = 0; d < 16; ++d) o[d] = 0.f;
         float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
         bool ok = true;
-        auto fold = [&](int j) -> bool {  // O = O * alpha_prev + O_t(j), this warp's 16 columns
-            if (!mbar_wait(&ctl->o_full[j & 1], (j >> 1) & 1, DEV_ERR_ATT_SOFTMAX, abort)) return false;
-            tc_fence_after();
-            float v[32];
-            tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(2 * AK + (j & 1) * AHS + (cs >> 1) * 32), v);
-            if (cs & 1) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) o[i] = o[i] * alpha_prev + v[16 + i];
-            } else {
+        if constexpr (TS) {
+            // P(j) overwrites S(j) in TMEM and is the A operand of P V(j), so
+            // the exponentials of tile j + 1 overlap P V(j) on the tensor
+            // cores. The row max is exchanged through shared memory (one
+            // partial per column slice, double-buffered by tile parity); every
+            // warp passes the same named barriers whatever happens, so a
+            // timed-out wait cannot strand the rest of its lane quarter.
+            float *pmax = (float *)(base + SM_P + 4 * AQ * sizeof(float));  // [2][4][AQ]
+            auto fold = [&](int j) -> bool {  // O = O * alpha_prev + O_t(j), this warp's 16 columns
+                if (!mbar_wait(&ctl->o_full[j & 1], (j >> 1) & 1, DEV_ERR_ATT_SOFTMAX, abort)) return false;
+                tc_fence_after();
+                float v[16];
+                tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)(2 * AK + (j & 1) * AHS + cs * 16), v);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) o[i] = o[i] * alpha_prev + v[i];
-            }
-            return true;
-        };
-        for (int j = 0; j < nkv; ++j) {
-            if (!mbar_wait(&ctl->s_full[j & 1], (j >> 1) & 1, DEV_ERR_ATT_SOFTMAX, abort)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const bool diag = (j == qt);
-            const int kb0 = j * AK;
-            float own[32];
-            float mraw = -INFINITY;  // max of the unscaled, unmasked scores
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
+                return true;
+            };
+            for (int j = 0; j < nkv; ++j) {
+                const int buf = j & 1;
+                ok = ok && mbar_wait(&ctl->s_full[buf], (j >> 1) & 1, DEV_ERR_ATT_SOFTMAX, abort);
+                ok = __all_sync(0xffffffffu, ok);
+                const bool diag = (j == qt);
+                const int kfirst = j * AK + cs * 32;
+                const uint32_t s_addr = tmem + lane_off + (uint32_t)(buf * AK + cs * 32);
                 float v[32];
-                tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((j & 1) * AK + c * 32), v);
-                if (diag) {
+                float pm = -INFINITY;  // max of this slice's unscaled, unmasked scores
+                if (ok) {
+                    tc_fence_after();
+                    tmem_ld_32x32b_x32(s_addr, v);
+                    if (diag) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (kb0 + c * 32 + i <= q) mraw = fmaxf(mraw, v[i]);
+                        for (int i = 0; i < 32; ++i)
+                            if (kfirst + i <= q) pm = fmaxf(pm, v[i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) pm = fmaxf(pm, v[i]);
+                    }
+                }
+                float *pb = pmax + buf * 4 * AQ;
+                pb[cs * AQ + r] = pm;
+                asm volatile("bar.sync %0, 128;" ::"r"(1 + quarter) : "memory");
+                if (!ok) continue;
+                const float mraw = fmaxf(fmaxf(pb[r], pb[AQ + r]), fmaxf(pb[2 * AQ + r], pb[3 * AQ + r]));
+                const float m_new = fmaxf(m, mraw * sl2);  // sl2 > 0: max commutes with the scale
+                const float alpha = ex2f(m - m_new);
+                float rs = 0.f;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float p = (diag && kfirst + i > q) ? 0.f : ex2f(v[i] * sl2 - m_new);
+                    v[i] = p;
+                    rs += p;
+                }
+                tmem_st_32x32b_x32(s_addr, v);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->p_full[buf]);
+                l = l * alpha + rs;
+                m = m_new;
+                if (j > 0) ok = __all_sync(0xffffffffu, fold(j - 1));
+                alpha_prev = alpha;
+            }
+            ok = ok && fold(nkv - 1);
+        } else {
+            uint8_t *pblk = base + SM_P + cs * (P_BYTES / 4) + (r >> 3) * 1024 + (r & 7) * 128;
+            auto fold = [&](int j) -> bool {  // O = O * alpha_prev + O_t(j), this warp's 16 columns
+                if (!mbar_wait(&ctl->o_full[j & 1], (j >> 1) & 1, DEV_ERR_ATT_SOFTMAX, abort)) return false;
+                tc_fence_after();
+                float v[32];
+                tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)(2 * AK + (j & 1) * AHS + (cs >> 1) * 32), v);
+                if (cs & 1) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o[i] = o[i] * alpha_prev + v[16 + i];
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, v[i]);
+                    for (int i = 0; i < 16; ++i) o[i] = o[i] * alpha_prev + v[i];
                 }
-                if (c == cs) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) own[i] = v[i];
+                return true;
+            };
+            for (int j = 0; j < nkv; ++j) {
+                if (!mbar_wait(&ctl->s_full[j & 1], (j >> 1) & 1, DEV_ERR_ATT_SOFTMAX, abort)) {
+                    ok = false;
+                    break;
                 }
-            }
-            const float m_new = fmaxf(m, mraw * sl2);  // sl2 > 0: max commutes with the scale
-            const float alpha = ex2f(m - m_new);
-            // P(j) may only be written once P V of tile j - 1 has read P
-            if (j > 0 && !fold(j - 1)) {
-                ok = false;
-                break;
-            }
-            const int kfirst = kb0 + cs * 32;
-            float rs = 0.f;
+                tc_fence_after();
+                const bool diag = (j == qt);
+                const int kb0 = j * AK;
+                float own[32];
+                float mraw = -INFINITY;  // max of the unscaled, unmasked scores
 #pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-                float p4[4];
+                for (int c = 0; c < 4; ++c) {
+                    float v[32];
+                    tmem_ld_32x32b_x32(tmem + lane_off + (uint32_t)((j & 1) * AK + c * 32), v);
+                    if (diag) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int i = ch * 4 + e;
-                    p4[e] = (diag && kfirst + i > q) ? 0.f : ex2f(own[i] * sl2 - m_new);
-                    rs += p4[e];
+                        for (int i = 0; i < 32; ++i)
+                            if (kb0 + c * 32 + i <= q) mraw = fmaxf(mraw, v[i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, v[i]);
+                    }
+                    if (c == cs) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) own[i] = v[i];
+                    }
                 }
-                *(float4 *)(pblk + ((ch ^ (r & 7)) << 4)) = make_float4(p4[0], p4[1], p4[2], p4[3]);
+                const float m_new = fmaxf(m, mraw * sl2);  // sl2 > 0: max commutes with the scale
+                const float alpha = ex2f(m - m_new);
+                // P(j) may only be written once P V of tile j - 1 has read P
+                if (j > 0 && !fold(j - 1)) {
+                    ok = false;
+                    break;
+                }
+                const int kfirst = kb0 + cs * 32;
+                float rs = 0.f;
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    float p4[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int i = ch * 4 + e;
+                        p4[e] = (diag && kfirst + i > q) ? 0.f : ex2f(own[i] * sl2 - m_new);
+                        rs += p4[e];
+                    }
+                    *(float4 *)(pblk + ((ch ^ (r & 7)) << 4)) = make_float4(p4[0], p4[1], p4[2], p4[3]);
+                }
+                l = l * alpha + rs;
+                m = m_new;
+                alpha_prev = alpha;
+                // generic-proxy P writes -> visible to the tensor core
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ctl->p_full[0]);
             }
-            l = l * alpha + rs;
-            m = m_new;
-            alpha_prev = alpha;
-            // generic-proxy P writes -> visible to the tensor core
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ctl->p_full);
+            ok = ok && fold(nkv - 1);
         }
-        ok = ok && fold(nkv - 1);
         // row sums: the four column slices of each row, added in slice order,
         // exchanged through the P buffer (free once the last P V completed)
         float *lsum = (float *)(base + SM_P);
@@ -305,23 +390,25 @@ constexpr int BT_DS = 128 * BQS * 4;                  // 32 KB: P^T / dS^T or dS
 // dK/dV: K, V resident; stages of {Q, dO} K-major + {Q, dO} MN-major
 constexpr int KV_SM_K = 0, KV_SM_V = BT_FULL, KV_SM_STAGE = 2 * BT_FULL, KV_STAGE = 4 * BT_HALF;
 constexpr int KV_SM_DS = KV_SM_STAGE + 2 * KV_STAGE, KV_SM_CTL = KV_SM_DS + BT_DS;
-constexpr int KV_SMEM = KV_SM_CTL + 128 + 1024;
+constexpr int KV_SMEM = KV_SM_CTL + 256 + 1024;
 // dQ: Q, dO resident; stages of {K, V} K-major + K MN-major
 constexpr int DQ_SM_Q = 0, DQ_SM_DO = BT_FULL, DQ_SM_STAGE = 2 * BT_FULL, DQ_STAGE = 3 * BT_HALF;
 constexpr int DQ_SM_DS = DQ_SM_STAGE + 2 * DQ_STAGE, DQ_SM_CTL = DQ_SM_DS + BT_DS;
-constexpr int DQ_SMEM = DQ_SM_CTL + 128 + 1024;
+constexpr int DQ_SMEM = DQ_SM_CTL + 256 + 1024;
 constexpr int BWD_WARPS = 16, BWD_TMA = 16, BWD_MMA = 17, BWD_THREADS = 18 * 32;
 constexpr float LOG2Ef = 1.4426950408889634f;
 
 struct BwdCtl {
     // st_*: ring of the K-major step operands (free once S / dP are done);
     // mn_*: ring of the MN-major step operands (free once the accumulating
-    // MMAs that read them are done)
+    // MMAs that read them are done). With P^T / dS in TMEM the compute warps
+    // arrive on a_full for even steps and b_full for odd ones.
     uint64_t in_full, st_full[2], st_empty[2], mn_full[2], mn_empty[2], sp_full[2], a_full, a_done, b_full,
         b_done, acc_done;
     uint32_t tmem_base;
     int abort;
 };
+static_assert(sizeof(BwdCtl) <= 256, "control block");
 
 enum : int { DEV_ERR_ATTB_TMA = 311, DEV_ERR_ATTB_MMA = 312, DEV_ERR_ATTB_CMP = 313 };
 
@@ -369,6 +456,19 @@ __device__ __forceinline__ void mma_k64(uint32_t d, uint32_t a, int a_kb, uint32
         }
 }
 
+// D (+)= A B^T over K = 64 with A in TMEM (128 lanes, columns a .. a + 63,
+// one fp32 element per column) and B MN-major at b (k-block stride 8192, dim
+// atoms 4096)
+__device__ __forceinline__ void mma_k64_ts(uint32_t d, uint32_t a, uint32_t b, uint32_t idesc, bool acc) {
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+            mma_tf32_ts(d, a + (uint32_t)(kb * 32 + kk * 8), smem_desc(b + kb * 8192 + kk * 1024, 4096, 512, 1),
+                        idesc, (acc || kb || kk) ? 1u : 0u);
+}
+
+template <bool TS>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
 attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_constant__ CUtensorMap tmQK64,
                         const __grid_constant__ CUtensorMap tmMN, const __grid_constant__ CUtensorMap tmDO64,
@@ -452,13 +552,26 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
             for (int s = 0; ok && s < ns; ++s) {
                 if (s + 1 < ns) {
                     if (!mbar_wait(&ctl->st_full[(s + 1) & 1], ((s + 1) >> 1) & 1, DEV_ERR_ATTB_MMA, abort)) break;
+                    // TS: step s + 1 overwrites the TMEM operands of step s - 1's
+                    // accumulating MMAs (not ordered against them): wait for those
+                    if (TS && s >= 1 &&
+                        !mbar_wait(&ctl->mn_empty[(s - 1) & 1], ((s - 1) >> 1) & 1, DEV_ERR_ATTB_MMA, abort))
+                        break;
                     tc_fence_after();
                     issue_sp(s + 1);
                 }
                 const uint32_t sg = smem_u32(stage(s & 1));
-                if (!mbar_wait(&ctl->a_full, s & 1, DEV_ERR_ATTB_MMA, abort)) break;  // P^T written
+                if (TS ? !mbar_wait((s & 1) ? &ctl->b_full : &ctl->a_full, (s >> 1) & 1, DEV_ERR_ATTB_MMA, abort)
+                       : !mbar_wait(&ctl->a_full, s & 1, DEV_ERR_ATTB_MMA, abort))
+                    break;  // P^T (TS: and dS^T) written
                 if (!mbar_wait(&ctl->mn_full[s & 1], (s >> 1) & 1, DEV_ERR_ATTB_MMA, abort)) break;
                 tc_fence_after();
+                if constexpr (TS) {  // P^T, dS^T in place of S^T, dP^T
+                    mma_k64_ts(tmem + 256, tmem + (s & 1) * 64, sg + 3 * BT_HALF, id_acc, s > 0);        // dV += P^T dO
+                    mma_k64_ts(tmem + 320, tmem + 128 + (s & 1) * 64, sg + 2 * BT_HALF, id_acc, s > 0);  // dK += dS^T Q
+                    mma_commit(&ctl->mn_empty[s & 1]);
+                    continue;
+                }
                 mma_k64(tmem + 256, dsa, BT_DS / 2, sg + 3 * BT_HALF, 0, true, id_acc, s > 0);  // dV += P^T dO
                 mma_commit(&ctl->a_done);
                 if (!mbar_wait(&ctl->b_full, s & 1, DEV_ERR_ATTB_MMA, abort)) break;  // dS^T written
@@ -497,6 +610,19 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
                 const float l2 = __shfl_sync(0xffffffffu, ld_, c), dd = __shfl_sync(0xffffffffu, ld_, 16 + c);
                 pv[c] = valid ? ex2f(sv[c] * sl2 - l2) : 0.f;
                 dsv[c] = pv[c] * (dp[c] - dd);
+            }
+            if constexpr (TS) {
+                // in place: S^T(s), dP^T(s) are not read again, and step s + 2
+                // overwrites them only after this step's dV / dK MMAs
+                tmem_st_32x32b_x16_nowait(tmem + lane_off + (uint32_t)((s & 1) * 64 + cq * 16), pv);
+                tmem_st_32x32b_x16_nowait(tmem + lane_off + (uint32_t)(128 + (s & 1) * 64 + cq * 16), dsv);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                // even / odd steps on separate barriers: nothing here waits for
+                // this step's MMAs, but step s + 2 needs them complete
+                if (lane == 0) mbar_arrive((s & 1) ? &ctl->b_full : &ctl->a_full);
+                continue;
             }
             // the dS^T of the previous step must have been read (dK MMA done)
             if (s > 0 && !mbar_wait(&ctl->b_done, (s - 1) & 1, DEV_ERR_ATTB_CMP, abort)) {
@@ -542,6 +668,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
     }
 }
 
+template <bool TS>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
 attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_constant__ CUtensorMap tmQK64,
                       const __grid_constant__ CUtensorMap tmMN, const __grid_constant__ CUtensorMap tmDO128,
@@ -623,13 +750,24 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_
             for (int s = 0; ok && s < ns; ++s) {
                 if (s + 1 < ns) {
                     if (!mbar_wait(&ctl->st_full[(s + 1) & 1], ((s + 1) >> 1) & 1, DEV_ERR_ATTB_MMA, abort)) break;
+                    // TS: step s + 1 overwrites the TMEM operands of step s - 1's
+                    // accumulating MMAs (not ordered against them): wait for those
+                    if (TS && s >= 1 &&
+                        !mbar_wait(&ctl->mn_empty[(s - 1) & 1], ((s - 1) >> 1) & 1, DEV_ERR_ATTB_MMA, abort))
+                        break;
                     tc_fence_after();
                     issue_sp(s + 1);
                 }
-                if (!mbar_wait(&ctl->a_full, s & 1, DEV_ERR_ATTB_MMA, abort)) break;  // dS written
+                if (TS ? !mbar_wait((s & 1) ? &ctl->b_full : &ctl->a_full, (s >> 1) & 1, DEV_ERR_ATTB_MMA, abort)
+                       : !mbar_wait(&ctl->a_full, s & 1, DEV_ERR_ATTB_MMA, abort))
+                    break;  // dS written
                 if (!mbar_wait(&ctl->mn_full[s & 1], (s >> 1) & 1, DEV_ERR_ATTB_MMA, abort)) break;
                 tc_fence_after();
-                mma_k64(tmem + 256, dsa, BT_DS / 2, smem_u32(stage(s & 1)) + 2 * BT_HALF, 0, true, id_acc, s > 0);
+                if constexpr (TS)  // dS in place of dP
+                    mma_k64_ts(tmem + 256, tmem + 128 + (s & 1) * 64, smem_u32(stage(s & 1)) + 2 * BT_HALF, id_acc,
+                               s > 0);
+                else
+                    mma_k64(tmem + 256, dsa, BT_DS / 2, smem_u32(stage(s & 1)) + 2 * BT_HALF, 0, true, id_acc, s > 0);
                 mma_commit(&ctl->a_done);
                 mma_commit(&ctl->mn_empty[s & 1]);
             }
@@ -658,6 +796,16 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_
                 const bool valid = qv && kf + c <= q;
                 const float p = valid ? ex2f(sv[c] * sl2 - l2) : 0.f;
                 dsv[c] = p * (dp[c] - dd);
+            }
+            if constexpr (TS) {
+                tmem_st_32x32b_x16_nowait(tmem + lane_off + (uint32_t)(128 + (s & 1) * 64 + cq * 16), dsv);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                // even / odd steps on separate barriers: nothing here waits for
+                // this step's MMAs, but step s + 2 needs them complete
+                if (lane == 0) mbar_arrive((s & 1) ? &ctl->b_full : &ctl->a_full);
+                continue;
             }
             if (s > 0 && !mbar_wait(&ctl->a_done, (s - 1) & 1, DEV_ERR_ATTB_CMP, abort)) {  // dQ MMA read dS
                 ok = false;
@@ -697,6 +845,19 @@ CG_DEV_ERROR_READER(attn_tc_take_dev_error)
 // TF32 causal attention forward on tcgen05; returns ERR_ARG (nothing
 // launched) when the shapes or alignment do not fit, so the caller can take
 // another kernel.
+// The forward and backward kernels keep P (and dS) in tensor memory, in place
+// of the scores they come from, and read them there as the A operand of the
+// following MMA; CNGPT_CUDA_ATTN_P_TMEM=0 stages them in shared memory instead
+// (the forward's output is bit-identical either way)
+static bool fwd_p_in_tmem() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("CNGPT_CUDA_ATTN_P_TMEM");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 int attention_fwd_tc(const float *qkv, float *out, float *lse, int B, int T, int C, int H, cudaStream_t s) {
     if (C / H != AHS || C % H != 0 || ((uintptr_t)qkv % 16) != 0 || ((uintptr_t)out % 16) != 0 ||
         (3L * C) % 4 != 0 || C % 4 != 0)
@@ -706,12 +867,16 @@ int attention_fwd_tc(const float *qkv, float *out, float *lse, int B, int T, int
     CG_TRY(make_tensor_map(&tv, qkv, 3L * C, (long)B * T, 3L * C, 32, 32, true));
     static bool attr = false;
     if (!attr) {
-        CG_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM));
+        CG_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM));
+        CG_CUDA(cudaFuncSetAttribute(attn_fwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM));
         attr = true;
     }
     const int nqt = (T + AQ - 1) / AQ;
     const float sl2 = (1.0f / sqrtf((float)AHS)) * 1.4426950408889634f;
-    attn_fwd_tc_kernel<<<nqt * B * H, ATT_THREADS, ATT_SMEM, s>>>(tqk, tv, out, lse, T, C, H, sl2);
+    if (fwd_p_in_tmem())
+        attn_fwd_tc_kernel<true><<<nqt * B * H, ATT_THREADS, ATT_SMEM, s>>>(tqk, tv, out, lse, T, C, H, sl2);
+    else
+        attn_fwd_tc_kernel<false><<<nqt * B * H, ATT_THREADS, ATT_SMEM, s>>>(tqk, tv, out, lse, T, C, H, sl2);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
     return OK;
@@ -734,18 +899,21 @@ int attention_bwd_tc(const float *qkv, const float *dout, const float *lse, cons
     CG_TRY(make_tensor_map(&domn, dout, C, rows, C, 32, 32, true));
     static bool attr = false;
     if (!attr) {
-        CG_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KV_SMEM));
-        CG_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM));
+        CG_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, KV_SMEM));
+        CG_CUDA(cudaFuncSetAttribute(attn_bwd_dkdv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, KV_SMEM));
+        CG_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM));
+        CG_CUDA(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM));
         attr = true;
     }
     const int nt = (T + 127) / 128;
     const float scale = 0.125f, sl2 = scale * LOG2Ef;  // 1 / sqrt(64)
-    attn_bwd_dkdv_tc_kernel<<<nt * B * H, BWD_THREADS, KV_SMEM, s>>>(qk128, qk64, mn, do64, domn, lse, D, dqkv, T,
-                                                                     C, H, sl2, scale);
+    const bool ts = fwd_p_in_tmem();
+    auto dkdv = ts ? attn_bwd_dkdv_tc_kernel<true> : attn_bwd_dkdv_tc_kernel<false>;
+    auto dq = ts ? attn_bwd_dq_tc_kernel<true> : attn_bwd_dq_tc_kernel<false>;
+    dkdv<<<nt * B * H, BWD_THREADS, KV_SMEM, s>>>(qk128, qk64, mn, do64, domn, lse, D, dqkv, T, C, H, sl2, scale);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
-    attn_bwd_dq_tc_kernel<<<nt * B * H, BWD_THREADS, DQ_SMEM, s>>>(qk128, qk64, mn, do128, lse, D, dqkv, T, C, H,
-                                                                   sl2, scale);
+    dq<<<nt * B * H, BWD_THREADS, DQ_SMEM, s>>>(qk128, qk64, mn, do128, lse, D, dqkv, T, C, H, sl2, scale);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
     return OK;
