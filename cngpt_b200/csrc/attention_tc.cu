@@ -233,9 +233,9 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
                 const bool diag = (j == qt);
                 const int kfirst = j * AK + cs * 32;
                 const uint32_t s_addr = tmem + lane_off + (uint32_t)(buf * AK + cs * 32);
-                float v[32];
                 float pm = -INFINITY;  // max of this slice's unscaled, unmasked scores
                 if (ok) {
+                    float v[32];
                     tc_fence_after();
                     tmem_ld_32x32b_x32(s_addr, v);
                     if (diag) {
@@ -254,14 +254,23 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQK, const __grid_consta
                 const float mraw = fmaxf(fmaxf(pb[r], pb[AQ + r]), fmaxf(pb[2 * AQ + r], pb[3 * AQ + r]));
                 const float m_new = fmaxf(m, mraw * sl2);  // sl2 > 0: max commutes with the scale
                 const float alpha = ex2f(m - m_new);
+                // P over S in two halves of 16 columns, the scores read again
+                // from TMEM (fewer live registers than holding all 32 across
+                // the barrier); the row sum keeps column order
                 float rs = 0.f;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float p = (diag && kfirst + i > q) ? 0.f : ex2f(v[i] * sl2 - m_new);
-                    v[i] = p;
-                    rs += p;
+                for (int hf = 0; hf < 2; ++hf) {
+                    float v[16];
+                    tmem_ld_32x32b_x16(s_addr + (uint32_t)(hf * 16), v);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float p = (diag && kfirst + hf * 16 + i > q) ? 0.f : ex2f(v[i] * sl2 - m_new);
+                        v[i] = p;
+                        rs += p;
+                    }
+                    tmem_st_32x32b_x16_nowait(s_addr + (uint32_t)(hf * 16), v);
                 }
-                tmem_st_32x32b_x32(s_addr, v);
+                tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ctl->p_full[buf]);
@@ -588,8 +597,18 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         uint8_t *ds = base + KV_SM_DS;
         const float *lse_bh = lse + (long)bh * T, *D_bh = Dd + (long)bh * T;
+        // lse and D of this warp's 16 queries of a step: one load per lane
+        // (lanes 0-15 lse, 16-31 D), handed out by shuffles; the next step's
+        // load is issued before this step's wait so its latency is hidden
+        auto lse_d = [&](int s) {
+            const int ql = k0 + s * BQS + cq * 16 + (lane & 15);
+            return ql < T ? ((lane < 16) ? lse_bh[ql] : D_bh[ql]) : 0.f;
+        };
+        float raw_next = lse_d(0);
         bool ok = true;
         for (int s = 0; s < ns; ++s) {
+            const float raw = raw_next;
+            if (s + 1 < ns) raw_next = lse_d(s + 1);
             if (!mbar_wait(&ctl->sp_full[s & 1], (s >> 1) & 1, DEV_ERR_ATTB_CMP, abort)) {
                 ok = false;
                 break;
@@ -599,10 +618,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __gri
             tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)((s & 1) * 64 + cq * 16), sv);
             tmem_ld_32x32b_x16(tmem + lane_off + (uint32_t)(128 + (s & 1) * 64 + cq * 16), dp);
             const int qf = k0 + s * BQS + cq * 16;
-            // lse and D of this warp's 16 queries: one load per lane (lanes
-            // 0-15 lse, 16-31 D), handed out by shuffles
-            const int ql = qf + (lane & 15);
-            const float ld_ = ql < T ? ((lane < 16) ? lse_bh[ql] * LOG2Ef : D_bh[ql]) : 0.f;
+            const float ld_ = (lane < 16) ? raw * LOG2Ef : raw;
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
                 const int q = qf + c;

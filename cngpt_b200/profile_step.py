@@ -5,6 +5,7 @@ for profilers (ncu) and quick timing.
                                       [--warmup 3] [--prec tf32|3xtf32|fp32]
     python -m cngpt_b200.profile_step --gemm M N K [--a-mn] [--b-mn] [--reps 3]
     python -m cngpt_b200.profile_step --decode xl|small [--B 1] [--T 128] [--new 8]
+    python -m cngpt_b200.profile_step --attention [--B 8] [--T 1024] [--heads 12] [--reps 10]
 
 Token ids live on the device before the first step; nothing else runs.
 """
@@ -43,6 +44,9 @@ def main() -> None:
     ap.add_argument("--decode", choices=["xl", "small"], help="greedy KV-cache decode of GPT-2 XL / small "
                     "(device-random weights): prefill B x T, then --new tokens")
     ap.add_argument("--new", type=int, default=8)
+    ap.add_argument("--attention", action="store_true", help="time one layer's causal attention forward and "
+                    "backward (head size 64) through the C ABI")
+    ap.add_argument("--heads", type=int, default=12)
     a = ap.parse_args()
     import torch
     torch.cuda.set_device(0)
@@ -74,6 +78,44 @@ def main() -> None:
         us = e0.elapsed_time(e1) * 1e3 / max(a.reps - 1, 1)
         print(f"gemm {M}x{N}x{K} a_mn={int(a.a_mn)} b_mn={int(a.b_mn)} epi={a.epi}: {us:.1f} us "
               f"({2.0 * M * N * K / us / 1e6:.1f} TFLOP/s, CUDA events, back to back)")
+        return
+    if a.attention:
+        B, T, H = a.B, a.T, a.heads
+        Cm = 64 * H
+        g = torch.Generator(device="cuda").manual_seed(1)
+        qkv = torch.randn(B, T, 3 * Cm, device="cuda", generator=g)
+        dout = torch.randn(B, T, Cm, device="cuda", generator=g)
+        out = torch.empty(B, T, Cm, device="cuda")
+        lse = torch.empty(B * H * T, device="cuda")
+        dqkv = torch.empty(B, T, 3 * Cm, device="cuda")
+
+        def fwd():
+            abi.check(lib, lib.cngpt_cuda_attention_fwd(qkv.data_ptr(), out.data_ptr(), lse.data_ptr(), B, T, Cm,
+                                                        H), "attention fwd")
+
+        def bwd():
+            abi.check(lib, lib.cngpt_cuda_attention_bwd(qkv.data_ptr(), out.data_ptr(), dout.data_ptr(),
+                                                        lse.data_ptr(), dqkv.data_ptr(), B, T, Cm, H),
+                      "attention bwd")
+
+        def time_us(f):
+            for _ in range(3):
+                f()
+            abi.check(lib, lib.cngpt_cuda_check(), "sync")
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = max(a.reps, 10)
+            e0.record()
+            for _ in range(n):
+                f()
+            e1.record()
+            abi.check(lib, lib.cngpt_cuda_check(), "sync")
+            return e0.elapsed_time(e1) * 1e3 / n
+
+        tf, tb = time_us(fwd), time_us(bwd)
+        flop = 4.0 * B * H * (T * (T + 1) / 2) * 64  # causal Q K^T and P V
+        print(f"attention B={B} T={T} H={H} hs=64 prec={a.prec}: forward {tf:.1f} us ({flop / tf / 1e6:.0f} "
+              f"TFLOP/s), backward {tb:.1f} us ({2.5 * flop / tb / 1e6:.0f} TFLOP/s incl. the rowsum(dO*O) pass; "
+              f"CUDA events, back to back, inputs L2-resident)")
         return
     if a.decode:
         L, H, Cm = (48, 25, 1600) if a.decode == "xl" else (12, 12, 768)
