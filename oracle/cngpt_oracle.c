@@ -4,7 +4,7 @@
  * TEST INFRASTRUCTURE ONLY (see cngpt_oracle.h). Plain loops over fp32
  * data; every matrix product (the reference's cblas_sgemm calls) sums along K
  * in a double accumulator and rounds once, so the oracle's own rounding error
- * stays well below the fp32 noise of the implementations it judges.
+ * stays well below the fp32 noise of the implementations it checks.
  * Parallelised over output rows with OpenMP so GPT-2-sized checks finish.
  */
 #include "cngpt_oracle.h"
