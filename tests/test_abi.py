@@ -148,3 +148,20 @@ def test_tp_plan_rejects_bad_rank():
     assert lib.cngpt_cuda_tp_plan(12, 768, 50257, 2, 2, p) == abi.ERR_ARG
     assert lib.cngpt_cuda_tp_plan(12, 770, 50257, 2, 0, p) == abi.ERR_ARG
     lib.cngpt_cuda_clear_status()
+
+
+def test_load_checkpoint_rejects_missing_and_foreign_files():
+    """The checkpoint loader checks the file before any device work: a missing
+    path and a file without the model-file magic are ERR_ARG with a message."""
+    lib = abi.load()
+    m = abi.GPT()
+    with tempfile.TemporaryDirectory() as d:
+        missing = str(Path(d) / "none.bin").encode()
+        assert lib.cngpt_cuda_load_checkpoint(C.byref(m), missing) == abi.ERR_ARG
+        assert "cannot open" in lib.cngpt_cuda_last_message().decode()
+        foreign = Path(d) / "foreign.bin"
+        foreign.write_bytes(b"\x00" * 1024)
+        assert lib.cngpt_cuda_load_checkpoint(C.byref(m), str(foreign).encode()) == abi.ERR_ARG
+        assert "not a cngpt model file" in lib.cngpt_cuda_last_message().decode()
+    assert not m.param_buf  # nothing was allocated
+    lib.cngpt_cuda_clear_status()
