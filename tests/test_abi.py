@@ -165,3 +165,24 @@ def test_load_checkpoint_rejects_missing_and_foreign_files():
         assert "not a cngpt model file" in lib.cngpt_cuda_last_message().decode()
     assert not m.param_buf  # nothing was allocated
     lib.cngpt_cuda_clear_status()
+
+
+def test_argument_errors_are_reported_before_device_work():
+    """Argument checks of the extension entry points run on the host: the
+    status is returned and the message recorded, with no device involved."""
+    lib = abi.load()
+    assert lib.cngpt_cuda_set_precision(7) == abi.ERR_ARG
+    assert "precision" in lib.cngpt_cuda_last_message().decode()
+    # unknown epilogue mode, and a residual epilogue without its operands
+    assert lib.cngpt_cuda_gemm(None, 4, 0, None, 4, 0, 4, 4, 4, 9, 1.0, None, 4, None, None, 0, None, 0, None,
+                               0) == abi.ERR_ARG
+    assert lib.cngpt_cuda_gemm(None, 4, 0, None, 4, 0, 4, 4, 4, abi.EPI_RESID, 1.0, None, 4, None, None, 0, None,
+                               0, None, 0) == abi.ERR_ARG
+    assert "missing epilogue operand" in lib.cngpt_cuda_last_message().decode()
+    # C not divisible by the head count
+    assert lib.cngpt_cuda_attention_fwd(None, None, None, 1, 8, 770, 12) == abi.ERR_ARG
+    # a GPT the library never initialised
+    m = abi.GPT()
+    uid = (C.c_ubyte * 128)()
+    assert lib.cngpt_cuda_dp_init(C.byref(m), uid, 2, 0) == abi.ERR_STATE
+    lib.cngpt_cuda_clear_status()
