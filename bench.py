@@ -186,21 +186,13 @@ def run_reference_arm(args) -> None:
 
 
 # ------------------------------------------------------------------ our arm
-def gemm_replay(lib, torch, dev, prec: int, iters: int) -> dict:
-    """Time the tcgen05 GEMM alone on one training step's GEMM shapes (same
-    operand majorness and epilogues as the model), CUDA events on the stream
-    the kernels run on (the legacy default stream)."""
+def step_gemm_shapes() -> list:
+    """The GEMMs of one GPT-2 small training step (B=8, T=1024) in model
+    order, as (M, N, K, a_mn, b_mn, lda, ldb, epilogue, ldd): per layer the
+    forward qkv / c_proj / fc / proj and the backward dX / dW pairs, then the
+    tied LM head forward, dX and dW."""
     from cngpt_b200 import abi
     BT, Vp = B_ * T_, (V_ + 3) & ~3
-    f = lambda *s: torch.randn(*s, device=dev) * 0.02  # noqa: E731
-    X = f(BT, 4 * C_)
-    W = f(V_, C_)
-    Y = torch.empty(BT, Vp, device=dev)
-    DL = f(BT, Vp)
-    Dw = torch.zeros(V_, C_, device=dev)
-    bias = torch.zeros(4 * C_, device=dev)
-    G = f(BT, 4 * C_)
-    # (M, N, K, a_mn, b_mn, lda, ldb, epi, ldd)
     shapes = []
     for _ in range(L_):
         shapes += [(BT, 3 * C_, C_, 0, 0, C_, C_, abi.EPI_STORE, 3 * C_),
@@ -218,6 +210,24 @@ def gemm_replay(lib, torch, dev, prec: int, iters: int) -> dict:
     shapes += [(BT, V_, C_, 0, 0, C_, C_, abi.EPI_STORE, V_),
                (BT, C_, V_, 0, 1, Vp, C_, abi.EPI_STORE, C_),
                (V_, C_, BT, 1, 1, Vp, C_, abi.EPI_ACCUM, C_)]
+    return shapes
+
+
+def gemm_replay(lib, torch, dev, prec: int, iters: int) -> dict:
+    """Time the tcgen05 GEMM alone on one training step's GEMM shapes (same
+    operand majorness and epilogues as the model), CUDA events on the stream
+    the kernels run on (the legacy default stream)."""
+    from cngpt_b200 import abi
+    BT, Vp = B_ * T_, (V_ + 3) & ~3
+    f = lambda *s: torch.randn(*s, device=dev) * 0.02  # noqa: E731
+    X = f(BT, 4 * C_)
+    W = f(V_, C_)
+    Y = torch.empty(BT, Vp, device=dev)
+    DL = f(BT, Vp)
+    Dw = torch.zeros(V_, C_, device=dev)
+    bias = torch.zeros(4 * C_, device=dev)
+    G = f(BT, 4 * C_)
+    shapes = step_gemm_shapes()
     flops = sum(2.0 * M * N * K for (M, N, K, *_r) in shapes)
     lib.cngpt_cuda_set_precision(prec)
 

@@ -6,6 +6,7 @@ for profilers (ncu) and quick timing.
     python -m cngpt_b200.profile_step --gemm M N K [--a-mn] [--b-mn] [--reps 3]
     python -m cngpt_b200.profile_step --decode xl|small [--B 1] [--T 128] [--new 8]
     python -m cngpt_b200.profile_step --attention [--B 8] [--T 1024] [--heads 12] [--reps 10]
+    python -m cngpt_b200.profile_step --gemm-step [--reps 10] [--prec tf32]
 
 Token ids live on the device before the first step; nothing else runs.
 """
@@ -47,6 +48,8 @@ def main() -> None:
     ap.add_argument("--attention", action="store_true", help="time one layer's causal attention forward and "
                     "backward (head size 64) through the C ABI")
     ap.add_argument("--heads", type=int, default=12)
+    ap.add_argument("--gemm-step", action="store_true", help="time each distinct GEMM shape of one GPT-2 small "
+                    "training step (B=8, T=1024) alone and print its share of the step's GEMM time")
     a = ap.parse_args()
     import torch
     torch.cuda.set_device(0)
@@ -78,6 +81,54 @@ def main() -> None:
         us = e0.elapsed_time(e1) * 1e3 / max(a.reps - 1, 1)
         print(f"gemm {M}x{N}x{K} a_mn={int(a.a_mn)} b_mn={int(a.b_mn)} epi={a.epi}: {us:.1f} us "
               f"({2.0 * M * N * K / us / 1e6:.1f} TFLOP/s, CUDA events, back to back)")
+        return
+    if a.gemm_step:
+        import bench  # the step's GEMM shapes (repository root is on sys.path)
+        shapes = bench.step_gemm_shapes()
+        BT, V, Cm = bench.B_ * bench.T_, bench.V_, bench.C_
+        Vp = (V + 3) & ~3
+        g = torch.Generator(device="cuda").manual_seed(0)
+        f = lambda *sh: torch.randn(*sh, device="cuda", generator=g) * 0.02  # noqa: E731
+        X, W, DL, G = f(BT, 4 * Cm), f(V, Cm), f(BT, Vp), f(BT, 4 * Cm)
+        Y = torch.empty(BT, Vp, device="cuda")
+        Dw = torch.zeros(V, Cm, device="cuda")
+        bias = torch.zeros(4 * Cm, device="cuda")
+        counts: dict = {}
+        for sh in shapes:
+            counts[sh] = counts.get(sh, 0) + 1
+        names = {abi.EPI_STORE: "store", abi.EPI_ACCUM: "accum", abi.EPI_GELU: "gelu", abi.EPI_RESID: "resid",
+                 abi.EPI_GELU_BWD: "gelu_bwd"}
+        n = max(a.reps, 10)
+        rows = []
+        for sh, cnt in counts.items():
+            M, N, K, amn, bmn, lda, ldb, epi, ldd = sh
+            A_ = DL if lda == Vp else X
+            B_ = W if ((not bmn and N == V) or (bmn and K == V)) else X
+            D_ = Dw if epi == abi.EPI_ACCUM and M == V else Y
+
+            def one():
+                abi.check(lib, lib.cngpt_cuda_gemm(A_.data_ptr(), lda, amn, B_.data_ptr(), ldb, bmn, M, N, K, epi,
+                                                   1.0, D_.data_ptr(), ldd,
+                                                   bias.data_ptr() if epi in (abi.EPI_RESID, abi.EPI_GELU) else None,
+                                                   G.data_ptr(), ldd, G.data_ptr(), ldd, G.data_ptr(), ldd), "gemm")
+            for _ in range(2):
+                one()
+            abi.check(lib, lib.cngpt_cuda_check(), "sync")
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                one()
+            e1.record()
+            abi.check(lib, lib.cngpt_cuda_check(), "sync")
+            rows.append((sh, cnt, e0.elapsed_time(e1) * 1e3 / n))
+        total = sum(us * cnt for _, cnt, us in rows)
+        flops = sum(2.0 * M * N * K * cnt for (M, N, K, *_r), cnt, _us in rows)
+        print(f"{'M':>6} {'N':>6} {'K':>6} mn  epilogue  count      us  TFLOP/s  share")
+        for (M, N, K, amn, bmn, _la, _lb, epi, _ld), cnt, us in sorted(rows, key=lambda r: -r[1] * r[2]):
+            print(f"{M:>6} {N:>6} {K:>6} {amn}{bmn}  {names[epi]:<8} {cnt:>5} {us:>8.1f} {2.0 * M * N * K / us / 1e6:>8.1f}"
+                  f"  {100.0 * us * cnt / total:5.1f}%")
+        print(f"{len(shapes)} GEMMs, {total / 1e3:.2f} ms per step timed shape by shape, {flops / total / 1e6:.1f} "
+              f"TFLOP/s (prec={a.prec}; CUDA events, back to back, each shape alone)")
         return
     if a.attention:
         B, T, H = a.B, a.T, a.heads

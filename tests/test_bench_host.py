@@ -66,3 +66,11 @@ def test_clock_record_parsing():
     assert s["reasons"] == ["sw_power_cap"]
     c.lines.append("0, 1200, 1965, 700.0, 0x0000000000000008, Active, Not Active, Not Active, Not Active")
     assert "hw_slowdown" in c.summary()["reasons"]
+
+
+def test_step_gemm_shapes_cover_the_step():
+    """The replayed GEMM list is the step's: 147 launches (12 per layer + the
+    LM head's three) whose FLOPs are step_flops()'s GEMM part."""
+    shapes = bench.step_gemm_shapes()
+    assert len(shapes) == 12 * bench.L_ + 3 and len(set(shapes)) == 15
+    assert sum(2.0 * M * N * K for (M, N, K, *_r) in shapes) == pytest.approx(bench.step_flops(8, 1024)["gemm"])
