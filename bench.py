@@ -162,9 +162,33 @@ def cpu_reference_step_sample(steps: int, warmup: int, threads: int) -> dict:
     lib.gpt_free(C.byref(m))
     t = float(np.mean(times))
     return {"value": T_ / t, "unit": "tokens/s", "cores": threads, "kind": "reference",
-            "sample": f"{steps} timed step(s) after {warmup} warm-up of 1 sequence (B=1, T=1024) of the "
-                      f"B=8 workload, OpenBLAS threads={threads}, last loss {loss:.4f}",
-            "s_per_step": t}
+            "sample": f"per-token rate of a B=1 sample: {steps} timed step(s) after {warmup} warm-up, each one "
+                      f"sequence (B=1, T=1024, 1024 tokens) of the B=8 workload through the reference's "
+                      f"gpt_zero_grad/gpt_forward/gpt_backward/gpt_adamw, OpenBLAS threads={threads}, "
+                      f"last loss {loss:.4f} (a full B=8 step is 8 such sequences; CPU tokens/s do not grow "
+                      f"with B)",
+            "s_per_step": t, "host": host_cpu()}
+
+
+def host_cpu() -> dict:
+    """lscpu's socket / core / thread counts and model name of this host."""
+    info = {"threads": os.cpu_count()}
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+    except (OSError, subprocess.SubprocessError):
+        return info
+    kv = {}
+    for ln in out.splitlines():
+        if ":" in ln:
+            k, v = ln.split(":", 1)
+            kv[k.strip()] = v.strip()
+    try:
+        cores = int(kv.get("Core(s) per socket", "0")) * int(kv.get("Socket(s)", "0"))
+        info["physical_cores"] = cores or None
+    except ValueError:
+        pass
+    info["model"] = kv.get("Model name")
+    return info
 
 
 def run_reference_arm(args) -> None:
@@ -179,7 +203,7 @@ def run_reference_arm(args) -> None:
             "ms_per_step": cb["s_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic (reference LCG token ids)",
             "config": bench_config(world),
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "host")},
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -616,8 +640,8 @@ def run_ours(args) -> None:
         line["other_train_configs"] = train_configs_bench(lib, torch, dev, world, rank, barrier, max_over_ranks,
                                                           tf32_peak)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_reference_step_sample(1, 1, os.cpu_count() or 1)
-        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cb = cpu_reference_step_sample(3, 1, os.cpu_count() or 1)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "host")}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

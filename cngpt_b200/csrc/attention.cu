@@ -21,7 +21,7 @@
 
 namespace cg {
 
-CG_DEV_ERROR_READER(attn_take_dev_error)
+CG_DEV_ERROR_ACCESSORS(attn_take_dev_error, attn_set_wait_limit)
 
 namespace {
 

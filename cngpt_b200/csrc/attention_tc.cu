@@ -856,7 +856,7 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQK128, const __grid_
 
 }  // namespace
 
-CG_DEV_ERROR_READER(attn_tc_take_dev_error)
+CG_DEV_ERROR_ACCESSORS(attn_tc_take_dev_error, attn_tc_set_wait_limit)
 
 // TF32 causal attention forward on tcgen05; returns ERR_ARG (nothing
 // launched) when the shapes or alignment do not fit, so the caller can take

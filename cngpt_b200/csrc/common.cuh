@@ -4,7 +4,7 @@
 // loads only into its own shared memory), and the tcgen05 tensor-memory / MMA
 // instructions, plus
 // the library-wide error channel. Every spin-wait here is bounded: after
-// kWaitLimitNs of global time it records an error code in g_cngpt_dev_error
+// g_cngpt_wait_limit_ns of global time it records an error code in g_cngpt_dev_error
 // and returns false so the kernel can wind down instead of hanging the GPU.
 #pragma once
 
@@ -15,22 +15,28 @@
 
 namespace cg {
 
-// Device-side error word, read by the host after each synchronising call.
-// Each translation unit that launches kernels with bounded waits has its own
-// copy (no relocatable device code) and exports a reader via
-// CG_DEV_ERROR_READER.
+// Device-side error word, read by the host after each synchronising call,
+// and the limit of every bounded wait. Each translation unit that launches
+// kernels with bounded waits has its own copy of both (no relocatable device
+// code) and exports a reader of the word and a setter of the limit via
+// CG_DEV_ERROR_ACCESSORS.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // default: 2 s per wait
 static __device__ int g_cngpt_dev_error = 0;
+static __device__ unsigned long long g_cngpt_wait_limit_ns = kWaitLimitNs;
 
-#define CG_DEV_ERROR_READER(fn)                                                     \
-    int fn() {                                                                      \
-        int code = 0, zero = 0;                                                     \
+#define CG_DEV_ERROR_ACCESSORS(reader, limit_setter)                                    \
+    int reader() {                                                                      \
+        int code = 0, zero = 0;                                                         \
         if (cudaMemcpyFromSymbol(&code, g_cngpt_dev_error, sizeof(int)) != cudaSuccess) \
-            return -1;                                                              \
-        if (code) cudaMemcpyToSymbol(g_cngpt_dev_error, &zero, sizeof(int));        \
-        return code;                                                                \
+            return -1;                                                                  \
+        if (code) cudaMemcpyToSymbol(g_cngpt_dev_error, &zero, sizeof(int));            \
+        return code;                                                                    \
+    }                                                                                   \
+    int limit_setter(unsigned long long ns) {                                           \
+        return cudaMemcpyToSymbol(g_cngpt_wait_limit_ns, &ns, sizeof(ns)) == cudaSuccess  \
+                   ? 0                                                                  \
+                   : -1;                                                                \
     }
-
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
@@ -75,17 +81,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete. Returns false
-// (and records `code`) if it did not complete within kWaitLimitNs, or if
+// (and records `code`) if it did not complete within the wait limit, or if
 // *abort was raised by another role of the same CTA.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code,
                                           volatile int *abort) {
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t0 = globaltimer_ns();
+    const uint64_t t0 = globaltimer_ns();
+    const uint64_t limit = *(volatile unsigned long long *)&g_cngpt_wait_limit_ns;
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 255u) == 0u) {
             if (abort && *abort) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > limit) {
                 record_error(code);
                 if (abort) *abort = 1;
                 return false;

@@ -119,11 +119,15 @@ extern "C" int cngpt_cuda_dp_init(GPT *m, const unsigned char id[128], int world
         set_last_error(ERR_ARG, "dp_init: rank %d / world %d", rank, world);
         return ERR_ARG;
     }
-    if (world == 1) {
-        c->world = 1;
-        c->rank = 0;
-        return OK;
+    // a second dp_init replaces the communicator of the first
+    if (c->nccl_comm) {
+        cudaStreamSynchronize(g_stream);
+        nccl_comm_destroy(c->nccl_comm);
+        c->nccl_comm = nullptr;
     }
+    c->world = 1;
+    c->rank = 0;
+    if (world == 1) return OK;
     void *comm = nullptr;
     CG_TRY(nccl_comm_init(&comm, id, world, rank));
     c->nccl_comm = comm;

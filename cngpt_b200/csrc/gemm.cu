@@ -43,7 +43,7 @@ namespace cg {
 
 unsigned long long g_launch_count = 0;
 
-CG_DEV_ERROR_READER(gemm_take_dev_error)
+CG_DEV_ERROR_ACCESSORS(gemm_take_dev_error, gemm_set_wait_limit)
 
 namespace {
 

@@ -38,6 +38,13 @@ int gemm_take_dev_error();
 int attn_take_dev_error();
 int tp_take_dev_error();
 int attn_tc_take_dev_error();
+// set the limit of every bounded device wait of one translation unit (0 on
+// success); set_wait_limit_ns sets all of them
+int gemm_set_wait_limit(unsigned long long ns);
+int attn_set_wait_limit(unsigned long long ns);
+int tp_set_wait_limit(unsigned long long ns);
+int attn_tc_set_wait_limit(unsigned long long ns);
+int set_wait_limit_ns(unsigned long long ns);
 
 #define CG_CUDA(call)                                                                 \
     do {                                                                              \

@@ -632,8 +632,17 @@ int layernorm_fwd(const float *x, long ldx, const float *w, const float *b, floa
 
 constexpr int kLnBwdRowsPerChunk = 128;
 
+// Rows per dw/db partial chunk: the requested count, raised where needed so
+// that the chunks fit the grid's y dimension (65535).
+static int ln_bwd_chunk_rows(int T, int rows_per_chunk) {
+    if (rows_per_chunk <= 0) rows_per_chunk = kLnBwdRowsPerChunk;
+    const int min_rows = (int)(((long)T + 65534) / 65535);
+    return std::max(rows_per_chunk, min_rows);
+}
+
 size_t layernorm_bwd_scratch_bytes(int T, int C, int rows_per_chunk) {
-    const long chunks = (T + rows_per_chunk - 1) / rows_per_chunk;
+    rows_per_chunk = ln_bwd_chunk_rows(T, rows_per_chunk);
+    const long chunks = ((long)T + rows_per_chunk - 1) / rows_per_chunk;
     return (size_t)chunks * 2 * C * sizeof(float);
 }
 
@@ -643,10 +652,10 @@ int layernorm_bwd(const float *dout, const float *x, const float *w, const float
                   float *dx, float *dw, float *db, int T, int C, float *scratch, cudaStream_t s,
                   int rows_per_chunk) {
     if (T <= 0) return OK;
-    if (rows_per_chunk <= 0) rows_per_chunk = kLnBwdRowsPerChunk;
+    rows_per_chunk = ln_bwd_chunk_rows(T, rows_per_chunk);
     layernorm_bwd_dx_kernel<<<grid_for(T, 8, 148 * 16), 256, 0, s>>>(dout, x, w, mean, rstd, dx, T, C);
     LAUNCH_CHECK();
-    const int chunks = (T + rows_per_chunk - 1) / rows_per_chunk;
+    const int chunks = (int)(((long)T + rows_per_chunk - 1) / rows_per_chunk);
     dim3 g((C + 255) / 256, chunks);
     layernorm_bwd_dwdb_kernel<<<g, 256, 0, s>>>(dout, x, mean, rstd, scratch, T, C, rows_per_chunk);
     LAUNCH_CHECK();

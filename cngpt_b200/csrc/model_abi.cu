@@ -692,6 +692,8 @@ extern "C" int cngpt_cuda_save_checkpoint(GPT *m, const char *path) {
     return OK;
 }
 
+// The whole file is read and checked on the host before anything reaches the
+// device, so a truncated or foreign file leaves the model as it was.
 extern "C" int cngpt_cuda_load_checkpoint(GPT *m, const char *path) {
     FILE *f = fopen(path, "rb");
     if (!f) {
@@ -704,43 +706,51 @@ extern "C" int cngpt_cuda_load_checkpoint(GPT *m, const char *path) {
         set_last_error(ERR_ARG, "load_checkpoint: %s is not a cngpt model file", path);
         return ERR_ARG;
     }
-    if (!m->param_buf) {
-        GPTConfig cfg = {hdr.n_layer, hdr.n_head, hdr.n_embd, hdr.vocab_size, hdr.block_size, 0.0f};
-        if (gpt_init(m, cfg) != 0) {
-            fclose(f);
-            return ERR_ALLOC;
-        }
-    } else if (hdr.n_layer != m->cfg.n_layer || hdr.n_head != m->cfg.n_head || hdr.n_embd != m->cfg.n_embd ||
-               hdr.vocab_size != m->cfg.vocab_size || hdr.block_size != m->cfg.block_size) {
+    if (m->param_buf && (hdr.n_layer != m->cfg.n_layer || hdr.n_head != m->cfg.n_head ||
+                         hdr.n_embd != m->cfg.n_embd || hdr.vocab_size != m->cfg.vocab_size ||
+                         hdr.block_size != m->cfg.block_size)) {
         fclose(f);
         set_last_error(ERR_ARG, "load_checkpoint: %s holds a different configuration", path);
         return ERR_ARG;
     }
-    const size_t n = (size_t)m->n_params;
-    std::vector<float> h(n);
+    GPTConfig cfg = {hdr.n_layer, hdr.n_head, hdr.n_embd, hdr.vocab_size, hdr.block_size, 0.0f};
+    if (hdr.n_layer < 0 || hdr.n_head <= 0 || hdr.n_embd <= 0 || hdr.vocab_size <= 0 || hdr.block_size <= 0) {
+        fclose(f);
+        set_last_error(ERR_ARG, "load_checkpoint: %s has an invalid configuration", path);
+        return ERR_ARG;
+    }
+    const size_t n = (size_t)gpt_num_params(&cfg);
+    std::vector<float> params(n), mom1, mom2;
     uint32_t magic = 0;
     int32_t step = 0;
-    int st = read_all(f, h.data(), n * 4);
-    if (st == 0 && cudaMemcpy(m->param_buf, h.data(), n * 4, cudaMemcpyHostToDevice) != cudaSuccess) st = -2;
-    const bool has_opt = st == 0 && read_all(f, &magic, 4) == 0 && magic == kOptMagic && read_all(f, &step, 4) == 0;
-    if (st == 0) {
+    bool ok = read_all(f, params.data(), n * 4) == 0;
+    bool has_opt = false;
+    if (ok && read_all(f, &magic, 4) == 0) {
+        // a trailer that starts must be complete
+        has_opt = magic == kOptMagic;
         if (has_opt) {
-            float *dst[2] = {m->m_buf, m->v_buf};
-            for (int i = 0; i < 2 && st == 0; ++i) {
-                st = read_all(f, h.data(), n * 4);
-                if (st == 0 && cudaMemcpy(dst[i], h.data(), n * 4, cudaMemcpyHostToDevice) != cudaSuccess) st = -2;
-            }
-            if (st == 0) m->step = step;
-        } else if (cudaMemset(m->m_buf, 0, n * 4) != cudaSuccess || cudaMemset(m->v_buf, 0, n * 4) != cudaSuccess) {
-            st = -2;
-        } else {
-            m->step = 0;  // a plain gpt_save file: fresh optimizer state
+            mom1.resize(n);
+            mom2.resize(n);
+            ok = read_all(f, &step, 4) == 0 && read_all(f, mom1.data(), n * 4) == 0 &&
+                 read_all(f, mom2.data(), n * 4) == 0;
         }
     }
     fclose(f);
-    if (st != 0) {
-        set_last_error(st == -2 ? ERR_CUDA : ERR_ARG, "load_checkpoint: reading %s failed", path);
-        return st == -2 ? ERR_CUDA : ERR_ARG;
+    if (!ok) {
+        set_last_error(ERR_ARG, "load_checkpoint: %s is truncated", path);
+        return ERR_ARG;
+    }
+    if (!m->param_buf && gpt_init(m, cfg) != 0) return ERR_ALLOC;
+    CG_CUDA(cudaStreamSynchronize(g_stream));
+    CG_CUDA(cudaMemcpy(m->param_buf, params.data(), n * 4, cudaMemcpyHostToDevice));
+    if (has_opt) {
+        CG_CUDA(cudaMemcpy(m->m_buf, mom1.data(), n * 4, cudaMemcpyHostToDevice));
+        CG_CUDA(cudaMemcpy(m->v_buf, mom2.data(), n * 4, cudaMemcpyHostToDevice));
+        m->step = step;
+    } else {  // a plain gpt_save file: fresh optimizer state
+        CG_CUDA(cudaMemset(m->m_buf, 0, n * 4));
+        CG_CUDA(cudaMemset(m->v_buf, 0, n * 4));
+        m->step = 0;
     }
     return OK;
 }

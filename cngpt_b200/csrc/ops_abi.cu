@@ -406,6 +406,12 @@ extern "C" int cngpt_cuda_set_managed(int on) {
 
 extern "C" unsigned long long cngpt_cuda_launch_count(void) { return g_launch_count; }
 
+extern "C" int cngpt_cuda_set_wait_limit_ns(unsigned long long ns) {
+    // the device variables are read by kernels in flight: finish them first
+    CG_CUDA(cudaDeviceSynchronize());
+    return set_wait_limit_ns(ns ? ns : kWaitLimitNs);
+}
+
 extern "C" int cngpt_cuda_gemm(const float *A, long lda, int a_mn, const float *B, long ldb, int b_mn,
                                int M, int N, int K, int epi_mode, float alpha, float *D, long ldd,
                                const float *bias, float *D2, long ldd2, const float *R, long ldr,

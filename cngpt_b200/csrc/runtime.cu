@@ -52,6 +52,17 @@ int check_device_error() {
     return OK;
 }
 
+int set_wait_limit_ns(unsigned long long ns) {
+    int (*setters[])(unsigned long long) = {gemm_set_wait_limit, attn_set_wait_limit, tp_set_wait_limit,
+                                            attn_tc_set_wait_limit};
+    for (auto set : setters)
+        if (set(ns) != 0) {
+            set_last_error(ERR_CUDA, "setting the device wait limit failed");
+            return ERR_CUDA;
+        }
+    return OK;
+}
+
 int precision() { return g_precision; }
 void set_precision(int p) { g_precision = p; }
 

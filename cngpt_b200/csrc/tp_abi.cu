@@ -38,7 +38,7 @@ extern "C" {
 
 namespace cg {
 
-CG_DEV_ERROR_READER(tp_take_dev_error)
+CG_DEV_ERROR_ACCESSORS(tp_take_dev_error, tp_set_wait_limit)
 
 namespace {
 
@@ -151,8 +151,9 @@ __global__ void tp_argmax_merge_kernel(const int *__restrict__ gath, int B, int 
 // x[m, :] = sum over ranks r, in rank order, of the partial row rank r pushed
 // into this rank's receive slot (identical on every rank), then the LayerNorm
 // statistics of x for the next LayerNorm-fused GEMV. One block per row. The
-// peers' flags are awaited with a bounded spin (2 s of %globaltimer); on
-// expiry the block records DEV_ERR_TP_FLAG and leaves x unchanged.
+// peers' flags are awaited with a bounded spin (the wait limit, 2 s of
+// %globaltimer by default); on expiry the block records DEV_ERR_TP_FLAG and
+// leaves x unchanged.
 __global__ void __launch_bounds__(256)
 tp_reduce_kernel(char *__restrict__ buf, int world, int C, const int *__restrict__ step, int nk, int k,
                  float *__restrict__ x, float *__restrict__ stats) {
@@ -166,11 +167,12 @@ tp_reduce_kernel(char *__restrict__ buf, int world, int C, const int *__restrict
     if ((int)threadIdx.x < world) {
         const unsigned long long *flag = (const unsigned long long *)buf + threadIdx.x;
         const uint64_t t0 = globaltimer_ns();
+        const uint64_t limit = *(volatile unsigned long long *)&g_cngpt_wait_limit_ns;
         for (unsigned it = 0;; ++it) {
             unsigned long long v;
             asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
             if (v >= ep) break;
-            if ((it & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) {
+            if ((it & 255u) == 255u && globaltimer_ns() - t0 > limit) {
                 record_error(DEV_ERR_TP_FLAG);
                 ok = 0;
                 break;
@@ -760,6 +762,48 @@ extern "C" int cngpt_cuda_tp_generate(GPT *m, const int *prompt, int B, int T, i
     for (int b = 0; b < B; ++b)
         for (int i = 0; i < n_new; ++i) out_tokens[(size_t)b * n_new + i] = h[(size_t)i * B + b];
     return OK;
+}
+
+// Self-test of the decode exchange's bounded wait on one GPU: a receive
+// buffer of world 1 holds `partial` [rows, C] in the slot of exchange 1, and
+// its flag is raised to that exchange only when `publish` is set. Without it
+// nothing ever publishes, so tp_reduce_kernel's wait runs out after the wait
+// limit (cngpt_cuda_set_wait_limit_ns), records DEV_ERR_TP_FLAG and leaves x
+// untouched; the call then returns CNGPT_ERR_DEVICE_WAIT.
+extern "C" int cngpt_cuda_selftest_tp_reduce(float *x, const float *partial, int rows, int C, int publish,
+                                             float *stats) {
+    if (rows < 1 || rows > TP_MAX_ROWS || C < 1 || C > 8 * 256 || !x || !partial || !stats ||
+        mem_kind(x) == MEM_HOST || mem_kind(partial) == MEM_HOST || mem_kind(stats) == MEM_HOST) {
+        set_last_error(ERR_ARG, "selftest_tp_reduce: rows=%d (1..%d), C=%d (1..2048), device pointers", rows,
+                       TP_MAX_ROWS, C);
+        return ERR_ARG;
+    }
+    cudaStream_t s = g_stream;
+    char *buf = nullptr;
+    int *step = nullptr;
+    const size_t bytes = tp_buf_bytes(1, C);
+    CG_TRY(dev_alloc((void **)&buf, bytes, false));
+    int st = dev_alloc((void **)&step, sizeof(int), false);
+    const unsigned long long flag = publish ? 1ull : 0ull;
+    if (st == OK &&
+        (cudaMemsetAsync(buf, 0, bytes, s) != cudaSuccess || cudaMemsetAsync(step, 0, sizeof(int), s) != cudaSuccess ||
+         cudaMemcpyAsync(tp_slot(buf, 1, C, 1, 0), partial, (size_t)rows * C * 4, cudaMemcpyDeviceToDevice, s) !=
+             cudaSuccess ||
+         cudaMemcpyAsync(buf, &flag, sizeof(flag), cudaMemcpyHostToDevice, s) != cudaSuccess)) {
+        set_last_error(ERR_CUDA, "selftest_tp_reduce: buffer set-up failed");
+        st = ERR_CUDA;
+    }
+    if (st == OK) {
+        tp_reduce_kernel<<<rows, 256, 0, s>>>(buf, 1, C, step, 1, 0, x, stats);
+        ++g_launch_count;
+        if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) {
+            set_last_error(ERR_CUDA, "selftest_tp_reduce: launch failed");
+            st = ERR_CUDA;
+        }
+    }
+    dev_free(buf);
+    dev_free(step);
+    return st != OK ? st : check_device_error();
 }
 
 extern "C" int cngpt_cuda_tp_free(GPT *m) {

@@ -50,6 +50,13 @@ void *cngpt_cuda_get_stream(void);
 int   cngpt_cuda_set_managed(int on);
 /* number of kernels this library has launched so far */
 unsigned long long cngpt_cuda_launch_count(void);
+/* limit of every bounded device-side wait (mbarrier phases in the GEMM and
+ * attention kernels, peer flags of the tensor-parallel exchange), in
+ * nanoseconds of %globaltimer; 0 restores the default of 2 s. A wait that
+ * runs out records its site, ends its kernel without writing the output it
+ * waited for, and the next cngpt_cuda_check returns CNGPT_ERR_DEVICE_WAIT.
+ * Synchronises the device first. */
+int   cngpt_cuda_set_wait_limit_ns(unsigned long long ns);
 
 /* ---- GEMM with fused epilogue --------------------------------------------
  * out[M,N] = alpha * op(A)[M,K] op(B)[N,K]^T, then the epilogue:
@@ -168,6 +175,16 @@ int cngpt_cuda_tp_forward_last(GPT *m, const int *tokens, int B, int T, float *l
 /* cngpt_cuda_generate split over the ranks; out_tokens (host) on every rank */
 int cngpt_cuda_tp_generate(GPT *m, const int *prompt, int B, int T, int n_new, int *out_tokens);
 int cngpt_cuda_tp_free(GPT *m);
+
+/* ---- self-test hooks -------------------------------------------------------
+ * One launch of the tensor-parallel decode exchange's reduce kernel on one
+ * GPU, over a receive buffer of world 1 that holds partial [rows, C] (device;
+ * rows <= 8, C <= 2048) for exchange 1. publish = 1 raises the buffer's flag
+ * to that exchange: x [rows, C] becomes the partial and stats [rows][2] its
+ * LayerNorm mean / rstd. publish = 0 leaves the flag unraised, so the wait runs
+ * out after the wait limit: x and stats are left untouched and the call
+ * returns CNGPT_ERR_DEVICE_WAIT (site 201). Allocates and frees its buffer. */
+int cngpt_cuda_selftest_tp_reduce(float *x, const float *partial, int rows, int C, int publish, float *stats);
 
 #ifdef __cplusplus
 }

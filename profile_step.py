@@ -1,12 +1,12 @@
 """Run a few GPT-2 training steps (or one GEMM shape) through libcngpt_cuda,
 for profilers (ncu) and quick timing.
 
-    python -m cngpt_b200.profile_step [--B 8] [--T 1024] [--layers 12] [--steps 1]
+    python profile_step.py [--B 8] [--T 1024] [--layers 12] [--steps 1]
                                       [--warmup 3] [--prec tf32|3xtf32|fp32]
-    python -m cngpt_b200.profile_step --gemm M N K [--a-mn] [--b-mn] [--reps 3]
-    python -m cngpt_b200.profile_step --decode xl|small [--B 1] [--T 128] [--new 8]
-    python -m cngpt_b200.profile_step --attention [--B 8] [--T 1024] [--heads 12] [--reps 10]
-    python -m cngpt_b200.profile_step --gemm-step [--reps 10] [--prec tf32]
+    python profile_step.py --gemm M N K [--a-mn] [--b-mn] [--reps 3]
+    python profile_step.py --decode xl|small [--B 1] [--T 128] [--new 8]
+    python profile_step.py --attention [--B 8] [--T 1024] [--heads 12] [--reps 10]
+    python profile_step.py --gemm-step [--reps 10] [--prec tf32]
 
 Token ids live on the device before the first step; nothing else runs.
 """
@@ -20,7 +20,7 @@ from pathlib import Path
 
 import numpy as np
 
-ROOT = Path(__file__).resolve().parents[1]
+ROOT = Path(__file__).resolve().parent
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 

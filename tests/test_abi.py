@@ -9,6 +9,7 @@
 - the ctypes mirror in cngpt_b200/abi.py matches the C layout.
 """
 import ctypes as C
+import os
 import re
 import subprocess
 import tempfile
@@ -20,7 +21,8 @@ from cngpt_b200 import abi
 
 ROOT = Path(__file__).resolve().parents[1]
 INC = ROOT / "include"
-REF_SRC = Path("/root/reference/src")
+# the reference tree: $CNGPT_REFERENCE, else `reference` beside this repository
+REF_SRC = Path(os.environ.get("CNGPT_REFERENCE") or ROOT.parent / "reference") / "src"
 
 
 def declared_functions(path: Path) -> set[str]:
@@ -164,6 +166,22 @@ def test_load_checkpoint_rejects_missing_and_foreign_files():
         assert lib.cngpt_cuda_load_checkpoint(C.byref(m), str(foreign).encode()) == abi.ERR_ARG
         assert "not a cngpt model file" in lib.cngpt_cuda_last_message().decode()
     assert not m.param_buf  # nothing was allocated
+    lib.cngpt_cuda_clear_status()
+
+
+def test_load_checkpoint_rejects_truncated_file_before_device_work():
+    """A file whose header is valid but whose parameters stop short is read
+    whole on the host and rejected before the model is created."""
+    import struct
+    lib = abi.load()
+    m = abi.GPT()
+    with tempfile.TemporaryDirectory() as d:
+        short = Path(d) / "short.bin"
+        # magic, version, n_layer, n_head, n_embd, vocab, block (src/model.h:22-30)
+        short.write_bytes(struct.pack("<7i", 0x434E4750, 1, 1, 2, 8, 10, 4) + b"\x00" * 64)
+        assert lib.cngpt_cuda_load_checkpoint(C.byref(m), str(short).encode()) == abi.ERR_ARG
+        assert "truncated" in lib.cngpt_cuda_last_message().decode()
+    assert not m.param_buf
     lib.cngpt_cuda_clear_status()
 
 

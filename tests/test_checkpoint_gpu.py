@@ -83,3 +83,32 @@ def test_plain_model_file_loads_with_fresh_optimizer(lib, cuda):
         lib.cngpt_cuda_clear_status()
         wrong.free()
     a.free()
+
+
+def test_truncated_trailer_leaves_model_unchanged(lib, cuda):
+    """A checkpoint cut off inside the optimizer moments is rejected and the
+    model keeps its parameters, moments and step count."""
+    a = CudaModel(lib, *CFG, 5)
+    ids = oracle.lcg_tokens(2 * B * T + 1, CFG[3], seed=3)
+    steps(lib, a.m, ids, 2)
+    b = CudaModel(lib, *CFG, 9)
+    steps(lib, b.m, ids, 1)
+    p0 = b.params()
+    m0 = np.empty(b.n, np.float32)
+    abi.check(lib, lib.cngpt_cuda_copy(m0.ctypes.data, C.cast(b.m.m_buf, C.c_void_p), m0.nbytes), "m")
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "ckpt.bin")
+        abi.check(lib, lib.cngpt_cuda_save_checkpoint(C.byref(a.m), path.encode()), "save")
+        full = open(path, "rb").read()
+        with open(path, "wb") as f:
+            f.write(full[:len(full) - 4 * (a.n // 2)])  # stop inside the second moments
+        assert lib.cngpt_cuda_load_checkpoint(C.byref(b.m), path.encode()) == abi.ERR_ARG
+        assert b"truncated" in lib.cngpt_cuda_last_message()
+        lib.cngpt_cuda_clear_status()
+    assert b.m.step == 1
+    assert np.array_equal(b.params(), p0)
+    m1 = np.empty(b.n, np.float32)
+    abi.check(lib, lib.cngpt_cuda_copy(m1.ctypes.data, C.cast(b.m.m_buf, C.c_void_p), m1.nbytes), "m")
+    assert np.array_equal(m1, m0)
+    a.free()
+    b.free()
