@@ -120,7 +120,6 @@ EXT_SIGNATURES = {
     "cngpt_cuda_set_managed": (I, [I]),
     "cngpt_cuda_launch_count": (C.c_ulonglong, []),
     "cngpt_cuda_set_wait_limit_ns": (I, [C.c_ulonglong]),
-    "cngpt_cuda_selftest_tp_reduce": (I, [VP, VP, I, I, I, VP]),
     "cngpt_cuda_gemm": (I, [VP, L, I, VP, L, I, I, I, I, I, F, VP, L, VP, VP, L, VP, L, VP, L]),
     "cngpt_cuda_attention_fwd": (I, [VP, VP, VP, I, I, I, I]),
     "cngpt_cuda_attention_bwd": (I, [VP, VP, VP, VP, VP, I, I, I, I]),
@@ -142,6 +141,12 @@ EXT_SIGNATURES = {
     "cngpt_cuda_tp_forward_last": (I, [C.POINTER(GPT), VP, I, I, VP]),
     "cngpt_cuda_tp_generate": (I, [C.POINTER(GPT), VP, I, I, I, VP]),
     "cngpt_cuda_tp_free": (I, [C.POINTER(GPT)]),
+    "cngpt_cuda_selftest_tp_reduce": (I, [VP, VP, I, I, I, VP]),
+    "cngpt_cuda_loader_create": (I, [C.POINTER(VP), VP, C.c_size_t, I, I]),
+    "cngpt_cuda_loader_next": (I, [VP, C.POINTER(VP), C.POINTER(VP)]),
+    "cngpt_cuda_loader_reset": (I, [VP]),
+    "cngpt_cuda_loader_num_batches": (C.c_size_t, [VP]),
+    "cngpt_cuda_loader_free": (None, [VP]),
 }
 
 

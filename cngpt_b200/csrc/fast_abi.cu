@@ -288,20 +288,15 @@ extern "C" const float *gpt_forward_fast(GPT *m, FastCtx *f, const int *tokens, 
     return f->logits;
 }
 
-extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B, int T, int n_new,
-                                   int *out_tokens) {
-    ModelCtx *c = model_ctx(m);
-    if (!c) return ERR_STATE;
-    if (B <= 0 || T <= 0 || n_new <= 0 || T + n_new - 1 > m->cfg.block_size) {
-        set_last_error(ERR_ARG, "generate: B=%d T=%d n_new=%d exceeds block_size %d", B, T, n_new,
-                       m->cfg.block_size);
-        return ERR_ARG;
-    }
-    cudaStream_t s = g_stream;
-    FastDev *d = fast_dev(f, true);
-    CG_TRY(fast_resize(f, d, m, B, T, c->managed));
+namespace cg {
+namespace {
+// Decode state of a FastCtx for B sequences, a prompt of T tokens and n_new
+// generated tokens: the KV cache (capacity T + n_new positions), the decode
+// counters, the per-step token log and the statistics / argmax scratch.
+int kv_prepare(const GPT *m, FastCtx *f, FastDev *d, int B, int T, int n_new, bool managed, cudaStream_t s) {
+    CG_TRY(fast_resize(f, d, m, B, T, managed));
     const int Tmax = T + n_new;
-    const size_t C = m->cfg.n_embd, L = m->cfg.n_layer, V = m->cfg.vocab_size;
+    const size_t C = m->cfg.n_embd, L = m->cfg.n_layer;
     if (!d->cap_stream) {
         CG_CUDA(cudaStreamCreateWithFlags(&d->cap_stream, cudaStreamNonBlocking));
         CG_CUDA(cudaEventCreateWithFlags(&d->ev_a, cudaEventDisableTiming));
@@ -339,6 +334,24 @@ extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B,
         CG_TRY(dev_alloc((void **)&d->gen, (size_t)B * n_new * 4, false));
         d->gen_cap = (size_t)B * n_new;
     }
+    return OK;
+}
+}  // namespace
+}  // namespace cg
+
+extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B, int T, int n_new,
+                                   int *out_tokens) {
+    ModelCtx *c = model_ctx(m);
+    if (!c) return ERR_STATE;
+    if (B <= 0 || T <= 0 || n_new <= 0 || T + n_new - 1 > m->cfg.block_size) {
+        set_last_error(ERR_ARG, "generate: B=%d T=%d n_new=%d exceeds block_size %d", B, T, n_new,
+                       m->cfg.block_size);
+        return ERR_ARG;
+    }
+    cudaStream_t s = g_stream;
+    FastDev *d = fast_dev(f, true);
+    CG_TRY(kv_prepare(m, f, d, B, T, n_new, c->managed, s));
+    const size_t V = m->cfg.vocab_size;
     const int *tok = nullptr;
     CG_TRY(stage_tokens(prompt, (size_t)B * T, &d->tok, &d->tok_cap, &tok, s));
     // counters {T-1, 0}: the prefill's greedy token is logged at step 0, then
@@ -414,14 +427,66 @@ int sample_top_k(const float *logits, int V, float temp, int top_k) {
 }
 }  // namespace
 
+// The reference recomputes the whole (cropped) prefix for every token
+// (src/model.c:991-1016). While the context still fits block_size, nothing
+// is cropped and every position keeps its embedding, so here the prompt is
+// prefilled once into the KV cache and each further step runs one row
+// through the cached decode step; only the sampling runs on the host, on the
+// step's final-position logits, with the same rand() stream. Once the
+// context would exceed block_size the reference crops it and every position
+// shifts: those steps recompute the cropped prefix as the reference does.
+namespace {
+// tokens out[p, p + n) for p = prompt_len; returns the number produced
+int sample_cached(GPT *m, FastCtx *f, int *out, int prompt_len, int n, float temp, int top_k) {
+    ModelCtx *c = model_ctx(m);
+    if (!c) return 0;
+    cudaStream_t s = g_stream;
+    FastDev *d = fast_dev(f, true);
+    const int V = m->cfg.vocab_size;
+    std::vector<float> lg((size_t)V);
+    const int *tok = nullptr;
+    if (kv_prepare(m, f, d, 1, prompt_len, n, c->managed, s) != OK ||
+        stage_tokens(out, (size_t)prompt_len, &d->tok, &d->tok_cap, &tok, s) != OK ||
+        fast_forward(m, f, d, tok, 1, prompt_len, true, s) != OK ||
+        cudaMemcpyAsync(lg.data(), f->logits, (size_t)V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return 0;
+    for (int i = 0; i < n; ++i) {
+        const int t = sample_top_k(lg.data(), V, temp, top_k);
+        out[prompt_len + i] = t;
+        if (i + 1 == n) return n;
+        // the sampled token enters at position prompt_len + i; the step's own
+        // greedy bookkeeping (token log, next id) is overwritten by the sample
+        const int ctr[2] = {prompt_len + i, i + 1};
+        if (cudaMemcpyAsync(d->ctr, ctr, sizeof(ctr), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(d->next, &out[prompt_len + i], sizeof(int), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            decode_step(m, f, d, 1, s) != OK ||
+            cudaMemcpyAsync(lg.data(), f->logits, (size_t)V * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess || check_device_error() != OK)
+            return i + 1;
+    }
+    return n;
+}
+}  // namespace
+
 extern "C" void gpt_sample(GPT *m, const int *prompt_tokens, int prompt_len, int *out_tokens,
                            int max_new_tokens, float temp, int top_k) {
     const int block = m->cfg.block_size, V = m->cfg.vocab_size;
     memcpy(out_tokens, prompt_tokens, (size_t)prompt_len * sizeof(int));
     FastCtx f;
     fast_init(&f);
+    int i = 0;
+    if (prompt_len > 0 && prompt_len <= block && max_new_tokens > 0) {
+        const int n = std::min(max_new_tokens, block - prompt_len + 1);
+        i = sample_cached(m, &f, out_tokens, prompt_len, n, temp, top_k);
+        if (i < n) {
+            fprintf(stderr, "gpt_sample: cached decode failed: %s\n", last_message());
+            fast_free(&f);
+            return;
+        }
+    }
     std::vector<float> lg((size_t)V);
-    for (int i = 0; i < max_new_tokens; i++) {
+    for (; i < max_new_tokens; i++) {
         const int total = prompt_len + i;
         const int start = total > block ? total - block : 0;
         const float *d = gpt_forward_fast(m, &f, out_tokens + start, 1, total - start);

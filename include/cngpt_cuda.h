@@ -114,6 +114,25 @@ int cngpt_cuda_train_step(GPT *m, const int *tokens, const int *targets, int B, 
                           float grad_clip, float *loss_out);
 int cngpt_cuda_last_loss(GPT *m, float *loss_out);
 
+/* ---- training batches, uploaded one step ahead -----------------------------
+ * The reference's DataLoader (src/dataloader.c:62-82) fills host int arrays
+ * inputs[b*T+t] = data[pos + b*T + t], targets[b*T+t] = data[pos + b*T + t + 1]
+ * from an mmap'd uint16 token file, then advances pos by B*T and rewinds to 0
+ * when pos + B*T + 1 would pass the end. The loader produces the same batch
+ * sequence in device memory: each call returns the device inputs / targets of
+ * the current batch (the library stream waits for their upload) and starts
+ * uploading the next batch through a pinned buffer on a copy stream, so the
+ * upload overlaps the step that consumes the current one. The returned
+ * pointers stay valid until the call after next. `data` (host, e.g. the
+ * DataLoader's mmap) must outlive the loader. */
+typedef struct cngpt_cuda_loader cngpt_cuda_loader;
+int    cngpt_cuda_loader_create(cngpt_cuda_loader **out, const unsigned short *data, size_t n_tokens,
+                                int B, int T);
+int    cngpt_cuda_loader_next(cngpt_cuda_loader *dl, const int **inputs, const int **targets);
+int    cngpt_cuda_loader_reset(cngpt_cuda_loader *dl);                     /* dataloader_reset */
+size_t cngpt_cuda_loader_num_batches(const cngpt_cuda_loader *dl);        /* dataloader_num_batches */
+void   cngpt_cuda_loader_free(cngpt_cuda_loader *dl);
+
 /* parameter / gradient / optimizer state transfer (n_params floats) */
 int cngpt_cuda_params_to_host(GPT *m, float *dst);
 int cngpt_cuda_params_from_host(GPT *m, const float *src);

@@ -146,3 +146,44 @@ def adamw(c: OrcConfig, params, grads, m, v, step, lr, b1, b2, eps, wd, clip):
     lib.orc_adamw(ptr(params), ptr(grads), ptr(m), ptr(v), ptr(decay), params.size, C.byref(st),
                   lr, b1, b2, eps, wd, clip)
     return st.value
+
+
+# ---------------------------------------------------------------- data loader
+class DataLoader(C.Structure):
+    """src/dataloader.h:20-36, field for field"""
+    _fields_ = [("batch_size", I), ("seq_len", I), ("filename", C.c_char_p), ("fd", I),
+                ("data", C.POINTER(C.c_uint16)), ("n_tokens", C.c_size_t), ("pos", C.c_size_t),
+                ("inputs", C.POINTER(I)), ("targets", C.POINTER(I))]
+
+
+def reference_batches(path: str, B: int, T: int, n: int) -> list[tuple[np.ndarray, np.ndarray]]:
+    """n batches from the reference's own DataLoader (src/dataloader.c:19-82)
+    over a uint16 token file: (inputs, targets), each int32[B*T]."""
+    lib = reference()
+    lib.dataloader_init.restype = I
+    lib.dataloader_init.argtypes = [C.POINTER(DataLoader), C.c_char_p, I, I]
+    lib.dataloader_next_batch.argtypes = [C.POINTER(DataLoader)]
+    lib.dataloader_free.argtypes = [C.POINTER(DataLoader)]
+    dl = DataLoader()
+    assert lib.dataloader_init(C.byref(dl), path.encode(), B, T) == 0
+    out = []
+    for _ in range(n):
+        lib.dataloader_next_batch(C.byref(dl))
+        out.append((np.ctypeslib.as_array(dl.inputs, shape=(B * T,)).copy(),
+                    np.ctypeslib.as_array(dl.targets, shape=(B * T,)).copy()))
+    lib.dataloader_free(C.byref(dl))
+    return out
+
+
+def restated_batches(data: np.ndarray, B: int, T: int, n: int) -> list[tuple[np.ndarray, np.ndarray]]:
+    """The same batch sequence restated (src/dataloader.c:62-82): element
+    (b, t) of a batch at position pos is data[(pos + b*T + t) % N], its target
+    the next token; pos advances by B*T and rewinds when pos + B*T + 1 > N."""
+    N, BT, pos, out = data.size, B * T, 0, []
+    for _ in range(n):
+        idx = (pos + np.arange(BT)) % N
+        out.append((data[idx].astype(np.int32), data[(idx + 1) % N].astype(np.int32)))
+        pos += BT
+        if pos + BT + 1 > N:
+            pos = 0
+    return out

@@ -17,13 +17,14 @@ def _np(ptr, n, dtype=np.float32):
 
 
 class _Base:
-    def __init__(self, lib, L, H, Cemb, V, block, seed, dropout=0.0):
+    def __init__(self, lib, L, H, Cemb, V, block, seed, dropout=0.0, init=True):
         self.lib = lib
         self.cfg = abi.GPTConfig(L, H, Cemb, V, block, dropout)
         self.m = abi.GPT()
         assert lib.gpt_init(C.byref(self.m), self.cfg) == 0
-        oracle.libc_rand_stream(seed)
-        lib.gpt_init_weights(C.byref(self.m))
+        if init:  # otherwise the caller sets the parameters
+            oracle.libc_rand_stream(seed)
+            lib.gpt_init_weights(C.byref(self.m))
         self.n = self.m.n_params
 
     def forward(self, tok, tgt, B, T):

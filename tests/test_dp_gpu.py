@@ -22,30 +22,34 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_dp2_matches_single_gpu_average(lib, cuda):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_dp_matches_single_gpu_average(lib, cuda, world):
+    """world ranks, one per GPU (skipped with fewer GPUs)"""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from tests.dp_worker import B, CFG, T
     with tempfile.TemporaryDirectory() as d:
         env = dict(os.environ, NCCL_NVLS_ENABLE="0")
         cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-               "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533",
+               f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29520 + world}",
                str(ROOT / "tests" / "dp_worker.py"), d]
         r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=400)
         assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
-        r0, r1 = np.load(os.path.join(d, "rank0.npz")), np.load(os.path.join(d, "rank1.npz"))
-    assert np.array_equal(r0["params"], r1["params"]), "ranks diverged after AdamW"
-    assert np.array_equal(r0["grads"], r1["grads"])
+        res = [np.load(os.path.join(d, f"rank{k}.npz")) for k in range(world)]
+    for rk in range(1, world):
+        assert np.array_equal(res[0]["params"], res[rk]["params"]), f"rank {rk} diverged after AdamW"
+        assert np.array_equal(res[0]["grads"], res[rk]["grads"])
     m = CudaModel(lib, *CFG, 7)
-    ids = oracle.lcg_tokens(2 * B * T + 1, CFG[3], seed=31)
+    ids = oracle.lcg_tokens(world * B * T + 1, CFG[3], seed=31)
     n = B * T
     acc = np.zeros(m.n, np.float64)
-    for rank in range(2):
+    for rank in range(world):
         m.zero_grad()
         m.forward(ids[rank * n:(rank + 1) * n].copy(), ids[rank * n + 1:(rank + 1) * n + 1].copy(), B, T)
         m.backward(ids[rank * n:(rank + 1) * n].copy(), ids[rank * n + 1:(rank + 1) * n + 1].copy(), B, T)
         acc += m.grads()
-    avg = (acc / 2).astype(np.float32)
-    e = nwerr(r0["grads"], avg)
-    print(f"\ndp2 averaged gradient vs single-GPU mean: normwise {e:.2e}")
+    avg = (acc / world).astype(np.float32)
+    e = nwerr(res[0]["grads"], avg)
+    print(f"\ndp{world} averaged gradient vs single-GPU mean: normwise {e:.2e}")
     assert e < 1e-6
     m.free()

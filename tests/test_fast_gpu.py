@@ -134,3 +134,28 @@ def test_sample_matches_reference_stream(lib, cuda):
         assert np.array_equal(out_r, out_d), (temp, k, out_r, out_d)
     ref.free()
     dev.free()
+
+
+@pytest.mark.parametrize("temp,k", [(1.0, 0), (0.8, 10), (1.0, 1)])
+def test_sample_kv_cache_matches_reference_stream(lib, cuda, temp, k):
+    """gpt_sample on a head-size-64 model: 80 new tokens, all within
+    block_size, so every step after the prompt runs through the KV cache;
+    same rand() stream, same tokens as the reference's full-prefix loop."""
+    ref, dev, c = pair(lib, "hs64")
+    prompt = oracle.lcg_tokens(20, c["V"], seed=4)
+    n = 80
+    out_r = np.zeros(20 + n, np.int32)
+    out_d = np.zeros(20 + n, np.int32)
+    oracle.libc_rand_stream(11)
+    ref.lib.gpt_sample(C.byref(ref.m), prompt.ctypes.data, 20, out_r.ctypes.data, n, temp, k)
+    oracle.libc_rand_stream(11)
+    launches = lib.cngpt_cuda_launch_count()
+    lib.gpt_sample(C.byref(dev.m), prompt.ctypes.data, 20, out_d.ctypes.data, n, temp, k)
+    launches = lib.cngpt_cuda_launch_count() - launches
+    assert np.array_equal(out_r, out_d), (temp, k, np.nonzero(out_r != out_d))
+    # a full-prefix recompute launches at least 7 kernels per layer per token;
+    # the cached decode step launches 5 per layer plus 3 (embedding, LM head,
+    # token bookkeeping)
+    assert launches <= n * (5 * c["L"] + 3) + 100, launches
+    ref.free()
+    dev.free()

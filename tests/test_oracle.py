@@ -192,3 +192,19 @@ def test_restatement_full_grads_match_reference():
     assert abs(lo - lr_) < 1e-5
     assert nwerr(go, ref.grads()) < 1e-5
     ref.free()
+
+
+@pytest.mark.skipif(not oracle.reference_available(), reason="reference build absent")
+def test_reference_dataloader_matches_restatement(tmp_path):
+    """The reference's DataLoader (src/dataloader.c) and the restated batch
+    sequence agree over several rewinds, including a file of exactly B*T+1."""
+    rng = np.random.default_rng(3)
+    for B, T, N in [(3, 7, 3 * 7 * 4 + 5), (2, 5, 11), (1, 16, 100)]:
+        data = rng.integers(0, 65535, N, dtype=np.uint16)
+        path = tmp_path / f"tok_{N}.bin"
+        data.tofile(path)
+        n = 3 * (N // (B * T)) + 2
+        ref = oracle.reference_batches(str(path), B, T, n)
+        res = oracle.restated_batches(data, B, T, n)
+        for (ri, rt), (si, st) in zip(ref, res):
+            assert np.array_equal(ri, si) and np.array_equal(rt, st)

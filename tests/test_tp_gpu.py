@@ -7,9 +7,9 @@ Cases: 5 heads at n_embd 320 (uneven 3/2 head split, ragged vocabulary 1001),
 3 heads of size 32 (CUDA-core attention path), two layers of GPT-2 XL's
 shape (25 heads: 13/12 over two ranks), and a decode batch of 10 (above the
 8 rows the peer-memory exchange takes, so its partial sums go through
-ncclAllReduce). world = 1 runs on any GPU; world = 2 needs two GPUs and is
-skipped on a one-GPU box. At world = 2 the decode exchanges of batches up to
-8 run through the GEMV's peer-memory push and tp_reduce_kernel."""
+ncclAllReduce). world = 1 runs on any GPU; worlds 2, 4 and 8 need that many
+GPUs and are skipped on a smaller box. At world > 1 the decode exchanges of
+batches up to 8 run through the GEMV's peer-memory push and tp_reduce_kernel."""
 import ctypes as C
 import os
 import subprocess
@@ -91,18 +91,24 @@ def test_tp_requires_init(lib, cuda):
     m.free()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_reference(lib, cuda):
-    names = list(CASES)
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_multi_gpu_matches_reference(lib, cuda, world):
+    """world ranks, one per GPU (skipped with fewer GPUs); the cases whose
+    head count is at least world"""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    names = [n for n in CASES if CASES[n][0][1] >= world]
     with tempfile.TemporaryDirectory() as d:
         env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-        cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-               "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29534",
+        cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29530 + world}",
                str(ROOT / "tests" / "tp_worker.py"), d, *names]
-        r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=500)
+        r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=700)
         assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
-        res = [np.load(os.path.join(d, f"rank{k}.npz")) for k in range(2)]
+        res = [np.load(os.path.join(d, f"rank{k}.npz")) for k in range(world)]
     for name in names:
         for k in ("_logits", "_tokens"):
-            assert np.array_equal(res[0][name + k], res[1][name + k]), (name, k)
+            for rk in range(1, world):
+                assert np.array_equal(res[0][name + k], res[rk][name + k]), (name, k, rk)
         check_case(lib, name, res[0][name + "_logits"], res[0][name + "_tokens"])
+    print(f"\ntp world {world}: cases {names} match the reference and the one-GPU decode on every rank")
