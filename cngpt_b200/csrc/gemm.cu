@@ -112,6 +112,38 @@ __device__ __forceinline__ const float *epi_aux(const GemmEpi &e, long &ld) {
     }
 }
 
+// Cross-entropy statistics of one row's 32 columns [n0, n0 + 32) (thread =
+// row, v its raw products), folded into the running (max, sum exp(x - max))
+// of the row's current 64-column group.
+__device__ __forceinline__ void ce_fold(const float (&v)[32], int n0, int N, float alpha, float &m, float &s) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        if (n0 + j < N) mx = fmaxf(mx, v[j] * alpha);
+    if (mx == -INFINITY) return;
+    float add = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        if (n0 + j < N) add += expf(v[j] * alpha - mx);
+    if (mx > m) {
+        s = s * expf(m - mx) + add;
+        m = mx;
+    } else {
+        s += add * expf(mx - m);
+    }
+}
+
+// After chunk c (of 32 columns starting at n0) of a row: every second chunk
+// closes a 64-column group, whose (max, sum) is stored and reset.
+__device__ __forceinline__ void ce_flush(const GemmEpi &ep, int c, long m, int n0, int M, int N, float &cm,
+                                         float &cs) {
+    if (!(c & 1)) return;
+    const int g0 = n0 - 32;  // first column of the group
+    if (m < M && g0 < N) ep.ce_part[m * ep.ce_ld + g0 / 64] = make_float2(cm, cs);
+    cm = -INFINITY;
+    cs = 0.f;
+}
+
 // Epilogue of one 32x32 output block (thread = row on entry, `v` its 32
 // columns): transposed through the warp's padded shared tile `stile`; lane l
 // then handles row (4i + l/8) and columns 4(l%8)..+3 for i = 0..7 -
@@ -399,22 +431,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
             }
             if (!ok) break;
+            float cm = -INFINITY, cs = 0.f;
 #pragma unroll
             for (int c = 0; c < CH; ++c) {
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = sum[c * 32 + j];
-                store_block_(v, m0, tn * BN + (c0 + c) * 32);
+                const int n0 = tn * BN + (c0 + c) * 32;
+                if (ep.ce_part) ce_fold(v, n0, N, ep.alpha, cm, cs);
+                store_block_(v, m0, n0);
+                if (ep.ce_part) ce_flush(ep, c, m0 + lane, n0, M, N, cm, cs);
             }
         } else {
             if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) break;
             tc_fence_after();
+            float cm = -INFINITY, cs = 0.f;
 #pragma unroll 1
             for (int c = 0; c < CH; ++c) {
                 float v[32];
                 tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) +
                                        ((uint32_t)(q * 32) << 16), v);
-                store_block_(v, m0, tn * BN + (c0 + c) * 32);
+                const int n0 = tn * BN + (c0 + c) * 32;
+                if (ep.ce_part) ce_fold(v, n0, N, ep.alpha, cm, cs);
+                store_block_(v, m0, n0);
+                if (ep.ce_part) ce_flush(ep, c, m0 + lane, n0, M, N, cm, cs);
             }
             tc_fence_before();
             __syncwarp();
@@ -624,11 +664,15 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             const int c0 = half * CH;
             if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) break;
             tc_fence_after();
+            float cm = -INFINITY, cs = 0.f;
 #pragma unroll 1
             for (int c = 0; c < CH; ++c) {
                 float v[32];
                 tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) + ((uint32_t)(q * 32) << 16), v);
-                store_block(ep, stile, lane, v, m0, tn * BN + (c0 + c) * 32, M, N, aux, ldaux);
+                const int n0 = tn * BN + (c0 + c) * 32;
+                if (ep.ce_part) ce_fold(v, n0, N, ep.alpha, cm, cs);
+                store_block(ep, stile, lane, v, m0, n0, M, N, aux, ldaux);
+                if (ep.ce_part) ce_flush(ep, c, m0 + lane, n0, M, N, cm, cs);
             }
             tc_fence_before();
             __syncwarp();
@@ -1143,6 +1187,32 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ ws, int S, long s
     }
 }
 
+// Cross-entropy statistics of stored rows, for the paths whose epilogue does
+// not form them (split-K, CUDA-core, GEMV): one block per row, warp w takes
+// the 64-column groups w, w + 8, ... (two columns per lane), same layout as
+// the fused epilogue's.
+__global__ void __launch_bounds__(256)
+ce_stats_kernel(const float *__restrict__ D, long ldd, int N, float2 *__restrict__ part, int ce_ld) {
+    const long m = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *row = D + m * ldd;
+    for (int g = warp; g * 64 < N; g += 8) {
+        const int n0 = g * 64 + lane, n1 = n0 + 32;
+        const float a = n0 < N ? row[n0] : -INFINITY, b = n1 < N ? row[n1] : -INFINITY;
+        float mx = warp_max(fmaxf(a, b));
+        float sm = (n0 < N ? expf(a - mx) : 0.f) + (n1 < N ? expf(b - mx) : 0.f);
+        sm = warp_sum(sm);
+        if (lane == 0) part[m * ce_ld + g] = make_float2(mx, sm);
+    }
+}
+
+int ce_stats_pass(const GemmEpi &e, int M, int N, cudaStream_t s) {
+    ce_stats_kernel<<<M, 256, 0, s>>>(e.D, e.ldd, N, e.ce_part, e.ce_ld);
+    ++g_launch_count;
+    CG_CUDA(cudaGetLastError());
+    return OK;
+}
+
 // Modelled time of a GEMM run as `units` persistent work units on `workers`
 // (SMs, or CTA pairs): the slower of the tensor rate and the L2-to-SM operand
 // stream (bytes per FLOP of the CTA tile: (rows + loaded B rows) x 128 B per
@@ -1237,7 +1307,7 @@ int launch_tc(const float *A, long lda, const float *B, long ldb, int M, int N, 
     splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(ws, ks, stride, M, N, epi);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
-    return OK;
+    return epi.ce_part ? ce_stats_pass(epi, M, N, s) : OK;
 }
 
 bool pair_gemm_enabled() {
@@ -1315,7 +1385,7 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     splitk_reduce_kernel<<<rgrid, 256, 0, s>>>(ws, ks, stride, M, N, epi);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
-    return OK;
+    return epi.ce_part ? ce_stats_pass(epi, M, N, s) : OK;
 }
 
 // Tile width for the pair kernel: the modelled-faster of 256 and 128 (each
@@ -1373,6 +1443,10 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
         return ERR_ARG;
     }
     if (M == 0 || N == 0) return OK;
+    if (epi.ce_part && (epi.mode != EPI_STORE || !epi.D || epi.bias || epi.ce_ld != (N + 63) / 64)) {
+        set_last_error(ERR_ARG, "gemm: cross-entropy statistics need STORE without bias and ce_ld = ceil(N/64)");
+        return ERR_ARG;
+    }
     GemmEpi e2 = epi;
     {
         auto al = [](const void *p) { return ((uintptr_t)p % 16) == 0; };
@@ -1382,6 +1456,12 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
     }
     const int prec = precision();
     e2.fast_act = prec == PREC_TF32;
+    if (epi.ce_part && (M <= 8 || prec == PREC_FP32)) {  // paths without the fused statistics
+        GemmEpi e3 = epi;
+        e3.ce_part = nullptr;
+        CG_TRY(gemm(A, lda, a_mn, B, ldb, b_mn, M, N, K, e3, s));
+        return ce_stats_pass(epi, M, N, s);
+    }
     if (gemv_ok(A, lda, a_mn, B, ldb, b_mn, M, N, K, epi) &&
         ((long)N * K >= (1L << 16) || epi.kc || epi.ln_stats_out || epi.push_bufs || epi.argmax_key))
         return dispatch_gemv<false>(A, lda, B, ldb, M, N, K, epi, nullptr, nullptr, nullptr, s);
@@ -1437,7 +1517,7 @@ int gemm(const float *A, long lda, bool a_mn, const float *B, long ldb, bool b_m
     gemm_simt_kernel<<<grid, 256, 0, s>>>(A, lda, a_mn, B, ldb, b_mn, M, N, K, epi);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
-    return OK;
+    return epi.ce_part ? ce_stats_pass(epi, M, N, s) : OK;
 }
 
 int make_tensor_map(CUtensorMap_st *out, const float *p, long inner, long outer, long ld, int box0, int box1,

@@ -117,6 +117,13 @@ struct GemmEpi {
     // order-preserving 64-bit key (keys start at zero); greedy_finalize()
     // turns the keys into tokens and clears them
     unsigned long long *argmax_key = nullptr;
+    // fused cross-entropy statistics (STORE mode without bias, D = logits
+    // rows): for every row m and every 64-column group p of the output, the
+    // pair (max, sum of exp(x - max)) over the group's columns goes to
+    // ce_part[m * ce_ld + p], ce_ld = ceil(N / 64); cross_entropy_fused()
+    // merges them into the row's log-sum-exp
+    float2 *ce_part = nullptr;
+    int ce_ld = 0;
 };
 
 constexpr int TP_MAX_WORLD = 8;

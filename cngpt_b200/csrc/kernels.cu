@@ -261,6 +261,55 @@ ce_fwd_kernel(const float *__restrict__ logits, long ldl, const int *__restrict_
     if (threadIdx.x == 0 && rowterm) rowterm[r] = tgt >= 0 ? (lg[tgt] - m) - logf(sum) : 0.f;
 }
 
+// Fused cross-entropy, second half (the LM-head GEMM's epilogue formed the
+// per-64-column (max, sum exp) pairs of every logits row): one block per row
+// merges the row's pairs in a fixed order into (max, sum), keeps the row's
+// NLL term (l[tgt] - max) - log(sum) (src/ops.c:551-570), then overwrites the
+// logits row in place with dlogits = scale * (softmax - onehot)
+// (src/ops.c:576-590 into the zeroed buffer of src/model.c:644), pad columns
+// [V, ldd) zeroed. Rows are 16-byte aligned (ldd % 4 == 0).
+__global__ void __launch_bounds__(512)
+ce_fused_rows_kernel(float *__restrict__ rows_io, long ldd, const float2 *__restrict__ part, int ce_ld,
+                     const int *__restrict__ targets, float scale, float *__restrict__ rowterm, int V) {
+    constexpr int NT = 512;
+    __shared__ float shm[16], shs[16];
+    const long r = blockIdx.x;
+    float m = -INFINITY, sum = 0.f;
+    for (int g = threadIdx.x; g < ce_ld; g += NT) {
+        const float2 p = part[r * ce_ld + g];
+        ms_merge(m, sum, p.x, p.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, sum, o);
+        ms_merge(m, sum, m2, s2);
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) { shm[wid] = m; shs[wid] = sum; }
+    __syncthreads();
+    m = shm[0];
+    sum = shs[0];
+    for (int k = 1; k < NT / 32; ++k) ms_merge(m, sum, shm[k], shs[k]);
+    float *row = rows_io + r * ldd;
+    const int tgt = targets[r];
+    if (threadIdx.x == 0) rowterm[r] = (row[tgt] - m) - logf(sum);
+    __syncthreads();  // the target's logit is read before the row is overwritten
+    const float inv = 1.0f / sum;
+    float4 *row4 = (float4 *)row;
+    const int n4 = (int)(ldd >> 2);
+    for (int i = threadIdx.x; i < n4; i += NT) {
+        const float4 x = __ldcs(row4 + i);
+        const float xv[4] = {x.x, x.y, x.z, x.w};
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int v = 4 * i + j;
+            o[j] = v < V ? scale * (expf(xv[j] - m) * inv - (v == tgt ? 1.0f : 0.0f)) : 0.0f;
+        }
+        __stcs(row4 + i, make_float4(o[0], o[1], o[2], o[3]));
+    }
+}
+
 // loss = -(sum of the row terms) / rows: 1024 threads each sum a fixed
 // strided subset, then a fixed-shape tree (deterministic; the reference sums
 // in row order in one float, src/ops.c:503,548,573).
@@ -705,6 +754,18 @@ int cross_entropy_rows(const float *logits, long ldl, const int *targets, float 
     if (rows <= 0) return OK;
     ce_fwd_kernel<<<rows, 512, 0, s>>>(logits, ldl, targets, probs, ldp, dlogits, ldd, scale,
                                        rowterm, V);
+    LAUNCH_CHECK();
+    return OK;
+}
+
+int cross_entropy_fused(float *rows_io, long ldd, const float2 *part, int ce_ld, const int *targets, float scale,
+                        float *rowterm, int rows, int V, cudaStream_t s) {
+    if (rows <= 0) return OK;
+    if (ldd % 4 != 0 || ((uintptr_t)rows_io % 16) != 0 || ldd < V) {
+        set_last_error(ERR_ARG, "cross_entropy_fused: rows need a 16-byte aligned pitch >= V");
+        return ERR_ARG;
+    }
+    ce_fused_rows_kernel<<<rows, 512, 0, s>>>(rows_io, ldd, part, ce_ld, targets, scale, rowterm, V);
     LAUNCH_CHECK();
     return OK;
 }

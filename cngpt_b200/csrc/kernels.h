@@ -27,6 +27,12 @@ int cross_entropy_rows(const float *logits, long ldl, const int *targets, float 
                        float *dlogits, long ldd, float scale, float *rowterm, int rows, int V,
                        cudaStream_t s);
 int cross_entropy_loss(const float *rowterm, int rows, float *loss, cudaStream_t s);
+// second half of the fused LM-head + cross-entropy: merges the GEMM
+// epilogue's per-64-column (max, sum exp) pairs part[rows][ce_ld] into each
+// row's log-sum-exp, writes the NLL terms to rowterm and overwrites the
+// logits rows (pitch ldd, ldd % 4 == 0) with scale * (softmax - onehot)
+int cross_entropy_fused(float *rows_io, long ldd, const float2 *part, int ce_ld, const int *targets, float scale,
+                        float *rowterm, int rows, int V, cudaStream_t s);
 int cross_entropy_bwd(float *dlogits, const float *probs, const int *targets, float scale, int rows,
                       int V, cudaStream_t s);
 int axpy1(float *dst, const float *src, long n, cudaStream_t s);

@@ -180,6 +180,10 @@ void sync_if_managed(ModelCtx *c) {
     if (c->managed) cudaStreamSynchronize(g_stream);
 }
 
+// byte offset of the fused cross-entropy partials in the model's scratch,
+// after the BT row terms
+size_t ce_part_offset(size_t BT) { return (BT * sizeof(float) + 255) & ~(size_t)255; }
+
 // extras sized for B*T rows
 int ensure_extras(GPT *m, ModelCtx *c, int B, int T) {
     const size_t BT = (size_t)B * T;
@@ -206,6 +210,9 @@ int ensure_extras(GPT *m, ModelCtx *c, int B, int T) {
     sb = std::max(sb, colsum_scratch_bytes((int)BT, (int)(4 * C)));
     sb = std::max(sb, attention_bwd_scratch_bytes(B, T, (int)H));
     sb = std::max(sb, BT * sizeof(float));  // CE row terms
+    // fused LM-head + cross-entropy: row terms, then the per-64-column
+    // (max, sum exp) pairs of every row
+    sb = std::max(sb, ce_part_offset(BT) + BT * (size_t)((V + 63) / 64) * sizeof(float2));
     sb = std::max(sb, norm_scratch_bytes());
     c->scratch_bytes = sb;
     CG_TRY(dev_alloc((void **)&c->scratch, sb, false));
@@ -287,8 +294,13 @@ int resize_acts(GPT *m, ModelCtx *c, int B, int T) {
 }
 
 // ------------------------------------------------------------ forward
+// fused_ce (training step): the LM-head GEMM writes the logits straight into
+// the dlogits buffer and forms each row's softmax statistics in its epilogue;
+// one pass then turns the rows into dlogits in place. The arena's logits and
+// probs slots are not written. Otherwise logits and probs land in the arena
+// as in the reference.
 int forward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, int T, bool want_grad,
-            cudaStream_t s) {
+            cudaStream_t s, bool fused_ce = false) {
     const int C = m->cfg.n_embd, V = m->cfg.vocab_size, L = m->cfg.n_layer, H = m->cfg.n_head;
     const int BT = B * T;
     if (B <= 0 || T <= 0 || T > m->cfg.block_size || H <= 0 || C % H != 0) {
@@ -353,15 +365,31 @@ int forward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, i
     }
     CG_TRY(layernorm_fwd(x, C, w->ln_f_w, w->ln_f_b, a->ln_f_out, C, a->ln_f_mean, a->ln_f_rstd, BT,
                          C, s));
+    c->dlogits_valid = false;
+    c->fwd_targets = targets;
+    float *rowterm = c->scratch;
+    if (fused_ce && targets && want_grad) {
+        // src/model.c:612-623 and 644-665 in two kernels: logits with row
+        // statistics, then loss terms and dlogits
+        float2 *part = (float2 *)((char *)c->scratch + ce_part_offset(BT));
+        GemmEpi e;
+        e.mode = EPI_STORE;
+        e.D = c->dlogits;
+        e.ldd = c->ldlog;
+        e.ce_part = part;
+        e.ce_ld = (V + 63) / 64;
+        CG_TRY(gemm(a->ln_f_out, C, false, w->wte, C, false, BT, V, C, e, s));
+        CG_TRY(cross_entropy_fused(c->dlogits, c->ldlog, part, e.ce_ld, tgt, 1.0f / (float)BT, rowterm, BT, V, s));
+        CG_TRY(cross_entropy_loss(rowterm, BT, &c->dev_scalars[0], s));
+        c->dlogits_valid = true;
+        return OK;
+    }
     GemmEpi e;
     e.mode = EPI_STORE;
     e.D = a->logits;
     e.ldd = V;
     CG_TRY(gemm(a->ln_f_out, C, false, w->wte, C, false, BT, V, C, e, s));
-    c->dlogits_valid = false;
-    c->fwd_targets = targets;
     if (!targets) return OK;
-    float *rowterm = c->scratch;
     CG_TRY(cross_entropy_rows(a->logits, V, tgt, a->probs, V, want_grad ? c->dlogits : nullptr,
                               c->ldlog, 1.0f / (float)BT, rowterm, BT, V, s));
     CG_TRY(cross_entropy_loss(rowterm, BT, &c->dev_scalars[0], s));
@@ -859,7 +887,7 @@ extern "C" int cngpt_cuda_train_step(GPT *m, const int *tokens, const int *targe
     }
     cudaStream_t s = g_stream;
     CG_CUDA(cudaMemsetAsync(m->grad_buf, 0, (size_t)m->n_params * sizeof(float), s));
-    CG_TRY(forward(m, c, tokens, targets, B, T, true, s));
+    CG_TRY(forward(m, c, tokens, targets, B, T, true, s, true));
     CG_TRY(backward(m, c, tokens, targets, B, T, s));
     if (c->world > 1) CG_TRY(dp_allreduce(c, m->grad_buf, (size_t)m->n_params, s));
     CG_TRY(adamw_step(m, c, lr, beta1, beta2, eps, wd, grad_clip, s));
