@@ -18,6 +18,8 @@ extern "C" {
 #include "cngpt_cuda.h"
 }
 
+extern "C" int cngpt_cuda_dp_free(GPT *m);
+
 namespace cg {
 
 // NCCL is opened on first use rather than linked: a process that loads this
@@ -120,14 +122,20 @@ extern "C" int cngpt_cuda_dp_init(GPT *m, const unsigned char id[128], int world
         return ERR_ARG;
     }
     // a second dp_init replaces the communicator of the first
-    if (c->nccl_comm) {
-        cudaStreamSynchronize(g_stream);
-        nccl_comm_destroy(c->nccl_comm);
-        c->nccl_comm = nullptr;
-    }
+    if (c->nccl_comm) cngpt_cuda_dp_free(m);
     c->world = 1;
     c->rank = 0;
     if (world == 1) return OK;
+    // the gradient buckets' stream: non-blocking (no implicit order with the
+    // legacy default stream) and at the highest priority, so the collectives
+    // start as soon as their bucket is final
+    if (!c->comm_stream) {
+        int lo = 0, hi = 0;
+        CG_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+        CG_CUDA(cudaStreamCreateWithPriority(&c->comm_stream, cudaStreamNonBlocking, hi));
+        CG_CUDA(cudaEventCreateWithFlags(&c->ev_ready, cudaEventDisableTiming));
+        CG_CUDA(cudaEventCreateWithFlags(&c->ev_done, cudaEventDisableTiming));
+    }
     void *comm = nullptr;
     CG_TRY(nccl_comm_init(&comm, id, world, rank));
     c->nccl_comm = comm;
@@ -145,10 +153,18 @@ extern "C" int cngpt_cuda_dp_allreduce_grads(GPT *m) {
 extern "C" int cngpt_cuda_dp_free(GPT *m) {
     ModelCtx *c = model_ctx(m);
     if (!c) return ERR_STATE;
+    cudaStreamSynchronize(g_stream);
+    if (c->comm_stream) cudaStreamSynchronize(c->comm_stream);
     if (c->nccl_comm) {
-        cudaStreamSynchronize(g_stream);
         nccl_comm_destroy(c->nccl_comm);
         c->nccl_comm = nullptr;
+    }
+    if (c->comm_stream) {
+        cudaStreamDestroy(c->comm_stream);
+        cudaEventDestroy(c->ev_ready);
+        cudaEventDestroy(c->ev_done);
+        c->comm_stream = nullptr;
+        c->ev_ready = c->ev_done = nullptr;
     }
     c->world = 1;
     c->rank = 0;

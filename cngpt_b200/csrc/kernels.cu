@@ -127,6 +127,102 @@ layernorm_bwd_reduce(const float *__restrict__ part, int nblocks, int C, float *
     }
 }
 
+// Fused LayerNorm backward of the training step, one pass over the rows:
+//   dx[t, c] += rstd (dn - mean(dn) - xhat mean(dn xhat)), dn = dout w
+//   (src/ops.c:305-329), with the column sums that follow it folded in:
+//   dw += sum_t dout xhat, db += sum_t dout (src/ops.c:322-327) and, when cs
+//   is given, cs += sum_t dx_new - the bias gradient of the linear layer
+//   whose output gradient the updated dx is (src/ops.c:145-148).
+// C = 128 NJ: lane l of a warp owns the float4 columns 4 (l + 32 j). Warp w of
+// a block takes rows r0 + w, r0 + w + 8, ... of the block's row range and adds
+// its column terms into its own shared-memory partials (no two lanes share a
+// column); the block's 8 partials are then summed in warp order into
+// part[block][3][C], and ln_bwd_part_reduce adds the blocks in block order -
+// a fixed order, so the result is deterministic.
+template <int NJ>
+__global__ void __launch_bounds__(256)
+ln_bwd_fused_kernel(const float *__restrict__ dout, const float *__restrict__ x, const float *__restrict__ w,
+                    const float *__restrict__ mean, const float *__restrict__ rstd, float *__restrict__ dx, int T,
+                    int rows_per_block, float *__restrict__ part, int want_cs) {
+    constexpr int C = 128 * NJ;
+    extern __shared__ float4 ln_sp[];  // [8 warps][3][C / 4]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float4 *my = ln_sp + warp * 3 * (C / 4);
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        my[lane + 32 * j] = z;
+        my[C / 4 + lane + 32 * j] = z;
+        my[2 * (C / 4) + lane + 32 * j] = z;
+    }
+    float4 wv[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) wv[j] = __ldg((const float4 *)w + lane + 32 * j);
+    const long r0 = (long)blockIdx.x * rows_per_block;
+    const long r1 = std::min<long>(T, r0 + rows_per_block);
+    const float invC = 1.0f / (float)C;
+    for (long t = r0 + warp; t < r1; t += 8) {
+        const float4 *d4 = (const float4 *)(dout + t * C), *x4 = (const float4 *)(x + t * C);
+        float4 *o4 = (float4 *)(dx + t * C);
+        float4 d[NJ], xh[NJ], o[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            d[j] = __ldcs(d4 + lane + 32 * j);
+            xh[j] = __ldcs(x4 + lane + 32 * j);
+            o[j] = __ldcs(o4 + lane + 32 * j);
+        }
+        const float m = mean[t], rs = rstd[t];
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            xh[j] = make_float4((xh[j].x - m) * rs, (xh[j].y - m) * rs, (xh[j].z - m) * rs, (xh[j].w - m) * rs);
+            const float4 dn = make_float4(d[j].x * wv[j].x, d[j].y * wv[j].y, d[j].z * wv[j].z, d[j].w * wv[j].w);
+            s1 += (dn.x + dn.y) + (dn.z + dn.w);
+            s2 += (dn.x * xh[j].x + dn.y * xh[j].y) + (dn.z * xh[j].z + dn.w * xh[j].w);
+        }
+        s1 = warp_sum(s1) * invC;
+        s2 = warp_sum(s2) * invC;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const float4 dv = d[j], xv = xh[j], wj = wv[j];
+            float4 n = o[j];
+            n.x += rs * (dv.x * wj.x - s1 - xv.x * s2);
+            n.y += rs * (dv.y * wj.y - s1 - xv.y * s2);
+            n.z += rs * (dv.z * wj.z - s1 - xv.z * s2);
+            n.w += rs * (dv.w * wj.w - s1 - xv.w * s2);
+            __stcs(o4 + lane + 32 * j, n);
+            float4 &pw = my[lane + 32 * j], &pb = my[C / 4 + lane + 32 * j];
+            pw.x += dv.x * xv.x; pw.y += dv.y * xv.y; pw.z += dv.z * xv.z; pw.w += dv.w * xv.w;
+            pb.x += dv.x; pb.y += dv.y; pb.z += dv.z; pb.w += dv.w;
+            if (want_cs) {
+                float4 &pc = my[2 * (C / 4) + lane + 32 * j];
+                pc.x += n.x; pc.y += n.y; pc.z += n.z; pc.w += n.w;
+            }
+        }
+    }
+    __syncthreads();
+    const float *spf = (const float *)ln_sp;
+    for (int c = threadIdx.x; c < 3 * C; c += blockDim.x) {
+        float v = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v += spf[k * 3 * C + c];
+        part[(long)blockIdx.x * 3 * C + c] = v;
+    }
+}
+
+// dw, db (and cs) += the blocks' partials part[nb][3][C], summed in block order
+__global__ void __launch_bounds__(256)
+ln_bwd_part_reduce(const float *__restrict__ part, int nb, int C, float *__restrict__ dw, float *__restrict__ db,
+                   float *__restrict__ cs) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int k = blockIdx.y;  // 0: dw, 1: db, 2: cs
+    float *dst = k == 0 ? dw : (k == 1 ? db : cs);
+    if (c >= C || !dst) return;
+    float v = 0.f;
+    for (int b = 0; b < nb; ++b) v += part[((long)b * 3 + k) * C + c];
+    dst[c] += v;
+}
+
 // ---------------------------------------------------------------- GELU
 __global__ void gelu_fwd_kernel(const float *__restrict__ x, float *__restrict__ out, long n) {
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
@@ -717,6 +813,56 @@ int layernorm_bwd(const float *dout, const float *x, const float *w, const float
                   const float *rstd, float *dx, float *dw, float *db, int T, int C, float *scratch,
                   cudaStream_t s) {
     return layernorm_bwd(dout, x, w, mean, rstd, dx, dw, db, T, C, scratch, s, kLnBwdRowsPerChunk);
+}
+
+namespace {
+int ln_bwd_fused_blocks(int T) { return std::max(1, std::min((T + 7) / 8, 148 * 2)); }
+
+template <int NJ>
+int launch_ln_bwd_fused(const float *dout, const float *x, const float *w, const float *mean, const float *rstd,
+                        float *dx, int T, int nb, int rpb, float *part, bool want_cs, cudaStream_t s) {
+    constexpr int smem = 8 * 3 * 128 * NJ * 4;
+    static bool attr = false;
+    if (!attr) {
+        CG_CUDA(cudaFuncSetAttribute(ln_bwd_fused_kernel<NJ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr = true;
+    }
+    ln_bwd_fused_kernel<NJ><<<nb, 256, smem, s>>>(dout, x, w, mean, rstd, dx, T, rpb, part, want_cs ? 1 : 0);
+    LAUNCH_CHECK();
+    return OK;
+}
+}  // namespace
+
+bool layernorm_bwd_fused_ok(int C, const void *dout, const void *x, const void *w, const void *dx) {
+    const uintptr_t a = (uintptr_t)dout | (uintptr_t)x | (uintptr_t)w | (uintptr_t)dx;
+    return C > 0 && C % 128 == 0 && C <= 1024 && (a % 16) == 0;
+}
+
+size_t layernorm_bwd_fused_scratch_bytes(int T, int C) {
+    return (size_t)ln_bwd_fused_blocks(T) * 3 * C * sizeof(float);
+}
+
+int layernorm_bwd_fused(const float *dout, const float *x, const float *w, const float *mean, const float *rstd,
+                        float *dx, float *dw, float *db, float *cs, int T, int C, float *scratch, cudaStream_t s) {
+    if (T <= 0) return OK;
+    if (!layernorm_bwd_fused_ok(C, dout, x, w, dx)) {
+        set_last_error(ERR_ARG, "layernorm_bwd_fused: C=%d needs C %% 128 == 0, C <= 1024, aligned rows", C);
+        return ERR_ARG;
+    }
+    const int nb = ln_bwd_fused_blocks(T), rpb = (T + nb - 1) / nb;
+    switch (C / 128) {
+        case 1: CG_TRY(launch_ln_bwd_fused<1>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
+        case 2: CG_TRY(launch_ln_bwd_fused<2>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
+        case 3: CG_TRY(launch_ln_bwd_fused<3>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
+        case 4: CG_TRY(launch_ln_bwd_fused<4>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
+        case 5: CG_TRY(launch_ln_bwd_fused<5>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
+        case 6: CG_TRY(launch_ln_bwd_fused<6>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
+        case 7: CG_TRY(launch_ln_bwd_fused<7>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
+        default: CG_TRY(launch_ln_bwd_fused<8>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
+    }
+    ln_bwd_part_reduce<<<dim3((C + 255) / 256, 3), 256, 0, s>>>(scratch, nb, C, dw, db, cs);
+    LAUNCH_CHECK();
+    return OK;
 }
 
 int gelu_fwd(const float *x, float *out, long n, cudaStream_t s) {

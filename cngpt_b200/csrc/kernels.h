@@ -19,6 +19,14 @@ int layernorm_bwd(const float *dout, const float *x, const float *w, const float
                   float *dx, float *dw, float *db, int T, int C, float *scratch, cudaStream_t s,
                   int rows_per_chunk);
 constexpr int kLnBwdTrainRows = 32;
+// LayerNorm backward in one pass over the rows with dw / db and, when cs is
+// given, cs += column sums of the updated dx (the bias gradient of the linear
+// layer that produced the LayerNorm input's gradient); C % 128 == 0,
+// C <= 1024, 16-byte aligned rows (layernorm_bwd_fused_ok)
+bool layernorm_bwd_fused_ok(int C, const void *dout, const void *x, const void *w, const void *dx);
+size_t layernorm_bwd_fused_scratch_bytes(int T, int C);
+int layernorm_bwd_fused(const float *dout, const float *x, const float *w, const float *mean, const float *rstd,
+                        float *dx, float *dw, float *db, float *cs, int T, int C, float *scratch, cudaStream_t s);
 int gelu_fwd(const float *x, float *out, long n, cudaStream_t s);
 int gelu_bwd(const float *dout, const float *x, float *dx, long n, cudaStream_t s);
 int softmax_rows(float *x, int rows, int cols, cudaStream_t s);

@@ -208,6 +208,7 @@ int ensure_extras(GPT *m, ModelCtx *c, int B, int T) {
     CG_TRY(dev_alloc((void **)&c->d_qkv, BT * 3 * C * sizeof(float), false));
     size_t sb = layernorm_bwd_scratch_bytes((int)BT, (int)C, kLnBwdTrainRows);
     sb = std::max(sb, colsum_scratch_bytes((int)BT, (int)(4 * C)));
+    sb = std::max(sb, layernorm_bwd_fused_scratch_bytes((int)BT, (int)C));
     sb = std::max(sb, attention_bwd_scratch_bytes(B, T, (int)H));
     sb = std::max(sb, BT * sizeof(float));  // CE row terms
     // fused LM-head + cross-entropy: row terms, then the per-64-column
@@ -398,7 +399,21 @@ int forward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, i
 }
 
 // ------------------------------------------------------------ backward
-int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, int T, cudaStream_t s) {
+// Data-parallel gradient buckets (world > 1, from the training step): each
+// layer's gradient range is final once its iteration of the backward loop has
+// run (src/model.c:691-842; the ranges are contiguous, src/model.c:66-79), so
+// it is averaged over the ranks on the communication stream while the
+// backward continues below it. The last layer's bucket also takes ln_f (final
+// after the LN_f backward, and next in the arena); wte and wpe, which the
+// embedding backward completes last, form the final bucket.
+int grad_bucket(GPT *m, ModelCtx *c, size_t off, size_t n, cudaStream_t s) {
+    CG_CUDA(cudaEventRecord(c->ev_ready, s));
+    CG_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_ready, 0));
+    return dp_allreduce(c, m->grad_buf + off, n, c->comm_stream);
+}
+
+int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, int T, cudaStream_t s,
+             bool dp_buckets = false) {
     const int C = m->cfg.n_embd, V = m->cfg.vocab_size, L = m->cfg.n_layer, H = m->cfg.n_head;
     const int BT = B * T;
     if (B != c->B || T != c->T || !m->act_buf) {
@@ -422,6 +437,20 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
         CG_TRY(ce_grad(a->probs, V, tgt, 1.0f / (float)BT, c->dlogits, c->ldlog, BT, V, s));
     }
     float *scr = c->scratch;
+    // Without dropout the LayerNorm backward passes fold in the column sums
+    // that follow them: dw / db, and the bias gradient of the projection
+    // whose output gradient the updated residual gradient is (mlp_proj after
+    // LN_f / LN1 of the layer above, c_proj after LN2). Dropout masks d_x
+    // between the two, so with dropout the separate passes run.
+    const bool fuse_ln = m->cfg.dropout <= 0.0f && C % 128 == 0 && C <= 1024;
+    auto ln_bwd = [&](const float *x_in, const float *lw, const float *mean, const float *rstd, float *gw, float *gb,
+                      float *bias_grad) -> int {
+        if (fuse_ln && layernorm_bwd_fused_ok(C, c->d_ln, x_in, lw, c->d_x))
+            return layernorm_bwd_fused(c->d_ln, x_in, lw, mean, rstd, c->d_x, gw, gb, bias_grad, BT, C, scr, s);
+        CG_TRY(layernorm_bwd(c->d_ln, x_in, lw, mean, rstd, c->d_x, gw, gb, BT, C, scr, s, kLnBwdTrainRows));
+        // unaligned rows: the bias column sum as its own pass, at the same point
+        return fuse_ln && bias_grad ? colsum_add(c->d_x, C, BT, C, bias_grad, scr, s) : OK;
+    };
     // LM head (src/model.c:672-674): d_ln_f = dlogits wte ; d_wte += dlogits^T ln_f_out
     GemmEpi e;
     e.mode = EPI_STORE;
@@ -435,8 +464,8 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
     CG_TRY(gemm(c->dlogits, c->ldlog, true, a->ln_f_out, C, true, V, C, BT, e, s));
     // LN_f (src/model.c:680-685): d_x = 0 + LN_f backward
     CG_CUDA(cudaMemsetAsync(c->d_x, 0, (size_t)BT * C * sizeof(float), s));
-    CG_TRY(layernorm_bwd(c->d_ln, L > 0 ? a->res2[L - 1] : a->emb, w->ln_f_w, a->ln_f_mean,
-                         a->ln_f_rstd, c->d_x, g->ln_f_w, g->ln_f_b, BT, C, scr, s, kLnBwdTrainRows));
+    CG_TRY(ln_bwd(L > 0 ? a->res2[L - 1] : a->emb, w->ln_f_w, a->ln_f_mean, a->ln_f_rstd, g->ln_f_w, g->ln_f_b,
+                  L > 0 ? g->mlp_proj_b[L - 1] : nullptr));
     for (int l = L - 1; l >= 0; l--) {
         const float *x_in = (l == 0) ? a->emb : a->res2[l - 1];
         if (m->cfg.dropout > 0.0f) dropout_bwd(c->d_x, a->res2_mask[l], BT * C, m->cfg.dropout);
@@ -453,7 +482,7 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
         e.D = g->mlp_proj_w[l];
         e.ldd = 4 * C;
         CG_TRY(gemm(c->d_x, C, true, a->mlp_gelu[l], 4 * C, true, C, 4 * C, BT, e, s));
-        CG_TRY(colsum_add(c->d_x, C, BT, C, g->mlp_proj_b[l], scr, s));
+        if (!fuse_ln) CG_TRY(colsum_add(c->d_x, C, BT, C, g->mlp_proj_b[l], scr, s));
         // fc (src/model.c:716-720)
         e = GemmEpi();
         e.mode = EPI_STORE;
@@ -467,8 +496,8 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
         CG_TRY(gemm(c->d_mlp, 4 * C, true, a->ln2_out[l], C, true, 4 * C, C, BT, e, s));
         CG_TRY(colsum_add(c->d_mlp, 4 * C, BT, 4 * C, g->mlp_fc_b[l], scr, s));
         // LN2 accumulates into the residual gradient: d_x becomes d_res1
-        CG_TRY(layernorm_bwd(c->d_ln, a->res1[l], w->ln2_w[l], a->ln2_mean[l], a->ln2_rstd[l], c->d_x,
-                             g->ln2_w[l], g->ln2_b[l], BT, C, scr, s, kLnBwdTrainRows));
+        CG_TRY(ln_bwd(a->res1[l], w->ln2_w[l], a->ln2_mean[l], a->ln2_rstd[l], g->ln2_w[l], g->ln2_b[l],
+                      g->c_proj_b[l]));
         if (m->cfg.dropout > 0.0f) dropout_bwd(c->d_x, a->res1_mask[l], BT * C, m->cfg.dropout);
         // c_proj (src/model.c:736-740)
         e = GemmEpi();
@@ -481,7 +510,7 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
         e.D = g->c_proj_w[l];
         e.ldd = C;
         CG_TRY(gemm(c->d_x, C, true, a->attn_out[l], C, true, C, C, BT, e, s));
-        CG_TRY(colsum_add(c->d_x, C, BT, C, g->c_proj_b[l], scr, s));
+        if (!fuse_ln) CG_TRY(colsum_add(c->d_x, C, BT, C, g->c_proj_b[l], scr, s));
         // attention (src/model.c:742-822)
         CG_TRY(attention_bwd(a->qkv[l], a->attn_out[l], c->d_ao, a->attn_scores[l], c->d_qkv, scr, B,
                              T, C, H, s));
@@ -498,12 +527,24 @@ int backward(GPT *m, ModelCtx *c, const int *tokens, const int *targets, int B, 
         CG_TRY(gemm(c->d_qkv, 3 * C, true, a->ln1_out[l], C, true, 3 * C, C, BT, e, s));
         CG_TRY(colsum_add(c->d_qkv, 3 * C, BT, 3 * C, g->c_attn_b[l], scr, s));
         // LN1 accumulates into d_x (= d_res1 + LN1 backward, src/model.c:833-840)
-        CG_TRY(layernorm_bwd(c->d_ln, x_in, w->ln1_w[l], a->ln1_mean[l], a->ln1_rstd[l], c->d_x,
-                             g->ln1_w[l], g->ln1_b[l], BT, C, scr, s, kLnBwdTrainRows));
+        CG_TRY(ln_bwd(x_in, w->ln1_w[l], a->ln1_mean[l], a->ln1_rstd[l], g->ln1_w[l], g->ln1_b[l],
+                      l > 0 ? g->mlp_proj_b[l - 1] : nullptr));
+        if (dp_buckets) {
+            const size_t off = (size_t)(g->ln1_w[l] - m->grad_buf);
+            const size_t n = l == L - 1 ? (size_t)m->n_params - off : (size_t)layer_floats(C);
+            CG_TRY(grad_bucket(m, c, off, n, s));
+        }
     }
     if (m->cfg.dropout > 0.0f) dropout_bwd(c->d_x, a->emb_mask, BT * C, m->cfg.dropout);
     // embeddings (src/model.c:852-867)
     CG_TRY(embed_bwd(tok, c->d_x, g->wte, g->wpe, B, T, C, s));
+    if (dp_buckets) {
+        const size_t n_emb = (size_t)(g->ln1_w && L > 0 ? g->ln1_w[0] - m->grad_buf : m->n_params);
+        CG_TRY(grad_bucket(m, c, 0, n_emb, s));
+        // the optimizer waits for every bucket
+        CG_CUDA(cudaEventRecord(c->ev_done, c->comm_stream));
+        CG_CUDA(cudaStreamWaitEvent(s, c->ev_done, 0));
+    }
     return OK;
 }
 
@@ -793,7 +834,7 @@ extern "C" void gpt_free(GPT *m) {
         if (it != g_models.end()) c = it->second;
     }
     cudaStreamSynchronize(g_stream);
-    if (c && c->nccl_comm) cngpt_cuda_dp_free(m);
+    if (c && (c->nccl_comm || c->comm_stream)) cngpt_cuda_dp_free(m);
     tp_release(m);
     dev_free(m->param_buf);
     dev_free(m->grad_buf);
@@ -886,10 +927,16 @@ extern "C" int cngpt_cuda_train_step(GPT *m, const int *tokens, const int *targe
         return ERR_ARG;
     }
     cudaStream_t s = g_stream;
+    const bool dp = c->world > 1 && c->nccl_comm;
     CG_CUDA(cudaMemsetAsync(m->grad_buf, 0, (size_t)m->n_params * sizeof(float), s));
     CG_TRY(forward(m, c, tokens, targets, B, T, true, s, true));
-    CG_TRY(backward(m, c, tokens, targets, B, T, s));
-    if (c->world > 1) CG_TRY(dp_allreduce(c, m->grad_buf, (size_t)m->n_params, s));
+    if (dp) {
+        // the reported loss is the mean over the global batch (every rank has B*T rows)
+        CG_CUDA(cudaEventRecord(c->ev_ready, s));
+        CG_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_ready, 0));
+        CG_TRY(dp_allreduce(c, &c->dev_scalars[0], 1, c->comm_stream));
+    }
+    CG_TRY(backward(m, c, tokens, targets, B, T, s, dp));
     CG_TRY(adamw_step(m, c, lr, beta1, beta2, eps, wd, grad_clip, s));
     if (loss_out) {
         CG_CUDA(cudaMemcpyAsync(c->host_loss, &c->dev_scalars[0], sizeof(float), cudaMemcpyDeviceToHost, s));

@@ -37,6 +37,9 @@ struct ModelCtx {
     // data parallel
     void *nccl_comm = nullptr;
     int world = 1, rank = 0;
+    // gradient buckets averaged on their own stream while the backward runs
+    cudaStream_t comm_stream = nullptr;
+    cudaEvent_t ev_ready = nullptr, ev_done = nullptr;
 };
 
 struct FastDev {

@@ -162,9 +162,14 @@ int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B, int T, int
 
 /* ---- data-parallel training over NCCL -------------------------------------
  * One process per GPU. Rank 0 creates the id and shares it out of band. After
- * dp_init, gpt_backward is followed by a sum-allreduce of the gradient arena
- * scaled by 1/world (the mean over the global batch) inside
- * cngpt_cuda_train_step, and explicitly by cngpt_cuda_dp_allreduce_grads. */
+ * dp_init, cngpt_cuda_train_step averages the gradient arena over the ranks
+ * (the gradient of the mean loss over the global batch) in per-layer buckets:
+ * each layer's gradients are averaged on a separate stream as soon as the
+ * backward has finished that layer, while it continues with the layers below;
+ * the embeddings (wte, wpe) go last. Its loss_out is the mean loss over the
+ * global batch. cngpt_cuda_dp_allreduce_grads averages the whole arena at
+ * once, for callers that drive gpt_backward themselves. A second dp_init
+ * replaces the first one's communicator. */
 int cngpt_cuda_dp_unique_id(unsigned char id[128]);
 int cngpt_cuda_dp_init(GPT *m, const unsigned char id[128], int world, int rank);
 int cngpt_cuda_dp_allreduce_grads(GPT *m);

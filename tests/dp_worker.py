@@ -1,8 +1,10 @@
-"""One rank of the 2-GPU data-parallel parity test (tests/test_dp_gpu.py),
+"""One rank of the data-parallel parity tests (tests/test_dp_gpu.py),
 launched by torchrun. Each rank runs forward + backward of its own slice of
 the global batch through libcngpt_cuda, averages the gradient arena over NCCL
-(cngpt_cuda_dp_allreduce_grads), takes one AdamW step, and saves its
-gradients and parameters for the parent test to compare."""
+(cngpt_cuda_dp_allreduce_grads) and takes one AdamW step; then, on a fresh
+model, cngpt_cuda_train_step with its per-layer buckets overlapped with the
+backward (lr 0, then three real steps). It saves gradients, parameters and
+losses for the parent test to compare."""
 import ctypes as C
 import os
 import sys
@@ -51,7 +53,29 @@ def main(out_dir: str):
     lib.gpt_adamw(C.byref(m), 1e-3, 0.9, 0.95, 1e-8, 0.1, 1.0)
     p = np.empty(m.n_params, np.float32)
     abi.check(lib, lib.cngpt_cuda_params_to_host(C.byref(m), p.ctypes.data), "params")
-    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), grads=g, params=p, loss=np.float32(loss))
+    abi.check(lib, lib.cngpt_cuda_dp_free(C.byref(m)), "dp_free")
+    lib.gpt_free(C.byref(m))
+    # the training step's bucketed average (overlapped with the backward): with
+    # lr = 0 and no clipping the arena keeps the averaged gradients
+    m = abi.GPT()
+    assert lib.gpt_init(C.byref(m), abi.GPTConfig(*CFG, 0.0)) == 0
+    oracle.libc_rand_stream(7)
+    lib.gpt_init_weights(C.byref(m))
+    abi.check(lib, lib.cngpt_cuda_dp_init(C.byref(m), uid, world, rank), "dp_init")
+    ts_loss = C.c_float()
+    abi.check(lib, lib.cngpt_cuda_train_step(C.byref(m), tok.ctypes.data, tgt.ctypes.data, B, T, 0.0, 0.9, 0.95,
+                                             1e-8, 0.0, 0.0, C.byref(ts_loss)), "train_step lr 0")
+    ts_loss0 = ts_loss.value
+    ts_g = np.empty(m.n_params, np.float32)
+    abi.check(lib, lib.cngpt_cuda_grads_to_host(C.byref(m), ts_g.ctypes.data), "grads")
+    # then real steps: every rank must hold the same parameters
+    for _ in range(3):
+        abi.check(lib, lib.cngpt_cuda_train_step(C.byref(m), tok.ctypes.data, tgt.ctypes.data, B, T, 1e-3, 0.9, 0.95,
+                                                 1e-8, 0.1, 1.0, C.byref(ts_loss)), "train_step")
+    ts_p = np.empty(m.n_params, np.float32)
+    abi.check(lib, lib.cngpt_cuda_params_to_host(C.byref(m), ts_p.ctypes.data), "params")
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), grads=g, params=p, loss=np.float32(loss), ts_grads=ts_g,
+             ts_params=ts_p, ts_loss=np.float32(ts_loss.value), ts_loss0=np.float32(ts_loss0))
     abi.check(lib, lib.cngpt_cuda_dp_free(C.byref(m)), "dp_free")
     lib.gpt_free(C.byref(m))
     dist.destroy_process_group()

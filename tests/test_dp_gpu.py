@@ -50,6 +50,16 @@ def test_dp_matches_single_gpu_average(lib, cuda, world):
         acc += m.grads()
     avg = (acc / world).astype(np.float32)
     e = nwerr(res[0]["grads"], avg)
-    print(f"\ndp{world} averaged gradient vs single-GPU mean: normwise {e:.2e}")
+    e_ts = nwerr(res[0]["ts_grads"], avg)
+    print(f"\ndp{world} averaged gradient vs single-GPU mean: normwise {e:.2e}; "
+          f"train_step buckets: {e_ts:.2e}")
     assert e < 1e-6
+    # train_step's fused cross-entropy sums the softmax in another order than
+    # gpt_forward's: 1e-5 (the 3xTF32 gradient level of these tests)
+    assert e_ts < 1e-5
+    losses = [float(r["loss"]) for r in res]
+    assert abs(float(res[0]["ts_loss0"]) - float(np.mean(losses))) <= 1e-5 * abs(np.mean(losses))
+    for rk in range(1, world):
+        assert float(res[rk]["ts_loss"]) == float(res[0]["ts_loss"])
+        assert np.array_equal(res[rk]["ts_params"], res[0]["ts_params"]), f"rank {rk} diverged in train_step"
     m.free()
