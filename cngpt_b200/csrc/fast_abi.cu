@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "abi_common.h"
+#include "decode_mk.h"
 #include "kernels.h"
 #include "model_ctx.h"
 
@@ -153,6 +154,40 @@ int fast_forward(const GPT *m, FastCtx *f, FastDev *d, const int *tok, int B, in
 int decode_step(const GPT *m, FastCtx *f, FastDev *d, int B, cudaStream_t s) {
     const int C = m->cfg.n_embd, V = m->cfg.vocab_size, L = m->cfg.n_layer, H = m->cfg.n_head;
     const GPTWeights *w = &m->params;
+    if (d->mk_bar && mk_decode_ok(B, C, H, d->kv_T)) {
+        // the whole step as one cooperative launch (decode_mk.cu)
+        MkArgs a;
+        a.params = m->param_buf;
+        a.wte = w->wte;
+        a.wpe = w->wpe;
+        a.L = L;
+        a.C = C;
+        a.H = H;
+        a.V = V;
+        a.block = m->cfg.block_size;
+        a.B = B;
+        a.Tmax = d->kv_T;
+        a.scale = 1.0f / sqrtf((float)(C / H));
+        a.x = d->xl;
+        a.qkv = f->qkv;
+        a.att = d->al;
+        a.hid = f->hid;
+        a.logits = f->logits;
+        a.ldlog = V;
+        a.kc = d->kc;
+        a.vc = d->vc;
+        a.part = d->dec_part;
+        a.tickets = (int *)(d->dec_part + mk_part_floats(B, H, d->kv_T));
+        a.S = (int)((d->kv_T + 63) / 64);
+        a.next = d->next;
+        a.gen = d->gen;
+        a.ctr = d->ctr;
+        a.am_key = d->am_key;
+        a.bar = d->mk_bar;
+        a.abort = (int *)(d->mk_bar + 1);
+        a.fast_act = 0;  // accurate tanh, as the GEMV decode path
+        return decode_step_mk(a, s);
+    }
     float *x = d->xl;
     CG_TRY(embed_fwd_at(d->next, w->wte, w->wpe, x, B, C, d->ctr, s));
     const size_t per = (size_t)d->kv_B * d->kv_T * C;
@@ -258,6 +293,7 @@ extern "C" void fast_free(FastCtx *f) {
         dev_free(d->ln_stats);
         dev_free(d->ln_ticket);
         dev_free(d->am_key);
+        dev_free(d->mk_bar);
         drop_graph(d);
         if (d->ev_a) cudaEventDestroy(d->ev_a);
         if (d->ev_b) cudaEventDestroy(d->ev_b);
@@ -307,6 +343,8 @@ int kv_prepare(const GPT *m, FastCtx *f, FastDev *d, int B, int T, int n_new, bo
         CG_CUDA(cudaMemsetAsync(d->ln_ticket, 0, 4 * sizeof(int), s));
         CG_TRY(dev_alloc((void **)&d->am_key, 8 * sizeof(unsigned long long), false));
         CG_CUDA(cudaMemsetAsync(d->am_key, 0, 8 * sizeof(unsigned long long), s));
+        CG_TRY(dev_alloc((void **)&d->mk_bar, 2 * sizeof(unsigned long long), false));
+        CG_CUDA(cudaMemsetAsync(d->mk_bar, 0, 2 * sizeof(unsigned long long), s));
     }
     if (d->kv_B != B || d->kv_T < Tmax) {
         CG_CUDA(cudaStreamSynchronize(s));

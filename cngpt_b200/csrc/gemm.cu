@@ -1169,6 +1169,20 @@ __global__ void splitk_reduce_kernel(const float *__restrict__ ws, int S, long s
                 a.w += b.w;
             }
             const int m = i / N4, n = (i - m * N4) * 4;
+            if (epi.vec4 && (epi.mode == EPI_ACCUM || epi.mode == EPI_STORE)) {
+                // the weight-gradient products: 16-byte accesses of D
+                const float4 b4 = epi.bias ? *(const float4 *)(epi.bias + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+                float4 *d = (float4 *)(epi.D + (long)m * epi.ldd + n);
+                const float al = epi.alpha;
+                if (epi.mode == EPI_ACCUM) {
+                    const float4 o = *d;
+                    *d = make_float4((o.x + a.x * al) + b4.x, (o.y + a.y * al) + b4.y, (o.z + a.z * al) + b4.z,
+                                     (o.w + a.w * al) + b4.w);
+                } else {
+                    *d = make_float4(a.x * al + b4.x, a.y * al + b4.y, a.z * al + b4.z, a.w * al + b4.w);
+                }
+                continue;
+            }
             const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j)

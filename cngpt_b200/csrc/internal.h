@@ -28,6 +28,7 @@ enum DevError : int {
     DEV_ERR_GEMM_EPILOGUE = 103,
     DEV_ERR_GEMM_TRANSFORM = 104,
     DEV_ERR_TP_FLAG = 201,  // a peer's partial sum did not arrive in time
+    DEV_ERR_DECODE_BARRIER = 301,  // a grid barrier of the single-launch decode step gave up
 };
 
 void set_last_error(int status, const char *fmt, ...);
@@ -38,12 +39,14 @@ int gemm_take_dev_error();
 int attn_take_dev_error();
 int tp_take_dev_error();
 int attn_tc_take_dev_error();
+int mk_take_dev_error();
 // set the limit of every bounded device wait of one translation unit (0 on
 // success); set_wait_limit_ns sets all of them
 int gemm_set_wait_limit(unsigned long long ns);
 int attn_set_wait_limit(unsigned long long ns);
 int tp_set_wait_limit(unsigned long long ns);
 int attn_tc_set_wait_limit(unsigned long long ns);
+int mk_set_wait_limit(unsigned long long ns);
 int set_wait_limit_ns(unsigned long long ns);
 
 #define CG_CUDA(call)                                                                 \

@@ -210,17 +210,28 @@ ln_bwd_fused_kernel(const float *__restrict__ dout, const float *__restrict__ x,
     }
 }
 
-// dw, db (and cs) += the blocks' partials part[nb][3][C], summed in block order
+// dw, db (and cs) += the blocks' partials part[nb][3][C]: one block per 32 of
+// the 3C sums, lane = sum, warp w adds the partials of blocks w, w + 8, ... in
+// order, then the 8 warp totals are added in warp order (fixed order).
 __global__ void __launch_bounds__(256)
 ln_bwd_part_reduce(const float *__restrict__ part, int nb, int C, float *__restrict__ dw, float *__restrict__ db,
                    float *__restrict__ cs) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    const int k = blockIdx.y;  // 0: dw, 1: db, 2: cs
-    float *dst = k == 0 ? dw : (k == 1 ? db : cs);
-    if (c >= C || !dst) return;
+    __shared__ float red[8][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int j = blockIdx.x * 32 + lane;  // index into [3][C]
     float v = 0.f;
-    for (int b = 0; b < nb; ++b) v += part[((long)b * 3 + k) * C + c];
-    dst[c] += v;
+    if (j < 3 * C)
+        for (int b = warp; b < nb; b += 8) v += part[(long)b * 3 * C + j];
+    red[warp][lane] = v;
+    __syncthreads();
+    if (warp == 0 && j < 3 * C) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) t += red[w][lane];
+        const int k = j / C, c = j - k * C;  // 0: dw, 1: db, 2: cs
+        float *dst = k == 0 ? dw : (k == 1 ? db : cs);
+        if (dst) dst[c] += t;
+    }
 }
 
 // ---------------------------------------------------------------- GELU
@@ -860,7 +871,7 @@ int layernorm_bwd_fused(const float *dout, const float *x, const float *w, const
         case 7: CG_TRY(launch_ln_bwd_fused<7>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
         default: CG_TRY(launch_ln_bwd_fused<8>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
     }
-    ln_bwd_part_reduce<<<dim3((C + 255) / 256, 3), 256, 0, s>>>(scratch, nb, C, dw, db, cs);
+    ln_bwd_part_reduce<<<(3 * C + 31) / 32, 256, 0, s>>>(scratch, nb, C, dw, db, cs);
     LAUNCH_CHECK();
     return OK;
 }

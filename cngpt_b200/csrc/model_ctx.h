@@ -59,6 +59,7 @@ struct FastDev {
     float *ln_stats = nullptr;  // [2][8][2] LayerNorm statistics handed between decode GEMVs
     int *ln_ticket = nullptr;   // [4] last-block tickets of the statistics GEMVs ([0..1] used)
     unsigned long long *am_key = nullptr;  // [8] greedy argmax keys of the LM-head GEMV
+    unsigned long long *mk_bar = nullptr;  // grid-barrier counter + abort word of the single-launch step
     // one decode step captured as a CUDA graph, reused while the key matches
     cudaStream_t cap_stream = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;

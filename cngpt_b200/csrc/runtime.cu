@@ -37,7 +37,7 @@ const char *last_message() { return g_msg; }
 
 int check_device_error() {
     int (*readers[])() = {gemm_take_dev_error, attn_take_dev_error, tp_take_dev_error,
-                            attn_tc_take_dev_error};
+                            attn_tc_take_dev_error, mk_take_dev_error};
     for (auto rd : readers) {
         int code = rd();
         if (code < 0) {
@@ -54,7 +54,7 @@ int check_device_error() {
 
 int set_wait_limit_ns(unsigned long long ns) {
     int (*setters[])(unsigned long long) = {gemm_set_wait_limit, attn_set_wait_limit, tp_set_wait_limit,
-                                            attn_tc_set_wait_limit};
+                                            attn_tc_set_wait_limit, mk_set_wait_limit};
     for (auto set : setters)
         if (set(ns) != 0) {
             set_last_error(ERR_CUDA, "setting the device wait limit failed");

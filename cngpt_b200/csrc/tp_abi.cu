@@ -29,6 +29,7 @@
 
 #include "abi_common.h"
 #include "common.cuh"
+#include "decode_mk.h"
 #include "kernels.h"
 #include "model_ctx.h"
 
@@ -108,6 +109,7 @@ struct TpState {
     int *d_step = nullptr, *d_ticket = nullptr;
     float *d_stats = nullptr;  // [8][2] LayerNorm statistics of x after each exchange
     unsigned long long *am_key = nullptr;  // [8] greedy keys of the LM-head GEMV
+    unsigned long long *mk_bar = nullptr;  // grid barrier of the single-launch decode step (world 1)
 
     const float *qkv_w(int l) const { return wbuf + (size_t)l * 3 * Cl * C; }
     const float *qkv_b(int l) const { return wbuf + (size_t)L * 3 * Cl * C + (size_t)l * 3 * Cl; }
@@ -368,6 +370,40 @@ int prefill(const GPT *m, TpState *t, const int *tok, int B, int T, bool kv, cud
 int decode_step(const GPT *m, TpState *t, int B, cudaStream_t s) {
     const GPTWeights *w = &m->params;
     const int C = t->C, Cl = t->Cl, nf = t->p.nf, L = t->L;
+    if (t->world == 1 && t->mk_bar && mk_decode_ok(B, C, t->H, t->kv_T)) {
+        // one rank holds every head: the single-launch step over the arena (decode_mk.cu)
+        MkArgs a;
+        a.params = m->param_buf;
+        a.wte = w->wte;
+        a.wpe = w->wpe;
+        a.L = L;
+        a.C = C;
+        a.H = t->H;
+        a.V = t->V;
+        a.block = m->cfg.block_size;
+        a.B = B;
+        a.Tmax = t->kv_T;
+        a.scale = 1.0f / sqrtf((float)t->hs);
+        a.x = t->xl;
+        a.qkv = t->qkv;
+        a.att = t->al;
+        a.hid = t->hid;
+        a.logits = t->logits;
+        a.ldlog = t->ldlog;
+        a.kc = t->kc;
+        a.vc = t->vc;
+        a.part = t->dec_part;
+        a.tickets = (int *)(t->dec_part + mk_part_floats(B, t->H, t->kv_T));
+        a.S = (int)((t->kv_T + 63) / 64);
+        a.next = t->next;
+        a.gen = t->gen;
+        a.ctr = t->ctr;
+        a.am_key = t->am_key;
+        a.bar = t->mk_bar;
+        a.abort = (int *)(t->mk_bar + 1);
+        a.fast_act = 0;  // accurate tanh, as the GEMV decode path
+        return decode_step_mk(a, s);
+    }
     float *x = t->xl;
     CG_TRY(embed_fwd_at(t->next, w->wte, w->wpe, x, B, C, t->ctr, s));
     const size_t per = (size_t)t->kv_B * t->kv_T * Cl;
@@ -489,6 +525,7 @@ void release(TpState *t) {
     dev_free(t->d_ticket);
     dev_free(t->d_stats);
     dev_free(t->am_key);
+    dev_free(t->mk_bar);
     float *bufs[] = {t->wbuf, t->x,  t->ln,     t->qkv, t->aout, t->hid, t->mean, t->rstd,
                      t->xl,   t->al, t->logits, t->lgath, t->kc,  t->vc, t->dec_part};
     for (auto b : bufs) dev_free(b);
@@ -647,7 +684,9 @@ extern "C" int cngpt_cuda_tp_init(GPT *m, const unsigned char id[128], int world
     st = dev_alloc((void **)&t->ctr, 2 * sizeof(int), false);
     if (st != OK) return fail(st);
     if ((st = dev_alloc((void **)&t->am_key, 8 * sizeof(unsigned long long), false)) != OK) return fail(st);
-    if (cudaMemset(t->am_key, 0, 8 * sizeof(unsigned long long)) != cudaSuccess) {
+    if ((st = dev_alloc((void **)&t->mk_bar, 2 * sizeof(unsigned long long), false)) != OK) return fail(st);
+    if (cudaMemset(t->am_key, 0, 8 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(t->mk_bar, 0, 2 * sizeof(unsigned long long)) != cudaSuccess) {
         set_last_error(ERR_CUDA, "tp_init: clearing the argmax keys failed");
         return fail(ERR_CUDA);
     }

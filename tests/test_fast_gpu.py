@@ -159,3 +159,24 @@ def test_sample_kv_cache_matches_reference_stream(lib, cuda, temp, k):
     assert launches <= n * (5 * c["L"] + 3) + 100, launches
     ref.free()
     dev.free()
+
+
+@pytest.mark.parametrize("name,B", [("hs64", 1), ("hs64", 3), ("small1", 8)])
+def test_decode_step_is_one_launch(lib, cuda, name, B):
+    """Sequences up to 8 with head size 64 decode each token in one
+    cooperative launch (all layers, the LM head and the greedy pick)."""
+    ref, dev, c = pair(lib, name)
+    ref.free()
+    prompt = oracle.lcg_tokens(B * 8, c["V"], seed=2)
+    out = np.zeros(B * 2, np.int32)
+    fc = abi.FastCtx()
+    lib.fast_init(C.byref(fc))
+    counts = []
+    for n in (1, 2):
+        l0 = lib.cngpt_cuda_launch_count()
+        abi.check(lib, lib.cngpt_cuda_generate(C.byref(dev.m), C.byref(fc), prompt.ctypes.data, B, 8, n,
+                                               out.ctypes.data), "generate")
+        counts.append(lib.cngpt_cuda_launch_count() - l0)
+    lib.fast_free(C.byref(fc))
+    dev.free()
+    assert counts[1] - counts[0] == 1, counts  # n = 2 adds one eager decode step
