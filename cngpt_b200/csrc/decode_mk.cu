@@ -154,12 +154,13 @@ __device__ void mk_stage(float *xs, const float *src, long lds, int B, int K, co
     __syncthreads();
 }
 
-// ------------------------------------------------------------ warp GEMV
-// Rows of W [N, K] owned by this block: [n_lo, n_hi), taken RW at a time by
-// the block's warps in turn; the lanes split K in float4 units, CH at a time
-// per row (RW * CH float4 loads in flight per lane). The RW * MT partial sums are reduced across the warp by
-// recursive halving (lane ends with one total, index idx) and handed to the
-// epilogue with the row n and sequence m they belong to.
+// ------------------------------------------------------------ block GEMV
+// Rows of W [N, K] (row pitch ldw) owned by this block: [lo, hi), R at a time.
+// All 512 threads split K in float4 units (KI steps of 512 at most), so each
+// thread has R * KI 16-byte loads of W in flight before it multiplies; the
+// R * MT partial sums are reduced across each warp by recursive halving and
+// across the 16 warps through shared memory in warp order (fixed order), and
+// the epilogue gets (sequence m, row n, total).
 template <int NV>
 __device__ __forceinline__ void halve(float *a, int lane, int o, int &idx) {
     constexpr int h = NV / 2;
@@ -185,59 +186,63 @@ __device__ __forceinline__ int warp_reduce_vec(float *a, int lane) {
     return ((lane & (32 / NV - 1)) == 0) ? idx : -1;
 }
 
-// rows of a product owned by block b: contiguous, a multiple of RW each
-template <int RW>
+// rows of a product owned by block b: contiguous, a multiple of R each
+template <int R>
 __device__ __forceinline__ void mk_rows(int N, int &lo, int &hi) {
-    const int per = (((N + (int)gridDim.x - 1) / (int)gridDim.x) + RW - 1) / RW * RW;
+    const int per = (((N + (int)gridDim.x - 1) / (int)gridDim.x) + R - 1) / R * R;
     lo = min(N, (int)blockIdx.x * per);
     hi = min(N, lo + per);
 }
 
-template <int MT, int RW, int CH, class Epi>
-__device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__ W, int N, Epi epi) {
-    constexpr int NV = RW * MT;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, K4 = K >> 2;
+template <int MT, int R, int KI, class Epi>
+__device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__ W, long ldw, int N, Epi epi,
+                        float *red) {
+    constexpr int NV = R * MT;
+    static_assert(NV <= 32, "partial sums per thread");
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, K4 = K >> 2;
     const float4 *x4 = (const float4 *)xs;
     int lo, hi;
-    mk_rows<RW>(N, lo, hi);
-    for (int n0 = lo + warp * RW; n0 < hi; n0 += MK_WARPS * RW) {
-        const float4 *w4[RW];
+    mk_rows<R>(N, lo, hi);
+    for (int n0 = lo; n0 < hi; n0 += R) {
+        float4 wv[KI][R];
 #pragma unroll
-        for (int r = 0; r < RW; ++r) w4[r] = (const float4 *)(W + (long)min(n0 + r, N - 1) * K);
+        for (int i = 0; i < KI; ++i) {
+            const int k = t + i * MK_THREADS;
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                wv[i][r] = k < K4 ? __ldcs((const float4 *)(W + (long)min(n0 + r, N - 1) * ldw) + k)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         float acc[NV];
 #pragma unroll
-        for (int i = 0; i < NV; ++i) acc[i] = 0.f;
-        for (int k0 = lane; k0 < K4; k0 += 32 * CH) {
-            float4 wv[RW][CH];
+        for (int j = 0; j < NV; ++j) acc[j] = 0.f;
 #pragma unroll
-            for (int c = 0; c < CH; ++c) {
-                const int k = k0 + 32 * c;
+        for (int i = 0; i < KI; ++i) {
+            const int k = t + i * MK_THREADS;
+            if (k < K4) {
 #pragma unroll
-                for (int r = 0; r < RW; ++r)
-                    wv[r][c] = k < K4 ? __ldcs(w4[r] + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+                for (int m = 0; m < MT; ++m) {
+                    if (m < B) {
+                        const float4 xv = x4[m * K4 + k];
 #pragma unroll
-            for (int c = 0; c < CH; ++c) {
-                const int k = k0 + 32 * c;
-                if (k < K4) {
-#pragma unroll
-                    for (int m = 0; m < MT; ++m) {
-                        if (m < B) {
-                            const float4 xv = x4[m * K4 + k];
-#pragma unroll
-                            for (int r = 0; r < RW; ++r)
-                                acc[r * MT + m] += wv[r][c].x * xv.x + wv[r][c].y * xv.y + wv[r][c].z * xv.z +
-                                                   wv[r][c].w * xv.w;
-                        }
+                        for (int r = 0; r < R; ++r)
+                            acc[r * MT + m] += wv[i][r].x * xv.x + wv[i][r].y * xv.y + wv[i][r].z * xv.z +
+                                               wv[i][r].w * xv.w;
                     }
                 }
             }
         }
         const int idx = warp_reduce_vec<NV>(acc, lane);
-        if (idx >= 0) {
-            const int r = idx / MT, m = idx - r * MT, n = n0 + r;
-            if (m < B && n < hi) epi(m, n, acc[0]);
+        if (idx >= 0) red[warp * 32 + idx] = acc[0];
+        __syncthreads();
+        if (t < NV) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < MK_WARPS; ++w) v += red[w * 32 + t];
+            const int r = t / MT, m = t - r * MT, n = n0 + r;
+            if (m < B && n < hi) epi(m, n, v);
         }
+        __syncthreads();
     }
 }
 
@@ -254,105 +259,127 @@ __device__ __forceinline__ void mk_prefetch(const float *W, int N, int K) {
 }
 
 // ------------------------------------------------------------ attention
-// One (sequence b, head h, chunk ch) item on 256 threads (half `hf` of the
-// block, synchronised with named barrier 1 + hf): scores of the chunk's 64
-// keys (4 threads per key, 16 dimensions each), softmax terms, P V over
-// the chunk (4 key groups per dimension), the chunk's (max, sum, outputs) to
-// `part`; the last chunk of (b, h) to finish merges all chunks in chunk order.
-__device__ __forceinline__ void half_sync(int hf) {
-    asm volatile("bar.sync %0, %1;" ::"r"(1 + hf), "r"(256) : "memory");
+// One (sequence b, head h, 64-key chunk ch) item on a group of 128 threads
+// (four groups per block, each synchronised by its own named barrier): scores
+// of the chunk's keys (a half-warp per key, float4 of the head's 64
+// dimensions per lane), V of the chunk loaded while the scores reduce, softmax
+// terms, P V (two key halves per dimension), and the chunk's (max, sum,
+// outputs) to `part`; the last chunk of (b, h) to finish (integer ticket)
+// merges every chunk in chunk order into att.
+__device__ __forceinline__ void group_sync(int g) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(128) : "memory");
 }
 
+constexpr int MK_GROUP_FLOATS = 64 * 5 + 4;
+
 __device__ void mk_attention_item(const MkArgs &a, const float *kc_l, const float *vc_l, int b, int h, int ch,
-                                  int len, int nch, float *sm, int hf) {
-    const int t = threadIdx.x & 255, C = a.C;
-    float *sc = sm, *pr = sm + 64, *po = sm + 128, *misc = sm + 128 + 256;  // misc: m, l, last
+                                  int len, int nch, float *sm, int g) {
+    const int t = threadIdx.x & 127, C = a.C;
+    float *sc = sm, *pr = sm + 64, *so = sm + 128, *cm = sm + 192, *cl = sm + 256, *misc = sm + 320;
+    const int warp = t >> 5, lane = t & 31, half = lane >> 4, l16 = lane & 15;
     const int j0 = ch * MK_KEYS, kend = min(MK_KEYS, len - j0);
-    const int kk = t >> 2, qd = t & 3;
-    const float *q = a.qkv + (long)b * 3 * C + h * 64 + qd * 16;
     const long brow = (long)b * a.Tmax * C + h * 64;
-    float d = 0.f;
-    if (kk < kend) {
-        const float4 *kr = (const float4 *)(kc_l + brow + (long)(j0 + kk) * C + qd * 16);
+    const float4 qv = __ldcg((const float4 *)(a.qkv + (long)b * 3 * C + h * 64) + l16);
+    float d[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float4 kv = __ldcg(kr + i), qv = __ldcg((const float4 *)q + i);
-            d += (qv.x * kv.x + qv.y * kv.y) + (qv.z * kv.z + qv.w * kv.w);
+    for (int i = 0; i < 8; ++i) {
+        const int jl = warp * 16 + 2 * i + half;
+        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (jl < kend) kv = __ldcg((const float4 *)(kc_l + brow + (long)(j0 + jl) * C) + l16);
+        d[i] = qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+    }
+    // V of this thread's 32 keys (thread (kh, dim): keys 32 kh .., one dimension)
+    const int dim = t & 63, kh = t >> 6;
+    float vr[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        vr[i] = (kh * 32 + i < kend) ? __ldcg(vc_l + brow + (long)(j0 + kh * 32 + i) * C + dim) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) d[i] += __shfl_xor_sync(0xffffffffu, d[i], o);
+    if (l16 == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int jl = warp * 16 + 2 * i + half;
+            sc[jl] = jl < kend ? d[i] * a.scale : -INFINITY;
         }
     }
-    d += __shfl_xor_sync(0xffffffffu, d, 1);
-    d += __shfl_xor_sync(0xffffffffu, d, 2);
-    if (qd == 0) sc[kk] = kk < kend ? d * a.scale : -INFINITY;
-    // V of this thread's 16 keys (dimension t % 64, keys 16 (t / 64) ..), loaded while the scores settle
-    const int dim = t & 63, kg = t >> 6;
-    float vr[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int j = kg * 16 + i;
-        vr[i] = j < kend ? __ldcg(vc_l + brow + (long)(j0 + j) * C + dim) : 0.f;
-    }
-    half_sync(hf);
-    if (t < 32) {
-        float mx = fmaxf(sc[t], sc[t + 32]);
-        mx = warp_max(mx);  // sc[0] is a valid key: finite
-        const float p0 = expf(sc[t] - mx), p1 = expf(sc[t + 32] - mx);
-        pr[t] = p0;
-        pr[t + 32] = p1;
-        const float l = warp_sum(p0 + p1);
-        if (t == 0) {
-            misc[0] = mx;
-            misc[1] = l;
+    group_sync(g);
+    if (warp < 2) {
+        // warps 0 and 1 each take 32 of the scores; the maximum of all 64
+        // (sc[0] is a valid key, so it is finite) and the softmax terms
+        float m = fmaxf(sc[lane], sc[lane + 32]);
+        m = warp_max(m);
+        const float p = expf(sc[warp * 32 + lane] - m);
+        pr[warp * 32 + lane] = p;
+        const float w = warp_sum(p);
+        if (lane == 0) {
+            misc[warp] = w;
+            misc[2] = m;
         }
     }
-    half_sync(hf);
+    group_sync(g);
     float acc = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc += pr[kg * 16 + i] * vr[i];
-    po[kg * 64 + dim] = acc;
-    half_sync(hf);
+    for (int i = 0; i < 32; ++i) acc += pr[kh * 32 + i] * vr[i];
+    if (kh == 1) so[dim] = acc;
+    group_sync(g);
     const int bh = b * a.H + h;
     float *pp = a.part + ((long)bh * a.S + ch) * MK_PART;
-    if (t < 64) {
-        pp[2 + t] = (po[t] + po[64 + t]) + (po[128 + t] + po[192 + t]);
-        if (t == 0) {
-            pp[0] = misc[0];
-            pp[1] = misc[1];
+    if (kh == 0) {
+        pp[2 + dim] = acc + so[dim];
+        if (dim == 0) {
+            pp[0] = misc[2];
+            pp[1] = misc[0] + misc[1];
         }
     }
     __threadfence();
-    half_sync(hf);
-    if (t == 0) misc[2] = (atomicAdd(&a.tickets[bh], 1) == nch - 1) ? 1.f : 0.f;
-    half_sync(hf);
-    if (misc[2] != 0.f) {
+    group_sync(g);
+    if (t == 0) misc[3] = (atomicAdd(&a.tickets[bh], 1) == nch - 1) ? 1.f : 0.f;
+    group_sync(g);
+    if (misc[3] != 0.f) {
         __threadfence();
+        const float *pb = a.part + (long)bh * a.S * MK_PART;
+        for (int k = t; k < nch; k += 128) {
+            cm[k] = __ldcg(pb + k * MK_PART);
+            cl[k] = __ldcg(pb + k * MK_PART + 1);
+        }
+        group_sync(g);
         if (t < 64) {
-            const float *pb = a.part + (long)bh * a.S * MK_PART;
             float M = -INFINITY;
-            for (int k = 0; k < nch; ++k) M = fmaxf(M, __ldcg(pb + k * MK_PART));
+            for (int k = 0; k < nch; ++k) M = fmaxf(M, cm[k]);
             float L = 0.f, O = 0.f;
             for (int k = 0; k < nch; ++k) {
-                const float w = expf(__ldcg(pb + k * MK_PART) - M);
-                L += __ldcg(pb + k * MK_PART + 1) * w;
+                const float w = expf(cm[k] - M);
+                L += cl[k] * w;
                 O += __ldcg(pb + k * MK_PART + 2 + t) * w;
             }
             a.att[(long)b * C + h * 64 + t] = O / L;
             if (t == 0) a.tickets[bh] = 0;
         }
     }
-    half_sync(hf);
+    group_sync(g);
 }
 
 // ------------------------------------------------------------ the step
 template <int MT>
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     extern __shared__ float4 mk_smem4[];
-    float *xs = (float *)mk_smem4;                         // [B][4C] staged rows
-    float *red = xs + (size_t)MT * 4 * a.C;                // [16 warps][MT]
-    float *att_sm = red + MK_WARPS * MT;                   // 2 halves x 512 floats for attention
+    float *xs = (float *)mk_smem4;                  // [B][4C] staged rows
+    float *red = xs + (size_t)MT * 4 * a.C;         // [16 warps][32] partial sums
+    float *att_sm = red + MK_WARPS * 32;            // 4 attention groups
     __shared__ unsigned long long kmax[MT];
     const int C = a.C, B = a.B, L = a.L;
     const int pos = a.ctr[0], len = pos + 1;
     unsigned long long target = 0;
+    int phase = 0;
+    // phase trace (diagnostics): block 0 stamps the global timer after every barrier
+    auto stamp = [&]() {
+        if (a.trace && blockIdx.x == 0 && threadIdx.x == 0) a.trace[phase] = globaltimer_ns();
+        ++phase;
+    };
+    stamp();
     const long LF = 12L * C * C + 13L * C;
     const float *layer0 = a.params + (long)a.V * C + (long)a.block * C;
     auto P = [&](int l) { return layer0 + (long)l * LF; };
@@ -370,89 +397,95 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     auto proj2_w = [&](int l) { return fc_b(l) + 4L * C; };
     auto proj2_b = [&](int l) { return proj2_w(l) + 4L * C * C; };
     const float *lnf_w = layer0 + (long)L * LF, *lnf_b = lnf_w + C;
-    // rows per warp pass and float4 per lane per row in flight: RW * CH = 16
-    // loads per lane (8 at 8 sequences, where four rows share each staged x
-    // value and the registers go to the 32 partial sums)
-    constexpr int RW = MT == 8 ? 4 : 2, CH = MT == 8 ? 2 : 8;
+    // rows per pass: R * MT <= 32 partial sums per thread; K = C takes one
+    // 512-wide step of K per thread (C <= 2048), K = 4C four
+    constexpr int RC = MT == 1 ? 16 : (MT == 2 ? 16 : (MT == 4 ? 8 : 4));
+    constexpr int R4 = 4;
     // embedding of the incoming tokens at position pos (src/model.c:460-470)
     for (int i = blockIdx.x * MK_THREADS + threadIdx.x; i < B * C; i += gridDim.x * MK_THREADS) {
         const int m = i / C, c = i - m * C;
         a.x[i] = __ldg(a.wte + (long)a.next[m] * C + c) + __ldg(a.wpe + (long)pos * C + c);
     }
-    mk_prefetch<RW>(attn_w(0), 3 * C, C);
+    mk_prefetch<RC>(attn_w(0), 3 * C, C);
     if (!mk_barrier(a.bar, a.abort, target)) return;
+    stamp();
     for (int l = 0; l < L; ++l) {
+        float *kc_l = a.kc + (long)l * a.B * a.Tmax * C, *vc_l = a.vc + (long)l * a.B * a.Tmax * C;
         // P1: LN1, qkv (+ bias), K and V appended at pos
         mk_stage<MT>(xs, a.x, C, B, C, ln1_w(l), ln1_b(l), red);
         {
             const float *bias = attn_b(l);
-            float *kc_l = a.kc + (long)l * a.B * a.Tmax * C, *vc_l = a.vc + (long)l * a.B * a.Tmax * C;
-            mk_gemv<MT, RW, CH>(xs, B, C, attn_w(l), 3 * C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 1>(xs, B, C, attn_w(l), C, 3 * C, [&](int m, int n, float v) {
                 v += __ldg(bias + n);
                 a.qkv[(long)m * 3 * C + n] = v;
                 const long at = ((long)m * a.Tmax + pos) * C;
                 if (n >= 2 * C) vc_l[at + n - 2 * C] = v;
                 else if (n >= C) kc_l[at + n - C] = v;
-            });
+            }, red);
         }
-        mk_prefetch<RW>(proj1_w(l), C, C);
+        mk_prefetch<RC>(proj1_w(l), C, C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
-        // P2: attention over positions [0, pos]
+        stamp();
+        // P2: attention over positions [0, pos], four groups of 128 threads per block
         {
-            const float *kc_l = a.kc + (long)l * a.B * a.Tmax * C, *vc_l = a.vc + (long)l * a.B * a.Tmax * C;
-            const int nch = (len + MK_KEYS - 1) / MK_KEYS, items = B * a.H * nch, hf = threadIdx.x >> 8;
-            // each half of the block takes its own items (its barriers are its own)
-            for (int it = 2 * blockIdx.x + hf; it < items; it += 2 * gridDim.x) {
+            const int nch = (len + MK_KEYS - 1) / MK_KEYS, items = B * a.H * nch, g = threadIdx.x >> 7;
+            for (int it = 4 * blockIdx.x + g; it < items; it += 4 * gridDim.x) {
                 const int ch = it % nch, bh = it / nch;
-                mk_attention_item(a, kc_l, vc_l, bh / a.H, bh % a.H, ch, len, nch, att_sm + hf * 512, hf);
+                mk_attention_item(a, kc_l, vc_l, bh / a.H, bh % a.H, ch, len, nch, att_sm + g * MK_GROUP_FLOATS,
+                                  g);
             }
         }
-        mk_prefetch<RW>(fc_w(l), 4 * C, C);
+        mk_prefetch<RC>(fc_w(l), 4 * C, C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
+        stamp();
         // P3: c_proj, x += attn_proj + b
         mk_stage<MT>(xs, a.att, C, B, C, nullptr, nullptr, red);
         {
             const float *bias = proj1_b(l);
-            mk_gemv<MT, RW, CH>(xs, B, C, proj1_w(l), C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 1>(xs, B, C, proj1_w(l), C, C, [&](int m, int n, float v) {
                 a.x[(long)m * C + n] += v + __ldg(bias + n);
-            });
+            }, red);
         }
-        mk_prefetch<RW>(proj2_w(l), C, 4 * C);
+        mk_prefetch<R4>(proj2_w(l), C, 4 * C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
+        stamp();
         // P4: LN2, fc, GELU
         mk_stage<MT>(xs, a.x, C, B, C, ln2_w(l), ln2_b(l), red);
         {
             const float *bias = fc_b(l);
-            mk_gemv<MT, RW, CH>(xs, B, C, fc_w(l), 4 * C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 1>(xs, B, C, fc_w(l), C, 4 * C, [&](int m, int n, float v) {
                 a.hid[(long)m * 4 * C + n] = gelu_tanh(v + __ldg(bias + n), a.fast_act != 0);
-            });
+            }, red);
         }
-        if (l + 1 < L) mk_prefetch<RW>(attn_w(l + 1), 3 * C, C);
+        if (l + 1 < L) mk_prefetch<RC>(attn_w(l + 1), 3 * C, C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
+        stamp();
         // P5: proj, x += mlp_proj + b
         mk_stage<MT>(xs, a.hid, 4L * C, B, 4 * C, nullptr, nullptr, red);
         {
             const float *bias = proj2_b(l);
-            mk_gemv<MT, RW, CH>(xs, B, 4 * C, proj2_w(l), C, [&](int m, int n, float v) {
+            mk_gemv<MT, R4, 4>(xs, B, 4 * C, proj2_w(l), 4L * C, C, [&](int m, int n, float v) {
                 a.x[(long)m * C + n] += v + __ldg(bias + n);
-            });
+            }, red);
         }
-        if (l + 1 == L) mk_prefetch<RW>(a.wte, a.V, C);
+        if (l + 1 == L) mk_prefetch<RC>(a.wte, a.V, C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
+        stamp();
     }
     // P6: LN_f, LM head, greedy keys
     mk_stage<MT>(xs, a.x, C, B, C, lnf_w, lnf_b, red);
     if (threadIdx.x < MT) kmax[threadIdx.x] = 0ull;
     __syncthreads();
-    mk_gemv<MT, RW, CH>(xs, B, C, a.wte, a.V, [&](int m, int n, float v) {
+    mk_gemv<MT, RC, 1>(xs, B, C, a.wte, C, a.V, [&](int m, int n, float v) {
         a.logits[(long)m * a.ldlog + n] = v;
         const uint32_t u = __float_as_uint(v);
         const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
         atomicMax(&kmax[m], ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n));
-    });
+    }, red);
     __syncthreads();
     if (threadIdx.x < B && kmax[threadIdx.x]) atomicMax(a.am_key + threadIdx.x, kmax[threadIdx.x]);
     if (!mk_barrier(a.bar, a.abort, target)) return;
+    stamp();
     // P7: tokens (next input, step log), keys cleared, counters advanced
     if (blockIdx.x == 0) {
         const int t = threadIdx.x;
@@ -505,7 +538,7 @@ int launch_mk(const MkArgs &args, cudaStream_t s) {
 }  // namespace
 
 size_t mk_smem_bytes(int C, int MT) {
-    return ((size_t)MT * 4 * C + MK_WARPS * MT + 2 * 512) * sizeof(float);
+    return ((size_t)MT * 4 * C + MK_WARPS * 32 + 4 * MK_GROUP_FLOATS) * sizeof(float);
 }
 
 bool mk_decode_ok(int B, int C, int H, long Tmax) {
@@ -515,7 +548,7 @@ bool mk_decode_ok(int B, int C, int H, long Tmax) {
         off = (e && e[0] == '0') ? 1 : 0;
     }
     const int mt = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8;
-    return !off && B >= 1 && B <= 8 && H > 0 && C == 64 * H && C <= 2048 && Tmax > 0 &&
+    return !off && B >= 1 && B <= 8 && H > 0 && C == 64 * H && C <= 2048 && Tmax > 0 && Tmax <= 64 * MK_KEYS &&
            mk_smem_bytes(C, mt) + 1024 <= 227 * 1024;
 }
 

@@ -31,6 +31,9 @@ struct MkArgs {
     unsigned long long *bar = nullptr;     // 16 bytes: barrier counter and abort word, cleared per launch
     int *abort = nullptr;
     int fast_act = 0;
+    // diagnostics: when set, block 0 writes the global timer (ns) at the start
+    // and after every barrier: 2 + 5 L + 1 stamps
+    unsigned long long *trace = nullptr;
 };
 
 // whether the single-launch step handles this shape (CNGPT_CUDA_DECODE_STEP_KERNEL=0 turns it off)

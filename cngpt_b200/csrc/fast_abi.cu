@@ -186,6 +186,7 @@ int decode_step(const GPT *m, FastCtx *f, FastDev *d, int B, cudaStream_t s) {
         a.bar = d->mk_bar;
         a.abort = (int *)(d->mk_bar + 1);
         a.fast_act = 0;  // accurate tanh, as the GEMV decode path
+        a.trace = d->mk_trace;
         return decode_step_mk(a, s);
     }
     float *x = d->xl;
@@ -294,6 +295,7 @@ extern "C" void fast_free(FastCtx *f) {
         dev_free(d->ln_ticket);
         dev_free(d->am_key);
         dev_free(d->mk_bar);
+        dev_free(d->mk_trace);
         drop_graph(d);
         if (d->ev_a) cudaEventDestroy(d->ev_a);
         if (d->ev_b) cudaEventDestroy(d->ev_b);
@@ -326,6 +328,21 @@ extern "C" const float *gpt_forward_fast(GPT *m, FastCtx *f, const int *tokens, 
 
 namespace cg {
 namespace {
+// Phase stamps of the last single-launch decode step, summarised on stderr:
+// the embedding, each layer's five phases (mean over layers) and the LM head.
+void report_trace(const unsigned long long *dev, int L) {
+    std::vector<unsigned long long> t(5 * (size_t)L + 3);
+    if (cudaMemcpy(t.data(), dev, t.size() * sizeof(t[0]), cudaMemcpyDeviceToHost) != cudaSuccess) return;
+    double ph[5] = {0, 0, 0, 0, 0};
+    for (int l = 0; l < L; ++l)
+        for (int k = 0; k < 5; ++k) ph[k] += (double)(t[1 + 5 * l + k + 1] - t[1 + 5 * l + k]) / L;
+    fprintf(stderr,
+            "decode step trace: embed %.2f us; per layer ln1+qkv %.2f, attention %.2f, c_proj %.2f, ln2+fc %.2f, "
+            "proj %.2f us; ln_f+lm_head %.2f us; total %.1f us\n",
+            (t[1] - t[0]) * 1e-3, ph[0] * 1e-3, ph[1] * 1e-3, ph[2] * 1e-3, ph[3] * 1e-3, ph[4] * 1e-3,
+            (t[2 + 5 * L] - t[1 + 5 * L]) * 1e-3, (t[2 + 5 * L] - t[0]) * 1e-3);
+}
+
 // Decode state of a FastCtx for B sequences, a prompt of T tokens and n_new
 // generated tokens: the KV cache (capacity T + n_new positions), the decode
 // counters, the per-step token log and the statistics / argmax scratch.
@@ -345,6 +362,8 @@ int kv_prepare(const GPT *m, FastCtx *f, FastDev *d, int B, int T, int n_new, bo
         CG_CUDA(cudaMemsetAsync(d->am_key, 0, 8 * sizeof(unsigned long long), s));
         CG_TRY(dev_alloc((void **)&d->mk_bar, 2 * sizeof(unsigned long long), false));
         CG_CUDA(cudaMemsetAsync(d->mk_bar, 0, 2 * sizeof(unsigned long long), s));
+        if (getenv("CNGPT_CUDA_DECODE_TRACE"))
+            CG_TRY(dev_alloc((void **)&d->mk_trace, (5 * (size_t)L + 3) * sizeof(unsigned long long), false));
     }
     if (d->kv_B != B || d->kv_T < Tmax) {
         CG_CUDA(cudaStreamSynchronize(s));
@@ -417,6 +436,7 @@ extern "C" int cngpt_cuda_generate(GPT *m, FastCtx *f, const int *prompt, int B,
     CG_TRY(check_device_error());
     for (int b = 0; b < B; ++b)
         for (int i = 0; i < n_new; ++i) out_tokens[(size_t)b * n_new + i] = h[(size_t)i * B + b];
+    if (d->mk_trace && n_new > 1) report_trace(d->mk_trace, m->cfg.n_layer);
     return OK;
 }
 

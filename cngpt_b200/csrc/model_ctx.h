@@ -60,6 +60,7 @@ struct FastDev {
     int *ln_ticket = nullptr;   // [4] last-block tickets of the statistics GEMVs ([0..1] used)
     unsigned long long *am_key = nullptr;  // [8] greedy argmax keys of the LM-head GEMV
     unsigned long long *mk_bar = nullptr;  // grid-barrier counter + abort word of the single-launch step
+    unsigned long long *mk_trace = nullptr;  // phase stamps of the last step (CNGPT_CUDA_DECODE_TRACE=1)
     // one decode step captured as a CUDA graph, reused while the key matches
     cudaStream_t cap_stream = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
