@@ -56,8 +56,9 @@ __device__ __forceinline__ bool mk_barrier(unsigned long long *bar, int *abort, 
     target += gridDim.x;
     if (threadIdx.x == 0) {
         ok = 1;
-        __threadfence();
-        atomicAdd(bar, 1ull);
+        // arrive: a release reduction at GPU scope (cumulative over the
+        // block's writes ordered before it by the CTA barrier), no return value
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
         const uint64_t t0 = globaltimer_ns();
         const uint64_t limit = *(volatile unsigned long long *)&g_cngpt_wait_limit_ns;
         for (unsigned it = 0;; ++it) {
@@ -77,7 +78,6 @@ __device__ __forceinline__ bool mk_barrier(unsigned long long *bar, int *abort, 
                 }
             }
         }
-        __threadfence();
     }
     __syncthreads();
     return ok != 0;
@@ -156,10 +156,9 @@ __device__ void mk_stage(float *xs, const float *src, long lds, int B, int K, co
 
 // ------------------------------------------------------------ block GEMV
 // Rows of W [N, K] (row pitch ldw) owned by this block: [lo, hi), R at a time.
-// All 512 threads split K in float4 units (KI steps of 512 at most), so each
-// thread has R * KI 16-byte loads of W in flight before it multiplies; the
-// R * MT partial sums are reduced across each warp by recursive halving and
-// across the 16 warps through shared memory in warp order (fixed order), and
+// Each thread has R * KI 16-byte loads of W in flight before it multiplies;
+// the R * MT partial sums are reduced across each warp by recursive halving
+// and across the warps through shared memory in warp order (fixed order), and
 // the epilogue gets (sequence m, row n, total).
 template <int NV>
 __device__ __forceinline__ void halve(float *a, int lane, int o, int &idx) {
@@ -194,20 +193,29 @@ __device__ __forceinline__ void mk_rows(int N, int &lo, int &hi) {
     hi = min(N, lo + per);
 }
 
+__device__ __forceinline__ void team_sync(int team) {
+    asm volatile("bar.sync %0, %1;" ::"r"(5 + team), "r"(256) : "memory");
+}
+
+// The block's two teams of 256 threads take alternate R-row groups, so one
+// team's loads are in flight while the other reduces; within a team the
+// threads split K (KI steps of 256 float4 at most) and reduce through the
+// team's own shared partials (red + 256 * team) in warp order.
 template <int MT, int R, int KI, class Epi>
 __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__ W, long ldw, int N, Epi epi,
                         float *red) {
-    constexpr int NV = R * MT;
+    constexpr int NV = R * MT, TT = 256;
     static_assert(NV <= 32, "partial sums per thread");
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, K4 = K >> 2;
+    const int team = threadIdx.x >> 8, t = threadIdx.x & (TT - 1), lane = t & 31, warp = t >> 5, K4 = K >> 2;
+    float *tred = red + team * 256;
     const float4 *x4 = (const float4 *)xs;
     int lo, hi;
     mk_rows<R>(N, lo, hi);
-    for (int n0 = lo; n0 < hi; n0 += R) {
+    for (int n0 = lo + team * R; n0 < hi; n0 += 2 * R) {
         float4 wv[KI][R];
 #pragma unroll
         for (int i = 0; i < KI; ++i) {
-            const int k = t + i * MK_THREADS;
+            const int k = t + i * TT;
 #pragma unroll
             for (int r = 0; r < R; ++r)
                 wv[i][r] = k < K4 ? __ldcs((const float4 *)(W + (long)min(n0 + r, N - 1) * ldw) + k)
@@ -218,7 +226,7 @@ __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__
         for (int j = 0; j < NV; ++j) acc[j] = 0.f;
 #pragma unroll
         for (int i = 0; i < KI; ++i) {
-            const int k = t + i * MK_THREADS;
+            const int k = t + i * TT;
             if (k < K4) {
 #pragma unroll
                 for (int m = 0; m < MT; ++m) {
@@ -233,16 +241,16 @@ __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__
             }
         }
         const int idx = warp_reduce_vec<NV>(acc, lane);
-        if (idx >= 0) red[warp * 32 + idx] = acc[0];
-        __syncthreads();
+        if (idx >= 0) tred[warp * 32 + idx] = acc[0];
+        team_sync(team);
         if (t < NV) {
             float v = 0.f;
 #pragma unroll
-            for (int w = 0; w < MK_WARPS; ++w) v += red[w * 32 + t];
+            for (int w = 0; w < TT / 32; ++w) v += tred[w * 32 + t];
             const int r = t / MT, m = t - r * MT, n = n0 + r;
             if (m < B && n < hi) epi(m, n, v);
         }
-        __syncthreads();
+        team_sync(team);
     }
 }
 
@@ -350,6 +358,7 @@ __device__ void mk_attention_item(const MkArgs &a, const float *kc_l, const floa
             float M = -INFINITY;
             for (int k = 0; k < nch; ++k) M = fmaxf(M, cm[k]);
             float L = 0.f, O = 0.f;
+#pragma unroll 4
             for (int k = 0; k < nch; ++k) {
                 const float w = expf(cm[k] - M);
                 L += cl[k] * w;
@@ -397,10 +406,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     auto proj2_w = [&](int l) { return fc_b(l) + 4L * C; };
     auto proj2_b = [&](int l) { return proj2_w(l) + 4L * C * C; };
     const float *lnf_w = layer0 + (long)L * LF, *lnf_b = lnf_w + C;
-    // rows per pass: R * MT <= 32 partial sums per thread; K = C takes one
-    // 512-wide step of K per thread (C <= 2048), K = 4C four
-    constexpr int RC = MT == 1 ? 16 : (MT == 2 ? 16 : (MT == 4 ? 8 : 4));
-    constexpr int R4 = 4;
+    // rows per pass: R * MT <= 32 partial sums per thread and 16 loads of W in
+    // flight; K = C takes two 256-wide steps of K per thread (C <= 2048), K =
+    // 4C eight
+    constexpr int RC = MT <= 4 ? 8 : 4, R4 = 2;
     // embedding of the incoming tokens at position pos (src/model.c:460-470)
     for (int i = blockIdx.x * MK_THREADS + threadIdx.x; i < B * C; i += gridDim.x * MK_THREADS) {
         const int m = i / C, c = i - m * C;
@@ -415,7 +424,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         mk_stage<MT>(xs, a.x, C, B, C, ln1_w(l), ln1_b(l), red);
         {
             const float *bias = attn_b(l);
-            mk_gemv<MT, RC, 1>(xs, B, C, attn_w(l), C, 3 * C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 2>(xs, B, C, attn_w(l), C, 3 * C, [&](int m, int n, float v) {
                 v += __ldg(bias + n);
                 a.qkv[(long)m * 3 * C + n] = v;
                 const long at = ((long)m * a.Tmax + pos) * C;
@@ -442,7 +451,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         mk_stage<MT>(xs, a.att, C, B, C, nullptr, nullptr, red);
         {
             const float *bias = proj1_b(l);
-            mk_gemv<MT, RC, 1>(xs, B, C, proj1_w(l), C, C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 2>(xs, B, C, proj1_w(l), C, C, [&](int m, int n, float v) {
                 a.x[(long)m * C + n] += v + __ldg(bias + n);
             }, red);
         }
@@ -453,7 +462,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         mk_stage<MT>(xs, a.x, C, B, C, ln2_w(l), ln2_b(l), red);
         {
             const float *bias = fc_b(l);
-            mk_gemv<MT, RC, 1>(xs, B, C, fc_w(l), C, 4 * C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 2>(xs, B, C, fc_w(l), C, 4 * C, [&](int m, int n, float v) {
                 a.hid[(long)m * 4 * C + n] = gelu_tanh(v + __ldg(bias + n), a.fast_act != 0);
             }, red);
         }
@@ -464,7 +473,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         mk_stage<MT>(xs, a.hid, 4L * C, B, 4 * C, nullptr, nullptr, red);
         {
             const float *bias = proj2_b(l);
-            mk_gemv<MT, R4, 4>(xs, B, 4 * C, proj2_w(l), 4L * C, C, [&](int m, int n, float v) {
+            mk_gemv<MT, R4, 8>(xs, B, 4 * C, proj2_w(l), 4L * C, C, [&](int m, int n, float v) {
                 a.x[(long)m * C + n] += v + __ldg(bias + n);
             }, red);
         }
@@ -476,7 +485,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     mk_stage<MT>(xs, a.x, C, B, C, lnf_w, lnf_b, red);
     if (threadIdx.x < MT) kmax[threadIdx.x] = 0ull;
     __syncthreads();
-    mk_gemv<MT, RC, 1>(xs, B, C, a.wte, C, a.V, [&](int m, int n, float v) {
+    mk_gemv<MT, RC, 2>(xs, B, C, a.wte, C, a.V, [&](int m, int n, float v) {
         a.logits[(long)m * a.ldlog + n] = v;
         const uint32_t u = __float_as_uint(v);
         const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
