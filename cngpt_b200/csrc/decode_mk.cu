@@ -154,6 +154,11 @@ __device__ void mk_stage(float *xs, const float *src, long lds, int B, int K, co
     __syncthreads();
 }
 
+// named barrier of the 128-thread group g of a block (ids 1..4)
+__device__ __forceinline__ void group_sync(int g) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(128) : "memory");
+}
+
 // ------------------------------------------------------------ block GEMV
 // Rows of W [N, K] (row pitch ldw) owned by this block: [lo, hi), R at a time.
 // Each thread has R * KI 16-byte loads of W in flight before it multiplies;
@@ -193,25 +198,22 @@ __device__ __forceinline__ void mk_rows(int N, int &lo, int &hi) {
     hi = min(N, lo + per);
 }
 
-__device__ __forceinline__ void team_sync(int team) {
-    asm volatile("bar.sync %0, %1;" ::"r"(5 + team), "r"(256) : "memory");
-}
-
-// The block's two teams of 256 threads take alternate R-row groups, so one
-// team's loads are in flight while the other reduces; within a team the
-// threads split K (KI steps of 256 float4 at most) and reduce through the
-// team's own shared partials (red + 256 * team) in warp order.
+// The block's four teams of 128 threads take R-row groups in turn, so three
+// teams' loads are in flight while one reduces; within a team the threads
+// split K (KI steps of 128 float4 at most) and reduce through the team's own
+// shared partials (red + 128 * team) in warp order. A team is the same
+// thread range as an attention group and uses the same named barrier.
 template <int MT, int R, int KI, class Epi>
 __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__ W, long ldw, int N, Epi epi,
                         float *red) {
-    constexpr int NV = R * MT, TT = 256;
+    constexpr int NV = R * MT, TT = 128;
     static_assert(NV <= 32, "partial sums per thread");
-    const int team = threadIdx.x >> 8, t = threadIdx.x & (TT - 1), lane = t & 31, warp = t >> 5, K4 = K >> 2;
-    float *tred = red + team * 256;
+    const int team = threadIdx.x >> 7, t = threadIdx.x & (TT - 1), lane = t & 31, warp = t >> 5, K4 = K >> 2;
+    float *tred = red + team * TT;
     const float4 *x4 = (const float4 *)xs;
     int lo, hi;
     mk_rows<R>(N, lo, hi);
-    for (int n0 = lo + team * R; n0 < hi; n0 += 2 * R) {
+    for (int n0 = lo + team * R; n0 < hi; n0 += 4 * R) {
         float4 wv[KI][R];
 #pragma unroll
         for (int i = 0; i < KI; ++i) {
@@ -242,7 +244,7 @@ __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__
         }
         const int idx = warp_reduce_vec<NV>(acc, lane);
         if (idx >= 0) tred[warp * 32 + idx] = acc[0];
-        team_sync(team);
+        group_sync(team);
         if (t < NV) {
             float v = 0.f;
 #pragma unroll
@@ -250,7 +252,7 @@ __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__
             const int r = t / MT, m = t - r * MT, n = n0 + r;
             if (m < B && n < hi) epi(m, n, v);
         }
-        team_sync(team);
+        group_sync(team);
     }
 }
 
@@ -274,9 +276,6 @@ __device__ __forceinline__ void mk_prefetch(const float *W, int N, int K) {
 // terms, P V (two key halves per dimension), and the chunk's (max, sum,
 // outputs) to `part`; the last chunk of (b, h) to finish (integer ticket)
 // merges every chunk in chunk order into att.
-__device__ __forceinline__ void group_sync(int g) {
-    asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(128) : "memory");
-}
 
 constexpr int MK_GROUP_FLOATS = 64 * 5 + 4;
 
@@ -406,10 +405,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     auto proj2_w = [&](int l) { return fc_b(l) + 4L * C; };
     auto proj2_b = [&](int l) { return proj2_w(l) + 4L * C * C; };
     const float *lnf_w = layer0 + (long)L * LF, *lnf_b = lnf_w + C;
-    // rows per pass: R * MT <= 32 partial sums per thread and 16 loads of W in
-    // flight; K = C takes two 256-wide steps of K per thread (C <= 2048), K =
-    // 4C eight
-    constexpr int RC = MT <= 4 ? 8 : 4, R4 = 2;
+    // rows per pass: R * MT <= 32 partial sums per thread, at most 16 loads of
+    // W in flight per thread; K = C takes four 128-wide steps of K per thread
+    // (C <= 2048), K = 4C sixteen
+    constexpr int RC = 4, R4 = 1;
     // embedding of the incoming tokens at position pos (src/model.c:460-470)
     for (int i = blockIdx.x * MK_THREADS + threadIdx.x; i < B * C; i += gridDim.x * MK_THREADS) {
         const int m = i / C, c = i - m * C;
@@ -424,7 +423,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         mk_stage<MT>(xs, a.x, C, B, C, ln1_w(l), ln1_b(l), red);
         {
             const float *bias = attn_b(l);
-            mk_gemv<MT, RC, 2>(xs, B, C, attn_w(l), C, 3 * C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 4>(xs, B, C, attn_w(l), C, 3 * C, [&](int m, int n, float v) {
                 v += __ldg(bias + n);
                 a.qkv[(long)m * 3 * C + n] = v;
                 const long at = ((long)m * a.Tmax + pos) * C;
@@ -451,7 +450,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         mk_stage<MT>(xs, a.att, C, B, C, nullptr, nullptr, red);
         {
             const float *bias = proj1_b(l);
-            mk_gemv<MT, RC, 2>(xs, B, C, proj1_w(l), C, C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 4>(xs, B, C, proj1_w(l), C, C, [&](int m, int n, float v) {
                 a.x[(long)m * C + n] += v + __ldg(bias + n);
             }, red);
         }
@@ -462,7 +461,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         mk_stage<MT>(xs, a.x, C, B, C, ln2_w(l), ln2_b(l), red);
         {
             const float *bias = fc_b(l);
-            mk_gemv<MT, RC, 2>(xs, B, C, fc_w(l), C, 4 * C, [&](int m, int n, float v) {
+            mk_gemv<MT, RC, 4>(xs, B, C, fc_w(l), C, 4 * C, [&](int m, int n, float v) {
                 a.hid[(long)m * 4 * C + n] = gelu_tanh(v + __ldg(bias + n), a.fast_act != 0);
             }, red);
         }
@@ -473,7 +472,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         mk_stage<MT>(xs, a.hid, 4L * C, B, 4 * C, nullptr, nullptr, red);
         {
             const float *bias = proj2_b(l);
-            mk_gemv<MT, R4, 8>(xs, B, 4 * C, proj2_w(l), 4L * C, C, [&](int m, int n, float v) {
+            mk_gemv<MT, R4, 16>(xs, B, 4 * C, proj2_w(l), 4L * C, C, [&](int m, int n, float v) {
                 a.x[(long)m * C + n] += v + __ldg(bias + n);
             }, red);
         }
@@ -485,7 +484,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     mk_stage<MT>(xs, a.x, C, B, C, lnf_w, lnf_b, red);
     if (threadIdx.x < MT) kmax[threadIdx.x] = 0ull;
     __syncthreads();
-    mk_gemv<MT, RC, 2>(xs, B, C, a.wte, C, a.V, [&](int m, int n, float v) {
+    mk_gemv<MT, RC, 4>(xs, B, C, a.wte, C, a.V, [&](int m, int n, float v) {
         a.logits[(long)m * a.ldlog + n] = v;
         const uint32_t u = __float_as_uint(v);
         const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
