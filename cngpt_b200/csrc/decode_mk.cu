@@ -203,9 +203,33 @@ __device__ __forceinline__ void mk_rows(int N, int &lo, int &hi) {
 // split K (KI steps of 128 float4 at most) and reduce through the team's own
 // shared partials (red + 128 * team) in warp order. A team is the same
 // thread range as an attention group and uses the same named barrier.
+//
+// A team's first group of W does not depend on the previous phase, so it is
+// loaded (WTile::load) before the grid barrier that ends that phase: the
+// barrier's wait overlaps the first HBM round trip of the next product.
+template <int R, int KI>
+struct WTile {
+    float4 v[KI][R];
+    __device__ __forceinline__ void load(const float *__restrict__ W, long ldw, int N, int K) {
+        constexpr int TT = 128;
+        const int t = threadIdx.x & (TT - 1), K4 = K >> 2;
+        int lo, hi;
+        mk_rows<R>(N, lo, hi);
+        const int n0 = lo + (int)(threadIdx.x >> 7) * R;
+#pragma unroll
+        for (int i = 0; i < KI; ++i) {
+            const int k = t + i * TT;
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                v[i][r] = (k < K4 && n0 < hi) ? __ldcs((const float4 *)(W + (long)min(n0 + r, N - 1) * ldw) + k)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+};
+
 template <int MT, int R, int KI, class Epi>
 __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__ W, long ldw, int N, Epi epi,
-                        float *red) {
+                        float *red, WTile<R, KI> &wv) {
     constexpr int NV = R * MT, TT = 128;
     static_assert(NV <= 32, "partial sums per thread");
     const int team = threadIdx.x >> 7, t = threadIdx.x & (TT - 1), lane = t & 31, warp = t >> 5, K4 = K >> 2;
@@ -214,14 +238,15 @@ __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__
     int lo, hi;
     mk_rows<R>(N, lo, hi);
     for (int n0 = lo + team * R; n0 < hi; n0 += 4 * R) {
-        float4 wv[KI][R];
+        if (n0 != lo + team * R) {  // the first group was loaded before the barrier
 #pragma unroll
-        for (int i = 0; i < KI; ++i) {
-            const int k = t + i * TT;
+            for (int i = 0; i < KI; ++i) {
+                const int k = t + i * TT;
 #pragma unroll
-            for (int r = 0; r < R; ++r)
-                wv[i][r] = k < K4 ? __ldcs((const float4 *)(W + (long)min(n0 + r, N - 1) * ldw) + k)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int r = 0; r < R; ++r)
+                    wv.v[i][r] = k < K4 ? __ldcs((const float4 *)(W + (long)min(n0 + r, N - 1) * ldw) + k)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
         float acc[NV];
 #pragma unroll
@@ -236,8 +261,8 @@ __device__ void mk_gemv(const float *xs, int B, int K, const float *__restrict__
                         const float4 xv = x4[m * K4 + k];
 #pragma unroll
                         for (int r = 0; r < R; ++r)
-                            acc[r * MT + m] += wv[i][r].x * xv.x + wv[i][r].y * xv.y + wv[i][r].z * xv.z +
-                                               wv[i][r].w * xv.w;
+                            acc[r * MT + m] += wv.v[i][r].x * xv.x + wv.v[i][r].y * xv.y + wv.v[i][r].z * xv.z +
+                                               wv.v[i][r].w * xv.w;
                     }
                 }
             }
@@ -408,13 +433,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     // rows per pass: R * MT <= 32 partial sums per thread, at most 16 loads of
     // W in flight per thread; K = C takes four 128-wide steps of K per thread
     // (C <= 2048), K = 4C sixteen
-    constexpr int RC = 4, R4 = 1;
+    constexpr int RC = MT <= 2 ? 4 : 2, R4 = 1;
     // embedding of the incoming tokens at position pos (src/model.c:460-470)
     for (int i = blockIdx.x * MK_THREADS + threadIdx.x; i < B * C; i += gridDim.x * MK_THREADS) {
         const int m = i / C, c = i - m * C;
         a.x[i] = __ldg(a.wte + (long)a.next[m] * C + c) + __ldg(a.wpe + (long)pos * C + c);
     }
+    WTile<RC, 4> wc;   // first group of a K = C product, loaded before the barrier
+    WTile<R4, 16> w4;  // first group of the K = 4C product
     mk_prefetch<RC>(attn_w(0), 3 * C, C);
+    wc.load(attn_w(0), C, 3 * C, C);
     if (!mk_barrier(a.bar, a.abort, target)) return;
     stamp();
     for (int l = 0; l < L; ++l) {
@@ -429,7 +457,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
                 const long at = ((long)m * a.Tmax + pos) * C;
                 if (n >= 2 * C) vc_l[at + n - 2 * C] = v;
                 else if (n >= C) kc_l[at + n - C] = v;
-            }, red);
+            }, red, wc);
         }
         mk_prefetch<RC>(proj1_w(l), C, C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
@@ -444,6 +472,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
             }
         }
         mk_prefetch<RC>(fc_w(l), 4 * C, C);
+        wc.load(proj1_w(l), C, C, C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
         stamp();
         // P3: c_proj, x += attn_proj + b
@@ -452,9 +481,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
             const float *bias = proj1_b(l);
             mk_gemv<MT, RC, 4>(xs, B, C, proj1_w(l), C, C, [&](int m, int n, float v) {
                 a.x[(long)m * C + n] += v + __ldg(bias + n);
-            }, red);
+            }, red, wc);
         }
         mk_prefetch<R4>(proj2_w(l), C, 4 * C);
+        wc.load(fc_w(l), C, 4 * C, C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
         stamp();
         // P4: LN2, fc, GELU
@@ -463,9 +493,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
             const float *bias = fc_b(l);
             mk_gemv<MT, RC, 4>(xs, B, C, fc_w(l), C, 4 * C, [&](int m, int n, float v) {
                 a.hid[(long)m * 4 * C + n] = gelu_tanh(v + __ldg(bias + n), a.fast_act != 0);
-            }, red);
+            }, red, wc);
         }
         if (l + 1 < L) mk_prefetch<RC>(attn_w(l + 1), 3 * C, C);
+        w4.load(proj2_w(l), 4L * C, C, 4 * C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
         stamp();
         // P5: proj, x += mlp_proj + b
@@ -474,9 +505,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
             const float *bias = proj2_b(l);
             mk_gemv<MT, R4, 16>(xs, B, 4 * C, proj2_w(l), 4L * C, C, [&](int m, int n, float v) {
                 a.x[(long)m * C + n] += v + __ldg(bias + n);
-            }, red);
+            }, red, w4);
         }
         if (l + 1 == L) mk_prefetch<RC>(a.wte, a.V, C);
+        if (l + 1 < L) wc.load(attn_w(l + 1), C, 3 * C, C);
+        else wc.load(a.wte, C, a.V, C);
         if (!mk_barrier(a.bar, a.abort, target)) return;
         stamp();
     }
@@ -489,7 +522,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         const uint32_t u = __float_as_uint(v);
         const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
         atomicMax(&kmax[m], ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n));
-    }, red);
+    }, red, wc);
     __syncthreads();
     if (threadIdx.x < B && kmax[threadIdx.x]) atomicMax(a.am_key + threadIdx.x, kmax[threadIdx.x]);
     if (!mk_barrier(a.bar, a.abort, target)) return;
