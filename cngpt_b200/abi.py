@@ -120,6 +120,7 @@ EXT_SIGNATURES = {
     "cngpt_cuda_set_managed": (I, [I]),
     "cngpt_cuda_launch_count": (C.c_ulonglong, []),
     "cngpt_cuda_set_wait_limit_ns": (I, [C.c_ulonglong]),
+    "cngpt_cuda_set_decode_step_kernel": (I, [I]),
     "cngpt_cuda_gemm": (I, [VP, L, I, VP, L, I, I, I, I, I, F, VP, L, VP, VP, L, VP, L, VP, L]),
     "cngpt_cuda_attention_fwd": (I, [VP, VP, VP, I, I, I, I]),
     "cngpt_cuda_attention_bwd": (I, [VP, VP, VP, VP, VP, I, I, I, I]),

@@ -582,15 +582,26 @@ size_t mk_smem_bytes(int C, int MT) {
     return ((size_t)MT * 4 * C + MK_WARPS * 32 + 4 * MK_GROUP_FLOATS) * sizeof(float);
 }
 
-bool mk_decode_ok(int B, int C, int H, long Tmax) {
-    static int off = -1;
-    if (off < 0) {
+namespace {
+// off unless CNGPT_CUDA_DECODE_STEP_KERNEL=1 or cngpt_cuda_set_decode_step_kernel(1): measured on
+// B200 it does not beat the kernel chain yet (grid barriers and latency-bound phases)
+int g_mk_on = -1;
+}  // namespace
+
+void set_decode_step_kernel(bool on) { g_mk_on = on ? 1 : 0; }
+
+bool decode_step_kernel_on() {
+    if (g_mk_on < 0) {
         const char *e = getenv("CNGPT_CUDA_DECODE_STEP_KERNEL");
-        off = (e && e[0] == '0') ? 1 : 0;
+        g_mk_on = (e && e[0] == '1') ? 1 : 0;
     }
+    return g_mk_on == 1;
+}
+
+bool mk_decode_ok(int B, int C, int H, long Tmax) {
     const int mt = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8;
-    return !off && B >= 1 && B <= 8 && H > 0 && C == 64 * H && C <= 2048 && Tmax > 0 && Tmax <= 64 * MK_KEYS &&
-           mk_smem_bytes(C, mt) + 1024 <= 227 * 1024;
+    return decode_step_kernel_on() && B >= 1 && B <= 8 && H > 0 && C == 64 * H && C <= 2048 && Tmax > 0 &&
+           Tmax <= 64 * MK_KEYS && mk_smem_bytes(C, mt) + 1024 <= 227 * 1024;
 }
 
 size_t mk_part_floats(int B, int H, long Tmax) {

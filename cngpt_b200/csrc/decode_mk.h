@@ -36,8 +36,10 @@ struct MkArgs {
     unsigned long long *trace = nullptr;
 };
 
-// whether the single-launch step handles this shape (CNGPT_CUDA_DECODE_STEP_KERNEL=0 turns it off)
+// whether the single-launch step is enabled and handles this shape
 bool mk_decode_ok(int B, int C, int H, long Tmax);
+void set_decode_step_kernel(bool on);
+bool decode_step_kernel_on();
 size_t mk_smem_bytes(int C, int MT);
 // attention partial floats for B sequences, H heads, Tmax positions (the ticket
 // ints follow them in the same buffer)

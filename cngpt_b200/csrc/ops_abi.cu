@@ -12,6 +12,7 @@
 
 #include "abi_common.h"
 #include "common.cuh"
+#include "decode_mk.h"
 #include "kernels.h"
 
 extern "C" {
@@ -405,6 +406,11 @@ extern "C" int cngpt_cuda_set_managed(int on) {
 }
 
 extern "C" unsigned long long cngpt_cuda_launch_count(void) { return g_launch_count; }
+
+extern "C" int cngpt_cuda_set_decode_step_kernel(int on) {
+    set_decode_step_kernel(on != 0);
+    return OK;
+}
 
 extern "C" int cngpt_cuda_set_wait_limit_ns(unsigned long long ns) {
     // the device variables are read by kernels in flight: finish them first

@@ -114,6 +114,13 @@ int cngpt_cuda_train_step(GPT *m, const int *tokens, const int *targets, int B, 
                           float grad_clip, float *loss_out);
 int cngpt_cuda_last_loss(GPT *m, float *loss_out);
 
+/* Decode steps of up to 8 sequences (head size 64) as one cooperative launch
+ * per token - every layer, the LM head and the greedy pick, phases separated
+ * by bounded grid barriers - instead of a chain of five kernels per layer.
+ * Off by default (also CNGPT_CUDA_DECODE_STEP_KERNEL=1): on B200 it does not
+ * yet beat the kernel chain. Same tokens either way up to fp32 rounding. */
+int cngpt_cuda_set_decode_step_kernel(int on);
+
 /* ---- training batches, uploaded one step ahead -----------------------------
  * The reference's DataLoader (src/dataloader.c:62-82) fills host int arrays
  * inputs[b*T+t] = data[pos + b*T + t], targets[b*T+t] = data[pos + b*T + t + 1]

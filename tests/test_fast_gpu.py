@@ -162,21 +162,34 @@ def test_sample_kv_cache_matches_reference_stream(lib, cuda, temp, k):
 
 
 @pytest.mark.parametrize("name,B", [("hs64", 1), ("hs64", 3), ("small1", 8)])
-def test_decode_step_is_one_launch(lib, cuda, name, B):
-    """Sequences up to 8 with head size 64 decode each token in one
-    cooperative launch (all layers, the LM head and the greedy pick)."""
+def test_decode_step_kernel(lib, cuda, name, B):
+    """With the single-launch decode step enabled, sequences up to 8 with head
+    size 64 decode each token in one cooperative launch (all layers, the LM
+    head and the greedy pick), and a 16-token greedy window gives the same
+    tokens as the kernel-chain decode."""
     ref, dev, c = pair(lib, name)
     ref.free()
     prompt = oracle.lcg_tokens(B * 8, c["V"], seed=2)
-    out = np.zeros(B * 2, np.int32)
     fc = abi.FastCtx()
     lib.fast_init(C.byref(fc))
-    counts = []
-    for n in (1, 2):
-        l0 = lib.cngpt_cuda_launch_count()
-        abi.check(lib, lib.cngpt_cuda_generate(C.byref(dev.m), C.byref(fc), prompt.ctypes.data, B, 8, n,
-                                               out.ctypes.data), "generate")
-        counts.append(lib.cngpt_cuda_launch_count() - l0)
+    toks = {}
+    try:
+        for on in (1, 0):
+            lib.cngpt_cuda_set_decode_step_kernel(on)
+            counts = []
+            for n in (1, 2, 16):
+                out = np.zeros(B * n, np.int32)
+                l0 = lib.cngpt_cuda_launch_count()
+                abi.check(lib, lib.cngpt_cuda_generate(C.byref(dev.m), C.byref(fc), prompt.ctypes.data, B, 8, n,
+                                                       out.ctypes.data), "generate")
+                counts.append(lib.cngpt_cuda_launch_count() - l0)
+            toks[on] = out.copy()
+            if on:
+                assert counts[1] - counts[0] == 1, counts  # n = 2 adds one eager decode step
+            else:
+                assert counts[1] - counts[0] > 1, counts  # the kernel chain
+    finally:
+        lib.cngpt_cuda_set_decode_step_kernel(0)
     lib.fast_free(C.byref(fc))
     dev.free()
-    assert counts[1] - counts[0] == 1, counts  # n = 2 adds one eager decode step
+    assert np.array_equal(toks[1], toks[0])
