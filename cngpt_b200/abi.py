@@ -142,6 +142,7 @@ EXT_SIGNATURES = {
     "cngpt_cuda_tp_forward_last": (I, [C.POINTER(GPT), VP, I, I, VP]),
     "cngpt_cuda_tp_generate": (I, [C.POINTER(GPT), VP, I, I, I, VP]),
     "cngpt_cuda_tp_free": (I, [C.POINTER(GPT)]),
+    "cngpt_cuda_tp_set_decode_mode": (I, [C.POINTER(GPT), I]),
     "cngpt_cuda_selftest_tp_reduce": (I, [VP, VP, I, I, I, VP]),
     "cngpt_cuda_loader_create": (I, [C.POINTER(VP), VP, C.c_size_t, I, I]),
     "cngpt_cuda_loader_next": (I, [VP, C.POINTER(VP), C.POINTER(VP)]),

@@ -110,6 +110,10 @@ struct TpState {
     float *d_stats = nullptr;  // [8][2] LayerNorm statistics of x after each exchange
     unsigned long long *am_key = nullptr;  // [8] greedy keys of the LM-head GEMV
     unsigned long long *mk_bar = nullptr;  // grid barrier of the single-launch decode step (world 1)
+    // greedy decode split over the ranks (1), replicated on every rank (2), or
+    // by batch size (0: replicated at batch 1, split above)
+    int decode_mode = 0;
+    FastCtx fctx{};  // the replicated decode's one-GPU state
 
     const float *qkv_w(int l) const { return wbuf + (size_t)l * 3 * Cl * C; }
     const float *qkv_b(int l) const { return wbuf + (size_t)L * 3 * Cl * C + (size_t)l * 3 * Cl; }
@@ -534,6 +538,7 @@ void release(TpState *t) {
     if (t->ev_a) cudaEventDestroy(t->ev_a);
     if (t->ev_b) cudaEventDestroy(t->ev_b);
     if (t->cap_stream) cudaStreamDestroy(t->cap_stream);
+    fast_free(&t->fctx);
     nccl_comm_destroy(t->comm);
     delete t;
 }
@@ -638,6 +643,7 @@ extern "C" int cngpt_cuda_tp_init(GPT *m, const unsigned char id[128], int world
     const GPTConfig &cfg = m->cfg;
     CG_TRY(make_plan(cfg.n_head, cfg.n_embd, cfg.vocab_size, world, rank, &p));
     TpState *t = new TpState;
+    fast_init(&t->fctx);
     t->world = world;
     t->rank = rank;
     t->p = p;
@@ -737,6 +743,17 @@ extern "C" int cngpt_cuda_tp_forward_last(GPT *m, const int *tokens, int B, int 
     return OK;
 }
 
+extern "C" int cngpt_cuda_tp_set_decode_mode(GPT *m, int mode) {
+    TpState *t = tp_state(m);
+    if (!t) return ERR_STATE;
+    if (mode < 0 || mode > 2) {
+        set_last_error(ERR_ARG, "tp_set_decode_mode: mode %d (0 auto, 1 split, 2 replicated)", mode);
+        return ERR_ARG;
+    }
+    t->decode_mode = mode;
+    return OK;
+}
+
 extern "C" int cngpt_cuda_tp_generate(GPT *m, const int *prompt, int B, int T, int n_new, int *out_tokens) {
     TpState *t = tp_state(m);
     if (!t) return ERR_STATE;
@@ -745,6 +762,15 @@ extern "C" int cngpt_cuda_tp_generate(GPT *m, const int *prompt, int B, int T, i
                        m->cfg.block_size);
         return ERR_ARG;
     }
+    // At batch 1 a split step is bound by its two exchanges per layer (a few
+    // microseconds each over NVLink, 96 per GPT-2 XL token) rather than by its
+    // weight stream, which it divides by the world size: measured on B200, a
+    // split step at batch 1 is slower than one GPU at every world size, and
+    // faster at batch 8. Every rank holds the whole model, so at batch 1 each
+    // rank runs the one-GPU decode itself, bit-identically (same weights, same
+    // deterministic kernels), and no exchange is needed.
+    const bool replicate = t->world > 1 && (t->decode_mode == 2 || (t->decode_mode == 0 && B == 1));
+    if (replicate) return cngpt_cuda_generate(m, &t->fctx, prompt, B, T, n_new, out_tokens);
     cudaStream_t s = g_stream;
     CG_TRY(resize(t, B, T));
     const int Tmax = T + n_new;

@@ -205,6 +205,12 @@ int cngpt_cuda_tp_init(GPT *m, const unsigned char id[128], int world, int rank)
 int cngpt_cuda_tp_forward_last(GPT *m, const int *tokens, int B, int T, float *logits_out);
 /* cngpt_cuda_generate split over the ranks; out_tokens (host) on every rank */
 int cngpt_cuda_tp_generate(GPT *m, const int *prompt, int B, int T, int n_new, int *out_tokens);
+/* how tp_generate decodes: 1 split over the ranks as above; 2 replicated -
+ * every rank runs the whole one-GPU decode (cngpt_cuda_generate) on its full
+ * copy of the model, no exchange, identical tokens on every rank; 0 (default)
+ * replicated at batch 1, where the split step's two exchanges per layer cost
+ * more than the weight stream it divides, split at larger batches */
+int cngpt_cuda_tp_set_decode_mode(GPT *m, int mode);
 int cngpt_cuda_tp_free(GPT *m);
 
 /* ---- self-test hooks -------------------------------------------------------

@@ -83,6 +83,15 @@ def test_tp1_matches_reference(lib, cuda, name):
     check_case(lib, name, logits.reshape(fb, -1), out.reshape(gb, gn))
 
 
+def test_tp_decode_mode_rejects_unknown(lib, cuda):
+    m = CudaModel(lib, 1, 2, 128, 50, 16, 3)
+    uid = (C.c_ubyte * 128)()
+    abi.check(lib, lib.cngpt_cuda_tp_init(C.byref(m.m), uid, 1, 0), "tp_init")
+    assert lib.cngpt_cuda_tp_set_decode_mode(C.byref(m.m), 3) == abi.ERR_ARG
+    lib.cngpt_cuda_clear_status()
+    m.free()
+
+
 def test_tp_requires_init(lib, cuda):
     m = CudaModel(lib, 1, 2, 64, 50, 16, 3)
     out = np.zeros(4, np.int32)
@@ -107,8 +116,10 @@ def test_tp_multi_gpu_matches_reference(lib, cuda, world):
         assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
         res = [np.load(os.path.join(d, f"rank{k}.npz")) for k in range(world)]
     for name in names:
-        for k in ("_logits", "_tokens"):
+        for k in ("_logits", "_tokens", "_split"):
             for rk in range(1, world):
                 assert np.array_equal(res[0][name + k], res[rk][name + k]), (name, k, rk)
         check_case(lib, name, res[0][name + "_logits"], res[0][name + "_tokens"])
+        # the split decode (exchanges over NVLink) gives the same greedy tokens
+        assert np.array_equal(res[0][name + "_split"], res[0][name + "_tokens"]), name
     print(f"\ntp world {world}: cases {names} match the reference and the one-GPU decode on every rank")

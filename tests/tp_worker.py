@@ -25,6 +25,8 @@ CASES = {
     "xl2": ((2, 25, 1600, 50257, 1024, 3), (2, 48), (2, 16, 8)),
     # batch above the peer-exchange row limit: the decode exchanges go through NCCL
     "tp5w": ((2, 5, 320, 1001, 64, 11), (3, 40), (10, 6, 5)),
+    # batch 1: replicated decode by default, the split decode when asked
+    "tp5b1": ((2, 5, 320, 1001, 64, 11), (3, 40), (1, 12, 20)),
 }
 
 
@@ -43,9 +45,14 @@ def run(lib, name, world, rank, uid):
     out = np.zeros(gb * gn, np.int32)
     abi.check(lib, lib.cngpt_cuda_tp_generate(C.byref(m), prompt.ctypes.data, gb, gt, gn, out.ctypes.data),
               "tp_generate")
+    # the split decode, whatever the batch
+    split = np.zeros(gb * gn, np.int32)
+    abi.check(lib, lib.cngpt_cuda_tp_set_decode_mode(C.byref(m), 1), "decode mode")
+    abi.check(lib, lib.cngpt_cuda_tp_generate(C.byref(m), prompt.ctypes.data, gb, gt, gn, split.ctypes.data),
+              "tp_generate split")
     abi.check(lib, lib.cngpt_cuda_tp_free(C.byref(m)), "tp_free")
     lib.gpt_free(C.byref(m))
-    return logits.reshape(fb, -1), out.reshape(gb, gn)
+    return logits.reshape(fb, -1), out.reshape(gb, gn), split.reshape(gb, gn)
 
 
 def main(out_dir: str, names: list[str]):
@@ -62,7 +69,7 @@ def main(out_dir: str, names: list[str]):
         obj = [bytes(uid)]
         dist.broadcast_object_list(obj, src=0)
         uid = (C.c_ubyte * 128).from_buffer_copy(obj[0])
-        res[name + "_logits"], res[name + "_tokens"] = run(lib, name, world, rank, uid)
+        res[name + "_logits"], res[name + "_tokens"], res[name + "_split"] = run(lib, name, world, rank, uid)
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **res)
     dist.destroy_process_group()
 
