@@ -61,6 +61,12 @@ def main(out_dir: str):
     assert lib.gpt_init(C.byref(m), abi.GPTConfig(*CFG, 0.0)) == 0
     oracle.libc_rand_stream(7)
     lib.gpt_init_weights(C.byref(m))
+    uid = (C.c_ubyte * 128)()  # a communicator id serves one ncclCommInitRank round only
+    if rank == 0:
+        abi.check(lib, lib.cngpt_cuda_dp_unique_id(uid), "uid")
+    obj = [bytes(uid)]
+    dist.broadcast_object_list(obj, src=0)
+    uid = (C.c_ubyte * 128).from_buffer_copy(obj[0])
     abi.check(lib, lib.cngpt_cuda_dp_init(C.byref(m), uid, world, rank), "dp_init")
     ts_loss = C.c_float()
     abi.check(lib, lib.cngpt_cuda_train_step(C.byref(m), tok.ctypes.data, tgt.ctypes.data, B, T, 0.0, 0.9, 0.95,
