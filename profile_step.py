@@ -7,6 +7,7 @@ for profilers (ncu) and quick timing.
     python profile_step.py --decode xl|small [--B 1] [--T 128] [--new 8]
     python profile_step.py --attention [--B 8] [--T 1024] [--heads 12] [--reps 10]
     python profile_step.py --gemm-step [--reps 10] [--prec tf32]
+    python profile_step.py --tp-reduce [--B 1] [--reps 3]
 
 Token ids live on the device before the first step; nothing else runs.
 """
@@ -50,11 +51,23 @@ def main() -> None:
     ap.add_argument("--heads", type=int, default=12)
     ap.add_argument("--gemm-step", action="store_true", help="time each distinct GEMM shape of one GPT-2 small "
                     "training step (B=8, T=1024) alone and print its share of the step's GEMM time")
+    ap.add_argument("--tp-reduce", action="store_true", help="the tensor-parallel decode exchange's reduce "
+                    "kernel on one GPU (self-test hook, flag published): --B rows of n_embd 1600, --reps launches")
     a = ap.parse_args()
     import torch
     torch.cuda.set_device(0)
     lib = abi.load()
     lib.cngpt_cuda_set_precision(PREC[a.prec])
+    if a.tp_reduce:
+        rows, Cx = min(a.B, 8), 1600
+        part = torch.randn(rows, Cx, device="cuda")
+        x = torch.empty(rows, Cx, device="cuda")
+        stats = torch.empty(rows, 2, device="cuda")
+        for _ in range(a.reps):
+            abi.check(lib, lib.cngpt_cuda_selftest_tp_reduce(x.data_ptr(), part.data_ptr(), rows, Cx, 1,
+                                                            stats.data_ptr()), "tp reduce")
+        print(f"tp_reduce_kernel: {a.reps} launches of {rows} x {Cx}")
+        return
     if a.gemm:
         M, N, K = a.gemm
         A = torch.randn((K, M) if a.a_mn else (M, K), device="cuda")

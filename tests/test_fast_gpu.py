@@ -4,9 +4,11 @@ against the reference's CPU build on identical seeded weights.
 
 Tolerances: last-position logits normwise 1e-5 (3xTF32), 2e-3 (TF32).
 Greedy ids: every device token must be the reference's argmax of the
-full-prefix logits (teacher-forced on the device's own prefix), unless that
-position is a near-tie - the reference's top-1 and the device's token within
-1e-4 x max|logit| of each other - which the test counts and reports.
+full-prefix logits (teacher-forced on the device's own prefix: one causal
+reference forward over the window gives the final-position logits of every
+prefix), unless that position is a near-tie - the reference's top-1 and the
+device's token within 1e-4 x max|logit| of each other - which the test counts
+and reports.
 """
 import ctypes as C
 
@@ -85,19 +87,23 @@ def test_generate_greedy_matches_full_prefix_argmax(lib, cuda, name, B, T, n_new
                                            out.ctypes.data), "generate")
     lib.fast_free(C.byref(fc))
     out = out.reshape(B, n_new)
+    # step i's token is the argmax of the final-position logits of the prefix
+    # [0, T + i): one causal forward of the reference over the whole window
+    # (the device's own prefix) gives every such row at once (row T - 1 + i)
+    S = T + n_new - 1
+    seq = np.concatenate([prompt.reshape(B, T), out[:, :-1]], axis=1).astype(np.int32).ravel()
+    ref.forward(seq, None, B, S)
+    lgs = ref.logits(B, S)[:, T - 1:, :]
     ties = 0
     for b in range(B):
-        seq = list(prompt[b * T:(b + 1) * T])
         for i in range(n_new):
-            ctx = np.array(seq, np.int32)
-            lg = ref_fast(ref, ctx, 1, len(seq))[0]
+            lg = lgs[b, i]
             top = int(np.argmax(lg))
             got = int(out[b, i])
             if got != top:
                 margin = lg[top] - lg[got]
                 assert margin <= 1e-4 * np.max(np.abs(lg)), (b, i, top, got, margin)
                 ties += 1
-            seq.append(got)
     print(f"\n[{name}] {B}x{n_new} greedy tokens, {ties} near-tie(s)")
     assert ties <= max(1, (B * n_new) // 20)
     ref.free()
