@@ -299,6 +299,33 @@ __global__ void attn_bwd_dot_kernel(const float *__restrict__ out, const float *
     }
 }
 
+// Same for head size 64 with 16-byte loads: a warp takes a whole token row
+// (b, t) of every head - lane l reads float4 l + 32 j of O and dO, which lie
+// in head 2 j + l / 16 - so its loads are coalesced across the row, and each
+// half-warp reduces one head's 16 float4 products.
+__global__ void attn_bwd_dot64_kernel(const float *__restrict__ out, const float *__restrict__ dout,
+                                      float *__restrict__ D, int B, int T, int C, int H) {
+    const long rows = (long)B * T;
+    const int lane = threadIdx.x & 31, C4 = C >> 2;
+    for (long r = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5; r < rows;
+         r += ((long)gridDim.x * blockDim.x) >> 5) {
+        const int b = (int)(r / T), tt = (int)(r % T);
+        const float4 *o = (const float4 *)(out + r * C), *d = (const float4 *)(dout + r * C);
+        for (int j = 0; 32 * j < C4; ++j) {
+            const int f = lane + 32 * j;
+            float s = 0.f;
+            if (f < C4) {
+                const float4 a = __ldcs(o + f), g = __ldcs(d + f);
+                s = (a.x * g.x + a.y * g.y) + (a.z * g.z + a.w * g.w);
+            }
+#pragma unroll
+            for (int k = 8; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k);
+            const int h = 2 * j + (lane >> 4);
+            if ((lane & 15) == 0 && h < H) D[((long)b * H + h) * T + tt] = s;
+        }
+    }
+}
+
 // dK, dV for one 64-key tile; loops over query tiles qt >= kt with the next
 // Q / dO tile prefetched while the current one is used.
 template <bool SPLIT>
@@ -898,8 +925,14 @@ int attention_bwd(const float *qkv, const float *out, const float *dout, const f
     const float scale = 1.0f / sqrtf((float)hs);
     float *D = scratch;
     const long rows = (long)B * H * T;
-    attn_bwd_dot_kernel<<<(int)std::min<long>((rows + 7) / 8, 148L * 64), 256, 0, s>>>(out, dout, D, B,
-                                                                                      T, C, H, hs);
+    if (hs == 64 && C % 128 == 0 && ((uintptr_t)out % 16) == 0 && ((uintptr_t)dout % 16) == 0) {
+        const long trows = (long)B * T;
+        attn_bwd_dot64_kernel<<<(int)std::min<long>((trows + 7) / 8, 148L * 16), 256, 0, s>>>(out, dout, D, B, T,
+                                                                                            C, H);
+    } else {
+        attn_bwd_dot_kernel<<<(int)std::min<long>((rows + 7) / 8, 148L * 64), 256, 0, s>>>(out, dout, D, B, T, C,
+                                                                                          H, hs);
+    }
     LAUNCH_CHECK();
     if (precision() == PREC_TF32 && tc_attention_enabled() &&
         attention_bwd_tc(qkv, dout, lse, D, dqkv, B, T, C, H, s) == OK)
