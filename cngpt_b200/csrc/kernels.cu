@@ -47,6 +47,47 @@ __global__ void layernorm_fwd_kernel(const float *__restrict__ x, long ldx,
     }
 }
 
+// Same for C = 128 NJ with 16-byte rows: a warp holds its row in registers
+// (lane l: float4 l + 32 j), so x is read from memory once; the mean, then
+// the sum of squared deviations about it, as above.
+template <int NJ>
+__global__ void __launch_bounds__(256)
+layernorm_fwd4_kernel(const float *__restrict__ x, long ldx, const float *__restrict__ w, const float *__restrict__ b,
+                      float *__restrict__ out, long ldo, float *__restrict__ mean, float *__restrict__ rstd, int T) {
+    pdl_trigger();
+    constexpr int C = 128 * NJ;
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (long t = (long)blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += (long)gridDim.x * warps) {
+        const float4 *xr = (const float4 *)(x + t * ldx);
+        float4 v[NJ];
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            v[j] = __ldg(xr + lane + 32 * j);
+            s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+        }
+        const float m = warp_sum(s) / (float)C;
+        float q = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const float a = v[j].x - m, bb = v[j].y - m, c = v[j].z - m, d = v[j].w - m;
+            q += (a * a + bb * bb) + (c * c + d * d);
+        }
+        const float rs = 1.0f / sqrtf(warp_sum(q) / (float)C + 1e-5f);
+        if (lane == 0) {
+            if (mean) mean[t] = m;
+            if (rstd) rstd[t] = rs;
+        }
+        float4 *orow = (float4 *)(out + t * ldo);
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const float4 g = __ldg((const float4 *)w + lane + 32 * j), bv = __ldg((const float4 *)b + lane + 32 * j);
+            orow[lane + 32 * j] = make_float4((v[j].x - m) * rs * g.x + bv.x, (v[j].y - m) * rs * g.y + bv.y,
+                                              (v[j].z - m) * rs * g.z + bv.z, (v[j].w - m) * rs * g.w + bv.w);
+        }
+    }
+}
+
 // dx += rstd (dn - mean(dn) - xhat mean(dn xhat)) per row (src/ops.c:305-329),
 // dn = dout * w, xhat = (x - mean) * rstd: one warp per row, two passes.
 __global__ void __launch_bounds__(256)
@@ -140,7 +181,7 @@ layernorm_bwd_reduce(const float *__restrict__ part, int nblocks, int C, float *
 // part[block][3][C], and ln_bwd_part_reduce adds the blocks in block order -
 // a fixed order, so the result is deterministic.
 template <int NJ>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 ln_bwd_fused_kernel(const float *__restrict__ dout, const float *__restrict__ x, const float *__restrict__ w,
                     const float *__restrict__ mean, const float *__restrict__ rstd, float *__restrict__ dx, int T,
                     int rows_per_block, float *__restrict__ part, int want_cs) {
@@ -155,9 +196,7 @@ ln_bwd_fused_kernel(const float *__restrict__ dout, const float *__restrict__ x,
         my[C / 4 + lane + 32 * j] = z;
         my[2 * (C / 4) + lane + 32 * j] = z;
     }
-    float4 wv[NJ];
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) wv[j] = __ldg((const float4 *)w + lane + 32 * j);
+    const float4 *wv = (const float4 *)w;  // read through L1 at each use (3 KB, every row)
     const long r0 = (long)blockIdx.x * rows_per_block;
     const long r1 = std::min<long>(T, r0 + rows_per_block);
     const float invC = 1.0f / (float)C;
@@ -176,7 +215,8 @@ ln_bwd_fused_kernel(const float *__restrict__ dout, const float *__restrict__ x,
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
             xh[j] = make_float4((xh[j].x - m) * rs, (xh[j].y - m) * rs, (xh[j].z - m) * rs, (xh[j].w - m) * rs);
-            const float4 dn = make_float4(d[j].x * wv[j].x, d[j].y * wv[j].y, d[j].z * wv[j].z, d[j].w * wv[j].w);
+            const float4 wj = __ldg(wv + lane + 32 * j);
+            const float4 dn = make_float4(d[j].x * wj.x, d[j].y * wj.y, d[j].z * wj.z, d[j].w * wj.w);
             s1 += (dn.x + dn.y) + (dn.z + dn.w);
             s2 += (dn.x * xh[j].x + dn.y * xh[j].y) + (dn.z * xh[j].z + dn.w * xh[j].w);
         }
@@ -184,7 +224,7 @@ ln_bwd_fused_kernel(const float *__restrict__ dout, const float *__restrict__ x,
         s2 = warp_sum(s2) * invC;
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
-            const float4 dv = d[j], xv = xh[j], wj = wv[j];
+            const float4 dv = d[j], xv = xh[j], wj = __ldg(wv + lane + 32 * j);
             float4 n = o[j];
             n.x += rs * (dv.x * wj.x - s1 - xv.x * s2);
             n.y += rs * (dv.y * wj.y - s1 - xv.y * s2);
@@ -211,23 +251,24 @@ ln_bwd_fused_kernel(const float *__restrict__ dout, const float *__restrict__ x,
 }
 
 // dw, db (and cs) += the blocks' partials part[nb][3][C]: one block per 32 of
-// the 3C sums, lane = sum, warp w adds the partials of blocks w, w + 8, ... in
-// order, then the 8 warp totals are added in warp order (fixed order).
-__global__ void __launch_bounds__(256)
+// the 3C sums, lane = sum, warp w adds the partials of blocks w, w + 16, ...
+// in order, then the 16 warp totals are added in warp order (fixed order).
+__global__ void __launch_bounds__(512)
 ln_bwd_part_reduce(const float *__restrict__ part, int nb, int C, float *__restrict__ dw, float *__restrict__ db,
                    float *__restrict__ cs) {
-    __shared__ float red[8][32];
+    __shared__ float red[16][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int j = blockIdx.x * 32 + lane;  // index into [3][C]
     float v = 0.f;
     if (j < 3 * C)
-        for (int b = warp; b < nb; b += 8) v += part[(long)b * 3 * C + j];
+#pragma unroll 4
+        for (int b = warp; b < nb; b += 16) v += part[(long)b * 3 * C + j];
     red[warp][lane] = v;
     __syncthreads();
     if (warp == 0 && j < 3 * C) {
         float t = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) t += red[w][lane];
+        for (int w = 0; w < 16; ++w) t += red[w][lane];
         const int k = j / C, c = j - k * C;  // 0: dw, 1: db, 2: cs
         float *dst = k == 0 ? dw : (k == 1 ? db : cs);
         if (dst) dst[c] += t;
@@ -780,6 +821,17 @@ int layernorm_fwd(const float *x, long ldx, const float *w, const float *b, floa
                   float *mean, float *rstd, int T, int C, cudaStream_t s) {
     if (T <= 0) return OK;
     const int warps = 8;
+    const uintptr_t al = (uintptr_t)x | (uintptr_t)w | (uintptr_t)b | (uintptr_t)out;
+    if (C % 128 == 0 && C <= 1024 && ldx % 4 == 0 && ldo % 4 == 0 && al % 16 == 0) {
+        const int g = grid_for(T, warps, 148 * 8);
+        switch (C / 128) {
+#define LNF4(N) case N: layernorm_fwd4_kernel<N><<<g, warps * 32, 0, s>>>(x, ldx, w, b, out, ldo, mean, rstd, T); break;
+            LNF4(1) LNF4(2) LNF4(3) LNF4(4) LNF4(5) LNF4(6) LNF4(7) LNF4(8)
+#undef LNF4
+        }
+        LAUNCH_CHECK();
+        return OK;
+    }
     layernorm_fwd_kernel<<<grid_for(T, warps, 148 * 8), warps * 32, 0, s>>>(x, ldx, w, b, out, ldo,
                                                                            mean, rstd, T, C);
     LAUNCH_CHECK();
@@ -871,7 +923,7 @@ int layernorm_bwd_fused(const float *dout, const float *x, const float *w, const
         case 7: CG_TRY(launch_ln_bwd_fused<7>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
         default: CG_TRY(launch_ln_bwd_fused<8>(dout, x, w, mean, rstd, dx, T, nb, rpb, scratch, cs, s)); break;
     }
-    ln_bwd_part_reduce<<<(3 * C + 31) / 32, 256, 0, s>>>(scratch, nb, C, dw, db, cs);
+    ln_bwd_part_reduce<<<(3 * C + 31) / 32, 512, 0, s>>>(scratch, nb, C, dw, db, cs);
     LAUNCH_CHECK();
     return OK;
 }
