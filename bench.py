@@ -493,6 +493,39 @@ def train_configs_bench(lib, torch, dev, world: int, rank: int, barrier, max_ove
     return out
 
 
+def loader_e2e(lib, torch, m, rank: int, K: int, barrier, max_over_ranks, step_no) -> float:
+    """ms per training step fed by the device batch loader from a host uint16
+    token array (as the reference's DataLoader mmaps it), loss read back every
+    step: host copy into the pinned buffer, H2D and widening inside the timed
+    region, overlapped with the previous step."""
+    from cngpt_b200 import abi
+    data = lcg_tokens(4 * B_ * T_ + 1, V_, 777 + rank).astype(np.uint16)
+    h = C.c_void_p()
+    abi.check(lib, lib.cngpt_cuda_loader_create(C.byref(h), data.ctypes.data, data.size, B_, T_), "loader")
+    loss = C.c_float()
+
+    def step():
+        i, t = C.c_void_p(), C.c_void_p()
+        abi.check(lib, lib.cngpt_cuda_loader_next(h, C.byref(i), C.byref(t)), "loader next")
+        st = lib.cngpt_cuda_train_step(C.byref(m), i, t, B_, T_, lr_schedule(step_no[0]), 0.9, 0.95, 1e-8, 0.1,
+                                       1.0, C.addressof(loss))
+        step_no[0] += 1
+        if st:
+            raise RuntimeError(lib.cngpt_cuda_last_message().decode())
+    step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    lib.cngpt_cuda_loader_free(h)
+    return max_over_ranks(e0.elapsed_time(e1)) / K
+
+
 def step_flops_cfg(L: int, Cm: int, V: int, B: int, T: int) -> float:
     """Algorithmic FLOP of one training step (3 x forward: linears, causal
     attention over T(T+1)/2 pairs, LM head)."""
@@ -592,6 +625,7 @@ def run_ours(args) -> None:
     tokens = B_ * T_ * world
     value = tokens / (ms * 1e-3)
     ms_e2e, _, _ = timed(abi.PREC_TF32, True, max(3, args.steps // 2), 1)
+    ms_loader = loader_e2e(lib, torch, m, rank, max(3, args.steps // 2), barrier, max_over_ranks, step_no)
     ms_3x, _, loss_3x = timed(abi.PREC_3XTF32, False, max(3, args.steps // 2), 1)
     fl = step_flops(B_, T_)
     peaks = {}
@@ -616,6 +650,10 @@ def run_ours(args) -> None:
         "e2e": {"value": tokens / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 3 * B_ * T_ * 4, "d2h_bytes_per_step": 4,
                 "api": "cngpt_cuda_train_step with pinned host token buffers and the loss read back"},
+        "e2e_loader": {"value": tokens / (ms_loader * 1e-3), "unit": "tokens/s",
+                       "h2d_bytes_per_step": (B_ * T_ + 1) * 2, "d2h_bytes_per_step": 4,
+                       "api": "cngpt_cuda_loader_next (uint16 host token array through a pinned buffer, uploaded "
+                              "one batch ahead) + cngpt_cuda_train_step with the loss read back"},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": fc["tflops"], "peak": tf32_peak,
                      "unit": "TFLOP/s", "frac": fc["tflops"] / tf32_peak, "traffic": traffic,
