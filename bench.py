@@ -91,7 +91,8 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.window = None  # (start, end) of the timed region, monotonic seconds
 
     def __enter__(self):
         try:
@@ -106,7 +107,10 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def mark(self, start: float, end: float):
+        self.window = (start, end)
 
     def __exit__(self, *a):
         if self.proc:
@@ -117,9 +121,17 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        """Samples taken inside the timed region; when it was shorter than the
+        sampling period, the samples of the warm-up steps just before it (the
+        same load) with `samples_in_window` saying so."""
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        lines = [ln for _, ln in self.lines]
+        inside = lines
+        if self.window:
+            inside = [ln for t, ln in self.lines if self.window[0] <= t <= self.window[1] + 0.25]
+        n_inside = len(inside)
+        for ln in (inside if inside else lines):
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -132,7 +144,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "samples_in_window": n_inside}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -596,20 +608,23 @@ def run_ours(args) -> None:
         loss = C.c_float()
         args_ = ((tok_h.data_ptr(), tgt_h.data_ptr(), C.addressof(loss)) if host_io
                  else (tok_d.data_ptr(), tgt_d.data_ptr(), None))
-        for _ in range(W):
-            train_step(*args_)
-        torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        l0 = lib.cngpt_cuda_launch_count()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ctx = clocks if clocks is not None else _Null()
-        with ctx:
+        with ctx:  # the sampler starts before the warm-up: nvidia-smi takes a while to report
+            for _ in range(W):
+                train_step(*args_)
+            torch.cuda.synchronize()
+            barrier()
+            torch.cuda.synchronize()
+            l0 = lib.cngpt_cuda_launch_count()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t_start = time.monotonic()
             e0.record()
             for _ in range(K):
                 train_step(*args_)
             e1.record()
             torch.cuda.synchronize()
+            if clocks is not None:
+                clocks.mark(t_start, time.monotonic())
         barrier()
         launches = lib.cngpt_cuda_launch_count() - l0
         ms = max_over_ranks(e0.elapsed_time(e1)) / K

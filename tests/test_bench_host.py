@@ -55,17 +55,31 @@ def test_token_stream_and_schedule_follow_the_reference():
 
 def test_clock_record_parsing():
     c = bench.ClockSampler(0)
-    c.lines = [
+    c.lines = list(enumerate([
         "0, 1950, 1965, 900.1, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
         "0, 1965, 1965, 990.0, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
         "0, 1900, 1965, 999.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
         "garbage line",
-    ]
+    ]))
     s = c.summary()
     assert s["samples"] == 3 and s["sm_mhz"] == 1950 and s["sm_max_mhz"] == 1965
     assert s["reasons"] == ["sw_power_cap"]
-    c.lines.append("0, 1200, 1965, 700.0, 0x0000000000000008, Active, Not Active, Not Active, Not Active")
+    c.lines.append((4, "0, 1200, 1965, 700.0, 0x0000000000000008, Active, Not Active, Not Active, Not Active"))
     assert "hw_slowdown" in c.summary()["reasons"]
+
+
+def test_clock_window_keeps_timed_samples():
+    """Samples of the warm-up steps drop out once the timed region holds
+    some; a region shorter than the sampling period keeps the warm-up's."""
+    c = bench.ClockSampler(0)
+    row = "0, {}, 1965, 900.0, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active"
+    c.lines = [(0.0, row.format(1000)), (1.0, row.format(1900)), (1.2, row.format(1910))]
+    c.mark(0.9, 1.1)
+    s = c.summary()
+    assert s["samples_in_window"] == 2 and s["samples"] == 2 and s["sm_mhz"] == 1905
+    c.mark(5.0, 5.01)
+    s = c.summary()
+    assert s["samples_in_window"] == 0 and s["samples"] == 3
 
 
 def test_step_gemm_shapes_cover_the_step():
