@@ -427,8 +427,14 @@ def inference_bench(lib, torch, dev, world: int, rank: int, hbm_peak: float, bar
                                                                      toks.ctypes.data), "tp generate")
         t1, tn = timed(gen(1), 1), timed(gen(n), 1)
         per = (tn - t1) / (n - 1)
-        gbs = decode_bytes(m.n_params, L, Cx, B, T, n) / world / per / 1e9
+        # batch 1 decodes replicated on every rank (the default decode mode):
+        # each GPU streams all the weights and the whole cache; above batch 1
+        # the weights and the heads are split across the ranks
+        replicated = world > 1 and B == 1
+        shards = 1 if replicated else world
+        gbs = decode_bytes(m.n_params, L, Cx, B, T, n) / shards / per / 1e9
         xl[f"decode_B{B}"] = {"tokens_per_s": B / per, "ms_per_step": per * 1e3,
+                              "mode": "replicated" if replicated else ("split" if world > 1 else "one GPU"),
                               "hbm_gbs_per_gpu": gbs, "hbm_frac_per_gpu": gbs / hbm_peak}
     lib.cngpt_cuda_tp_free(C.byref(m))
     lib.gpt_free(C.byref(m))

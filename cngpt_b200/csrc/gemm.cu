@@ -22,6 +22,11 @@
 //               normwise for one accumulator over K); per-k-block partials keep
 //               3xTF32 at fp32-level accuracy for any K
 //
+// The TF32 CTA-pair kernel (gemm_tc2_kernel: two CTAs of a cluster share one
+// 256-row tile through tcgen05.mma.cta_group::2) runs 16 epilogue warps at
+// BN = 256; they read the accumulator in the 16x256b layout and store from
+// registers (store_frag).
+//
 // Operands may be K-major or MN-major in global memory (the instruction
 // descriptor's transpose bits), so X W^T (forward), dY W (dX) and dY^T X (dW)
 // all load straight from their row-major buffers without a transpose pass.
@@ -77,30 +82,35 @@ struct SmemCtl {
 // Fused epilogue for one output element (m, n) holding the raw product a;
 // `aux` is the element's prefetched second operand (D for ACCUM, R for RESID,
 // G for GELU_BWD).
-__device__ __forceinline__ void epi_apply(const GemmEpi &e, long m, int n, float a, float bias,
-                                          float aux) {
+// D is the output in place of e.D (the split-K kernels offset it per split).
+__device__ __forceinline__ void epi_apply_d(const GemmEpi &e, float *D, long m, int n, float a, float bias,
+                                            float aux) {
     a *= e.alpha;
     switch (e.mode) {
         case EPI_STORE:
-            e.D[m * e.ldd + n] = a + bias;
+            D[m * e.ldd + n] = a + bias;
             break;
         case EPI_ACCUM:
-            e.D[m * e.ldd + n] = (aux + a) + bias;
+            D[m * e.ldd + n] = (aux + a) + bias;
             break;
         case EPI_GELU:
             a += bias;
-            if (e.D) e.D[m * e.ldd + n] = a;
+            if (D) D[m * e.ldd + n] = a;
             e.D2[m * e.ldd2 + n] = gelu_tanh(a, e.fast_act);
             break;
         case EPI_RESID:
             a += bias;
-            if (e.D) e.D[m * e.ldd + n] = a;
+            if (D) D[m * e.ldd + n] = a;
             e.D2[m * e.ldd2 + n] = aux + a;
             break;
         case EPI_GELU_BWD:
-            e.D[m * e.ldd + n] = a * gelu_tanh_grad(aux, e.fast_act);
+            D[m * e.ldd + n] = a * gelu_tanh_grad(aux, e.fast_act);
             break;
     }
+}
+
+__device__ __forceinline__ void epi_apply(const GemmEpi &e, long m, int n, float a, float bias, float aux) {
+    epi_apply_d(e, e.D, m, n, a, bias, aux);
 }
 
 __device__ __forceinline__ const float *epi_aux(const GemmEpi &e, long &ld) {
@@ -114,17 +124,27 @@ __device__ __forceinline__ const float *epi_aux(const GemmEpi &e, long &ld) {
 
 // Cross-entropy statistics of one row's 32 columns [n0, n0 + 32) (thread =
 // row, v its raw products), folded into the running (max, sum exp(x - max))
-// of the row's current 64-column group.
-__device__ __forceinline__ void ce_fold(const float (&v)[32], int n0, int N, float alpha, float &m, float &s) {
+// of the row's current 64-column group. `fast` (TF32 mode, GemmEpi::fast_act)
+// sums the terms with the __expf intrinsic: each term is <= 1 and the group
+// sum is dominated by the terms near the maximum, where its error is a few
+// ulp - far below the TF32 products' own error.
+__device__ __forceinline__ void ce_fold(const float (&v)[32], int n0, int N, float alpha, float &m, float &s,
+                                        bool fast) {
     float mx = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 32; ++j)
         if (n0 + j < N) mx = fmaxf(mx, v[j] * alpha);
     if (mx == -INFINITY) return;
     float add = 0.f;
+    if (fast) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-        if (n0 + j < N) add += expf(v[j] * alpha - mx);
+        for (int j = 0; j < 32; ++j)
+            if (n0 + j < N) add += __expf(v[j] * alpha - mx);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (n0 + j < N) add += expf(v[j] * alpha - mx);
+    }
     if (mx > m) {
         s = s * expf(m - mx) + add;
         m = mx;
@@ -173,10 +193,17 @@ __device__ __forceinline__ void store_block(const GemmEpi &ep, float *stile, int
         };
         switch (ep.mode) {
             case EPI_STORE:
-                run([&](long m, float4 a) {
-                    *(float4 *)(ep.D + m * ep.ldd + n) =
-                        make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
-                });
+                if (ep.stream_out) {
+                    run([&](long m, float4 a) {
+                        __stcs((float4 *)(ep.D + m * ep.ldd + n),
+                               make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w));
+                    });
+                } else {
+                    run([&](long m, float4 a) {
+                        *(float4 *)(ep.D + m * ep.ldd + n) =
+                            make_float4(a.x + b4.x, a.y + b4.y, a.z + b4.z, a.w + b4.w);
+                    });
+                }
                 break;
             case EPI_ACCUM:
                 run([&](long m, float4 a) {
@@ -229,6 +256,103 @@ __device__ __forceinline__ void store_block(const GemmEpi &ep, float *stile, int
     }
     __syncwarp();
     }
+
+// ---- epilogue on the 16x256b TMEM layout (CTA-pair kernel)
+//
+// A 32 x 32 output block arrives as two 16-lane tcgen05.ld of 16x256b.x4:
+// v[16h + 4j + 2u + e] is row 16h + 8u + lane/4, column 8j + 2(lane%4) + e of
+// the block. Pair k = 8h + 2j + u (values v[2k], v[2k+1]) is one 8-byte
+// access, and a warp's access of one pair covers 8 rows x 32 contiguous bytes:
+// whole sectors, written straight from registers with no shared-memory
+// transpose.
+__device__ __forceinline__ long frag_row(int k, int lane) { return 16 * (k >> 3) + 8 * (k & 1) + (lane >> 2); }
+__device__ __forceinline__ int frag_col(int k, int lane) { return 8 * ((k >> 1) & 3) + (lane & 3) * 2; }
+
+// p[0] = o.x and, when `two`, p[1] = o.y: one 8-byte store when `vec` (p is
+// then 8-byte aligned), else two scalar stores.
+__device__ __forceinline__ void put2(float *p, float2 o, bool two, bool vec) {
+    if (two && vec) {
+        *(float2 *)p = o;
+    } else {
+        p[0] = o.x;
+        if (two) p[1] = o.y;
+    }
+}
+
+__device__ __forceinline__ float2 get2(const float *p, bool two, bool vec) {
+    if (two && vec) return *(const float2 *)p;
+    return make_float2(p[0], two ? p[1] : 0.f);
+}
+
+// `vec`: every operand pointer 16-byte aligned and every pitch a multiple of
+// 4 floats (GemmEpi::vec4), so the pairs at even columns are 8-byte aligned.
+__device__ __forceinline__ void store_frag(const GemmEpi &ep, float *D, const float (&v)[32], int lane, int m0,
+                                           int n0, int M, int N, const float *aux, long ldaux) {
+    const bool vec = ep.vec4 != 0;
+    float2 b[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int n = n0 + frag_col(2 * j, lane);
+        b[j] = ep.bias && n < N ? get2(ep.bias + n, n + 1 < N, vec) : make_float2(0.f, 0.f);
+    }
+    const float al = ep.alpha;
+    const bool fa = ep.fast_act != 0;
+    // two halves of 16 rows; in each, the second operands are loaded first so
+    // their loads are in flight together
+    auto run = [&](auto op) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float2 x[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int k = 8 * h + i;
+                const long m = m0 + frag_row(k, lane);
+                const int n = n0 + frag_col(k, lane);
+                x[i] = aux && m < M && n < N ? get2(aux + m * ldaux + n, n + 1 < N, vec) : make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int k = 8 * h + i;
+                const long m = m0 + frag_row(k, lane);
+                const int n = n0 + frag_col(k, lane);
+                if (m < M && n < N)
+                    op(m, n, make_float2(v[2 * k] * al, v[2 * k + 1] * al), b[(k >> 1) & 3], x[i], n + 1 < N);
+            }
+        }
+    };
+    switch (ep.mode) {
+        case EPI_STORE:
+            run([&](long m, int n, float2 a, float2 bb, float2, bool two) {
+                put2(D + m * ep.ldd + n, make_float2(a.x + bb.x, a.y + bb.y), two, vec);
+            });
+            break;
+        case EPI_ACCUM:
+            run([&](long m, int n, float2 a, float2 bb, float2 o, bool two) {
+                put2(D + m * ep.ldd + n, make_float2((o.x + a.x) + bb.x, (o.y + a.y) + bb.y), two, vec);
+            });
+            break;
+        case EPI_GELU:
+            run([&](long m, int n, float2 a, float2 bb, float2, bool two) {
+                a = make_float2(a.x + bb.x, a.y + bb.y);
+                if (D) put2(D + m * ep.ldd + n, a, two, vec);
+                put2(ep.D2 + m * ep.ldd2 + n, make_float2(gelu_tanh(a.x, fa), gelu_tanh(a.y, fa)), two, vec);
+            });
+            break;
+        case EPI_RESID:
+            run([&](long m, int n, float2 a, float2 bb, float2 r, bool two) {
+                a = make_float2(a.x + bb.x, a.y + bb.y);
+                if (D) put2(D + m * ep.ldd + n, a, two, vec);
+                put2(ep.D2 + m * ep.ldd2 + n, make_float2(r.x + a.x, r.y + a.y), two, vec);
+            });
+            break;
+        case EPI_GELU_BWD:
+            run([&](long m, int n, float2 a, float2, float2 g, bool two) {
+                put2(D + m * ep.ldd + n,
+                     make_float2(a.x * gelu_tanh_grad(g.x, fa), a.y * gelu_tanh_grad(g.y, fa)), two, vec);
+            });
+            break;
+    }
+}
 
 template <int BN, bool A_MN, bool B_MN, bool SPLIT>
 __global__ void __launch_bounds__(Cfg<BN, SPLIT>::THREADS, 1)
@@ -438,7 +562,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = sum[c * 32 + j];
                 const int n0 = tn * BN + (c0 + c) * 32;
-                if (ep.ce_part) ce_fold(v, n0, N, ep.alpha, cm, cs);
+                if (ep.ce_part) ce_fold(v, n0, N, ep.alpha, cm, cs, ep.fast_act != 0);
                 store_block_(v, m0, n0);
                 if (ep.ce_part) ce_flush(ep, c, m0 + lane, n0, M, N, cm, cs);
             }
@@ -452,7 +576,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) +
                                        ((uint32_t)(q * 32) << 16), v);
                 const int n0 = tn * BN + (c0 + c) * 32;
-                if (ep.ce_part) ce_fold(v, n0, N, ep.alpha, cm, cs);
+                if (ep.ce_part) ce_fold(v, n0, N, ep.alpha, cm, cs, ep.fast_act != 0);
                 store_block_(v, m0, n0);
                 if (ep.ce_part) ce_flush(ep, c, m0 + lane, n0, M, N, cm, cs);
             }
@@ -516,25 +640,37 @@ done:
 // CTAs' TMA completions count on the leader's `full` barrier, the MMA commits
 // arrive on `empty` / `tfull` in both CTAs, and the epilogue warps of both
 // CTAs release an accumulator on the leader's `tempty`. TF32 mode only.
-template <int BN>
+// ROWT selects the epilogue flavour. false: 16 epilogue warps at BN = 256
+// (four per TMEM lane quarter, two 32-column chunks each) reading the
+// accumulator in the 16x256b layout and storing 8-byte pairs from registers
+// (store_frag) - enough warps to hide the global stores and the GELU /
+// GELU-backward arithmetic behind the next tile's main loop. true: 8 warps
+// reading the 32x32b layout (thread = row), transposing each 32 x 32 block
+// through a padded shared tile and writing whole 128-byte row segments
+// (store_block), with the cross-entropy statistics folded in - measured
+// faster on the forward GEMMs whose output is far larger than L2 (the LM
+// head: 8192 x 50257 x 768, 1.46 ms against 1.79 ms).
+template <int BN, bool ROWT = false>
 struct Cfg2 {
     static constexpr int BNH = BN / 2;  // B rows per CTA
     static constexpr int A_BYTES = BM * KB_BYTES;
     static constexpr int B_BYTES = BNH * KB_BYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = BN == 256 ? 6 : 8;
-    static constexpr int EPI_WARPS = 8;
+    static constexpr int EPI_WARPS = BN == 256 && !ROWT ? 16 : 8;
+    static constexpr int CHUNKS = BN / 32 / (EPI_WARPS / 4);  // per warp and tile
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + EPI_WARPS * 32 * 33 * 4;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + (ROWT ? EPI_WARPS * 32 * 33 * 4 : 0);
+    static_assert(CHUNKS % 2 == 0, "the cross-entropy groups need chunk pairs");
 };
 
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg2<BN>::THREADS, 1)
+template <int BN, bool A_MN, bool B_MN, bool ROWT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg2<BN, ROWT>::THREADS, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 int M, int N, int K, int tiles_m, int tiles_n, int ksplit, int kb_per, long split_stride,
                 GemmEpi epi) {
-    using C = Cfg2<BN>;
+    using C = Cfg2<BN, ROWT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     SmemCtl *ctl = (SmemCtl *)(base + C::STAGES * C::STAGE_BYTES);
@@ -648,35 +784,55 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         }
     } else {
         // ------------------------------------------------- epilogue (both CTAs)
-        const int q = warp & 3, half = (warp - 2) >> 2;
-        constexpr int CH = BN / 64;
-        float *stile = (float *)(base + C::STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
+        // warp w reads TMEM lane quarter w % 4 and the column slice (w - 2) / 4
+        const int q = warp & 3, slice = (warp - 2) >> 2;
+        constexpr int CH = C::CHUNKS;
         const uint32_t tempty_leader = mapa_shared(smem_u32(&ctl->tempty[0]), 0);
-        GemmEpi ep = epi;
         long ldaux = 0;
         const float *aux = epi_aux(epi, ldaux);
+        float *stile = (float *)(base + C::STAGES * C::STAGE_BYTES + 256) + (warp - 2) * (32 * 33);
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs) {
             const int tm = (tile % mn_tiles) % tiles_m, tn = (tile % mn_tiles) / tiles_m;
-            ep.D = epi.D + (tile / mn_tiles) * split_stride;
+            float *const D = epi.D ? epi.D + (tile / mn_tiles) * split_stride : nullptr;
             const int m0 = tm * 2 * BM + (int)rank * BM + q * 32;
-            const int c0 = half * CH;
             if (!mbar_wait(&ctl->tfull[acc], acc_phase, DEV_ERR_GEMM_EPILOGUE, abort)) break;
             tc_fence_after();
             float cm = -INFINITY, cs = 0.f;
 #pragma unroll 1
             for (int c = 0; c < CH; ++c) {
-                float v[32];
-                tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * BN + (c0 + c) * 32) + ((uint32_t)(q * 32) << 16), v);
-                const int n0 = tn * BN + (c0 + c) * 32;
-                if (ep.ce_part) ce_fold(v, n0, N, ep.alpha, cm, cs);
-                store_block(ep, stile, lane, v, m0, n0, M, N, aux, ldaux);
-                if (ep.ce_part) ce_flush(ep, c, m0 + lane, n0, M, N, cm, cs);
+                const int col = (slice * CH + c) * 32;
+                const int n0 = tn * BN + col;
+                const uint32_t ta = tmem_base + (uint32_t)(acc * BN + col) + ((uint32_t)(q * 32) << 16);
+                auto release = [&] {  // the accumulator is read: the MMA warp may reuse it
+                    if (c == CH - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+                    }
+                };
+                if constexpr (ROWT) {
+                    float v[32];
+                    tmem_ld_32x32b_x32(ta, v);
+                    release();
+                    GemmEpi ep = epi;
+                    ep.D = D;
+                    if (epi.ce_part) ce_fold(v, n0, N, epi.alpha, cm, cs, epi.fast_act != 0);
+                    store_block(ep, stile, lane, v, m0, n0, M, N, aux, ldaux);
+                    if (epi.ce_part) ce_flush(epi, c, m0 + lane, n0, M, N, cm, cs);
+                } else {
+                    uint32_t r[32];
+                    tmem_ld_16x256b_x4_nowait(ta, r);
+                    tmem_ld_16x256b_x4_nowait(ta + (16u << 16), r + 16);
+                    tmem_ld_wait32(r);
+                    release();
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                    store_frag(epi, D, v, lane, m0, n0, M, N, aux, ldaux);
+                }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
     }
@@ -1355,11 +1511,18 @@ int pair_slots(Kern kern, int threads, int smem) {
 template <int BN, bool A_MN, bool B_MN>
 int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi,
                cudaStream_t s) {
-    using C = Cfg2<BN>;
+    using C = Cfg2<BN, false>;
+    // the row-transposed epilogue (Cfg2<BN, true>) is instantiated for the
+    // forward orientation at BN = 256 only: the LM head, whose statistics it
+    // folds, and STORE GEMMs whose output is far larger than L2
+    constexpr bool kRowT = !A_MN && !B_MN && BN == 256;
+    using CR = Cfg2<BN, kRowT>;
     static bool attr_set = false;
-    auto kern = gemm_tc2_kernel<BN, A_MN, B_MN>;
+    auto kern = gemm_tc2_kernel<BN, A_MN, B_MN, false>;
+    auto kern_rt = gemm_tc2_kernel<BN, A_MN, B_MN, kRowT>;
     if (!attr_set) {
         CG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        CG_CUDA(cudaFuncSetAttribute(kern_rt, cudaFuncAttributeMaxDynamicSharedMemorySize, CR::SMEM));
         attr_set = true;
     }
     CUtensorMap ta, tb;
@@ -1381,10 +1544,21 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     }
     const int grid = 2 * std::min(tiles * ks, slots);
     if (ks == 1) {
-        kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, 1, kb_per, 0L, epi);
+        const bool huge = (long)M * N >= (64L << 20);  // 256 MB of output, twice L2
+        const bool rowt = kRowT && (epi.ce_part || (epi.mode == EPI_STORE && huge));
+        if (rowt) {
+            // an output that large is not read again from L2: stores marked
+            // evict-first keep the operand tiles resident instead
+            GemmEpi e2 = epi;
+            e2.stream_out = huge;
+            const int grid_rt = 2 * std::min(tiles, pair_slots(kern_rt, CR::THREADS, CR::SMEM));
+            kern_rt<<<grid_rt, CR::THREADS, CR::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, 1, kb_per, 0L, e2);
+        } else {
+            kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, 1, kb_per, 0L, epi);
+        }
         ++g_launch_count;
         CG_CUDA(cudaGetLastError());
-        return OK;
+        return epi.ce_part && !rowt ? ce_stats_pass(epi, M, N, s) : OK;
     }
     GemmEpi pe;
     pe.mode = EPI_STORE;

@@ -93,6 +93,7 @@ struct GemmEpi {
     long ldg = 0;
     int vec4 = 0;  // set by gemm(): every pointer 16B-aligned and every pitch % 4 == 0
     int fast_act = 0;  // set by gemm() in TF32 mode: GELU epilogues use tanh_fast
+    int stream_out = 0;  // STORE outputs far larger than L2: evict-first stores (pair GEMM)
     // KV-cache decode (STORE mode, D = packed qkv rows): the K and V columns
     // [kv_C, 3 kv_C) are also written to kc / vc at position *kv_pos:
     // kc[m * kv_ld + pos * kv_C + (n - kv_C)], vc likewise for n >= 2 kv_C
