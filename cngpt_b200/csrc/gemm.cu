@@ -286,20 +286,49 @@ __device__ __forceinline__ float2 get2(const float *p, bool two, bool vec) {
 
 // `vec`: every operand pointer 16-byte aligned and every pitch a multiple of
 // 4 floats (GemmEpi::vec4), so the pairs at even columns are 8-byte aligned.
+// MODE: the epilogue mode when the kernel is specialised for one (>= 0), or
+// -1 to switch on GemmEpi::mode at run time. A block wholly inside the output
+// with aligned operands takes the unchecked path.
+template <int MODE>
 __device__ __forceinline__ void store_frag(const GemmEpi &ep, float *D, const float (&v)[32], int lane, int m0,
                                            int n0, int M, int N, const float *aux, long ldaux) {
     const bool vec = ep.vec4 != 0;
+    const int mode = MODE >= 0 ? MODE : ep.mode;
+    const bool full = vec && m0 + 32 <= M && n0 + 32 <= N;
     float2 b[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int n = n0 + frag_col(2 * j, lane);
-        b[j] = ep.bias && n < N ? get2(ep.bias + n, n + 1 < N, vec) : make_float2(0.f, 0.f);
+        b[j] = make_float2(0.f, 0.f);
+        if (ep.bias) {
+            if (full) b[j] = *(const float2 *)(ep.bias + n);
+            else if (n < N) b[j] = get2(ep.bias + n, n + 1 < N, vec);
+        }
     }
     const float al = ep.alpha;
     const bool fa = ep.fast_act != 0;
     // two halves of 16 rows; in each, the second operands are loaded first so
     // their loads are in flight together
     auto run = [&](auto op) {
+        if (full) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float2 x[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int k = 8 * h + i;
+                    x[i] = aux ? *(const float2 *)(aux + (m0 + frag_row(k, lane)) * ldaux + n0 + frag_col(k, lane))
+                               : make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int k = 8 * h + i;
+                    op(m0 + frag_row(k, lane), n0 + frag_col(k, lane),
+                       make_float2(v[2 * k] * al, v[2 * k + 1] * al), b[(k >> 1) & 3], x[i], true, true);
+                }
+            }
+            return;
+        }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             float2 x[8];
@@ -316,39 +345,39 @@ __device__ __forceinline__ void store_frag(const GemmEpi &ep, float *D, const fl
                 const long m = m0 + frag_row(k, lane);
                 const int n = n0 + frag_col(k, lane);
                 if (m < M && n < N)
-                    op(m, n, make_float2(v[2 * k] * al, v[2 * k + 1] * al), b[(k >> 1) & 3], x[i], n + 1 < N);
+                    op(m, n, make_float2(v[2 * k] * al, v[2 * k + 1] * al), b[(k >> 1) & 3], x[i], n + 1 < N, vec);
             }
         }
     };
-    switch (ep.mode) {
+    switch (mode) {
         case EPI_STORE:
-            run([&](long m, int n, float2 a, float2 bb, float2, bool two) {
-                put2(D + m * ep.ldd + n, make_float2(a.x + bb.x, a.y + bb.y), two, vec);
+            run([&](long m, int n, float2 a, float2 bb, float2, bool two, bool vv) {
+                put2(D + m * ep.ldd + n, make_float2(a.x + bb.x, a.y + bb.y), two, vv);
             });
             break;
         case EPI_ACCUM:
-            run([&](long m, int n, float2 a, float2 bb, float2 o, bool two) {
-                put2(D + m * ep.ldd + n, make_float2((o.x + a.x) + bb.x, (o.y + a.y) + bb.y), two, vec);
+            run([&](long m, int n, float2 a, float2 bb, float2 o, bool two, bool vv) {
+                put2(D + m * ep.ldd + n, make_float2((o.x + a.x) + bb.x, (o.y + a.y) + bb.y), two, vv);
             });
             break;
         case EPI_GELU:
-            run([&](long m, int n, float2 a, float2 bb, float2, bool two) {
+            run([&](long m, int n, float2 a, float2 bb, float2, bool two, bool vv) {
                 a = make_float2(a.x + bb.x, a.y + bb.y);
-                if (D) put2(D + m * ep.ldd + n, a, two, vec);
-                put2(ep.D2 + m * ep.ldd2 + n, make_float2(gelu_tanh(a.x, fa), gelu_tanh(a.y, fa)), two, vec);
+                if (D) put2(D + m * ep.ldd + n, a, two, vv);
+                put2(ep.D2 + m * ep.ldd2 + n, make_float2(gelu_tanh(a.x, fa), gelu_tanh(a.y, fa)), two, vv);
             });
             break;
         case EPI_RESID:
-            run([&](long m, int n, float2 a, float2 bb, float2 r, bool two) {
+            run([&](long m, int n, float2 a, float2 bb, float2 r, bool two, bool vv) {
                 a = make_float2(a.x + bb.x, a.y + bb.y);
-                if (D) put2(D + m * ep.ldd + n, a, two, vec);
-                put2(ep.D2 + m * ep.ldd2 + n, make_float2(r.x + a.x, r.y + a.y), two, vec);
+                if (D) put2(D + m * ep.ldd + n, a, two, vv);
+                put2(ep.D2 + m * ep.ldd2 + n, make_float2(r.x + a.x, r.y + a.y), two, vv);
             });
             break;
         case EPI_GELU_BWD:
-            run([&](long m, int n, float2 a, float2, float2 g, bool two) {
+            run([&](long m, int n, float2 a, float2, float2 g, bool two, bool vv) {
                 put2(D + m * ep.ldd + n,
-                     make_float2(a.x * gelu_tanh_grad(g.x, fa), a.y * gelu_tanh_grad(g.y, fa)), two, vec);
+                     make_float2(a.x * gelu_tanh_grad(g.x, fa), a.y * gelu_tanh_grad(g.y, fa)), two, vv);
             });
             break;
     }
@@ -665,7 +694,7 @@ struct Cfg2 {
     static_assert(CHUNKS % 2 == 0, "the cross-entropy groups need chunk pairs");
 };
 
-template <int BN, bool A_MN, bool B_MN, bool ROWT>
+template <int BN, bool A_MN, bool B_MN, bool ROWT, int MODE = -1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg2<BN, ROWT>::THREADS, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 int M, int N, int K, int tiles_m, int tiles_n, int ksplit, int kb_per, long split_stride,
@@ -830,7 +859,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     float v[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                    store_frag(epi, D, v, lane, m0, n0, M, N, aux, ldaux);
+                    store_frag<MODE>(epi, D, v, lane, m0, n0, M, N, aux, ldaux);
                 }
             }
             if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
@@ -1508,6 +1537,39 @@ int pair_slots(Kern kern, int threads, int smem) {
     return n;
 }
 
+// The dynamic shared-memory limit of each kernel, raised once per kernel.
+int smem_attr_once(const void *kern, int bytes) {
+    static std::mutex mu;
+    static std::unordered_map<const void *, int> done;
+    std::lock_guard<std::mutex> g(mu);
+    if (done.count(kern)) return OK;
+    CG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done[kern] = bytes;
+    return OK;
+}
+
+// The pair kernel for one epilogue mode: instantiations specialised to the
+// (orientation, mode) pairs of the training step - forward STORE / RESID /
+// GELU, dX STORE / ACCUM / GELU_BWD, dW STORE / ACCUM - carry only their own
+// epilogue code; every other pair runs the kernel that switches at run time.
+template <int BN, bool A_MN, bool B_MN>
+auto tc2_kernel_for(int mode) {
+    auto k = gemm_tc2_kernel<BN, A_MN, B_MN, false, -1>;
+    if constexpr (BN == 256 && !A_MN && !B_MN) {
+        if (mode == EPI_STORE) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_STORE>;
+        if (mode == EPI_RESID) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_RESID>;
+        if (mode == EPI_GELU) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_GELU>;
+    } else if constexpr (BN == 256 && !A_MN && B_MN) {
+        if (mode == EPI_STORE) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_STORE>;
+        if (mode == EPI_ACCUM) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_ACCUM>;
+        if (mode == EPI_GELU_BWD) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_GELU_BWD>;
+    } else if constexpr (BN == 256 && A_MN && B_MN) {
+        if (mode == EPI_STORE) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_STORE>;
+        if (mode == EPI_ACCUM) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_ACCUM>;
+    }
+    return k;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N, int K, const GemmEpi &epi,
                cudaStream_t s) {
@@ -1517,14 +1579,7 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     // folds, and STORE GEMMs whose output is far larger than L2
     constexpr bool kRowT = !A_MN && !B_MN && BN == 256;
     using CR = Cfg2<BN, kRowT>;
-    static bool attr_set = false;
-    auto kern = gemm_tc2_kernel<BN, A_MN, B_MN, false>;
     auto kern_rt = gemm_tc2_kernel<BN, A_MN, B_MN, kRowT>;
-    if (!attr_set) {
-        CG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-        CG_CUDA(cudaFuncSetAttribute(kern_rt, cudaFuncAttributeMaxDynamicSharedMemorySize, CR::SMEM));
-        attr_set = true;
-    }
     CUtensorMap ta, tb;
     if (A_MN) CG_TRY(make_map(&ta, A, M, K, lda, 32, BK, true));
     else      CG_TRY(make_map(&ta, A, K, M, lda, BK, BM, false));
@@ -1533,7 +1588,9 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     const int tiles_m = (M + 2 * BM - 1) / (2 * BM), tiles_n = (N + BN - 1) / BN;
     const int tiles = tiles_m * tiles_n;
     const int kblocks = (K + BK - 1) / BK;
-    const int slots = pair_slots(kern, C::THREADS, C::SMEM);
+    auto kern_any = gemm_tc2_kernel<BN, A_MN, B_MN, false, -1>;
+    CG_TRY(smem_attr_once((const void *)kern_any, C::SMEM));
+    const int slots = pair_slots(kern_any, C::THREADS, C::SMEM);
     int ks = choose_ksplit(tiles, kblocks, M, N, K, false, slots, BN, true);
     int kb_per = (kblocks + ks - 1) / ks;
     ks = (kblocks + kb_per - 1) / kb_per;
@@ -1551,9 +1608,12 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
             // evict-first keep the operand tiles resident instead
             GemmEpi e2 = epi;
             e2.stream_out = huge;
+            CG_TRY(smem_attr_once((const void *)kern_rt, CR::SMEM));
             const int grid_rt = 2 * std::min(tiles, pair_slots(kern_rt, CR::THREADS, CR::SMEM));
             kern_rt<<<grid_rt, CR::THREADS, CR::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, 1, kb_per, 0L, e2);
         } else {
+            auto kern = tc2_kernel_for<BN, A_MN, B_MN>(epi.mode);
+            CG_TRY(smem_attr_once((const void *)kern, C::SMEM));
             kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, 1, kb_per, 0L, epi);
         }
         ++g_launch_count;
@@ -1566,6 +1626,8 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     pe.ldd = N;
     pe.vec4 = (N % 4) == 0;
     const long stride = (long)M * N;
+    auto kern = tc2_kernel_for<BN, A_MN, B_MN>(EPI_STORE);
+    CG_TRY(smem_attr_once((const void *)kern, C::SMEM));
     kern<<<grid, C::THREADS, C::SMEM, s>>>(ta, tb, M, N, K, tiles_m, tiles_n, ks, kb_per, stride, pe);
     ++g_launch_count;
     CG_CUDA(cudaGetLastError());
