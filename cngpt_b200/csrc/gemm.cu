@@ -669,8 +669,10 @@ done:
 // CTAs' TMA completions count on the leader's `full` barrier, the MMA commits
 // arrive on `empty` / `tfull` in both CTAs, and the epilogue warps of both
 // CTAs release an accumulator on the leader's `tempty`. TF32 mode only.
-// ROWT selects the epilogue flavour. false: 16 epilogue warps at BN = 256
-// (four per TMEM lane quarter, two 32-column chunks each) reading the
+// BN: 256, 192 or 128 output columns per pair tile (192 fills whole waves
+// on the N = 768 products of GPT-2 small: 128 tiles instead of 96 on 74
+// pairs). ROWT selects the epilogue flavour. false: BN / 16 epilogue warps
+// (at BN = 256 four per TMEM lane quarter, two 32-column chunks each) reading the
 // accumulator in the 16x256b layout and storing 8-byte pairs from registers
 // (store_frag) - enough warps to hide the global stores and the GELU /
 // GELU-backward arithmetic behind the next tile's main loop. true: 8 warps
@@ -686,10 +688,10 @@ struct Cfg2 {
     static constexpr int B_BYTES = BNH * KB_BYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = BN == 256 ? 6 : 8;
-    static constexpr int EPI_WARPS = BN == 256 && !ROWT ? 16 : 8;
+    static constexpr int EPI_WARPS = ROWT ? 8 : BN / 16;  // two 32-column chunks per warp and tile
     static constexpr int CHUNKS = BN / 32 / (EPI_WARPS / 4);  // per warp and tile
     static constexpr int THREADS = (2 + EPI_WARPS) * 32;
-    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int TMEM_COLS = BN == 192 ? 512 : 2 * BN;  // two accumulators, a power of two
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + (ROWT ? EPI_WARPS * 32 * 33 * 4 : 0);
     static_assert(CHUNKS % 2 == 0, "the cross-entropy groups need chunk pairs");
 };
@@ -1566,6 +1568,11 @@ auto tc2_kernel_for(int mode) {
     } else if constexpr (BN == 256 && A_MN && B_MN) {
         if (mode == EPI_STORE) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_STORE>;
         if (mode == EPI_ACCUM) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_ACCUM>;
+    } else if constexpr (BN == 192 && !A_MN && !B_MN) {  // the N = 768 products
+        if (mode == EPI_STORE) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_STORE>;
+        if (mode == EPI_RESID) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_RESID>;
+    } else if constexpr (BN == 192 && !A_MN && B_MN) {
+        if (mode == EPI_STORE) k = gemm_tc2_kernel<BN, A_MN, B_MN, false, EPI_STORE>;
     }
     return k;
 }
@@ -1638,15 +1645,32 @@ int launch_tc2(const float *A, long lda, const float *B, long ldb, int M, int N,
     return epi.ce_part ? ce_stats_pass(epi, M, N, s) : OK;
 }
 
-// Tile width for the pair kernel: the modelled-faster of 256 and 128 (each
-// with its best K split).
-int pair_tile_width(int M, int N, int K) {
+// Tile width for the pair kernel: the modelled-fastest of 256, 192 (unless
+// `no192`) and 128, each with its best K split. CNGPT_CUDA_PAIR_BN=256|192|128
+// forces one.
+int pair_tile_width(int M, int N, int K, bool no192) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char *e = getenv("CNGPT_CUDA_PAIR_BN");
+        const int v = e ? atoi(e) : 0;
+        forced = (v == 256 || v == 192 || v == 128) ? v : 0;
+    }
+    if (forced) return forced;
     const int pairs = num_sms() / 2, tm = (M + 2 * BM - 1) / (2 * BM), kblocks = (K + BK - 1) / BK;
     if (N <= 128) return 128;
-    double t256 = 0, t128 = 0;
-    choose_ksplit(tm * ((N + 255) / 256), kblocks, M, N, K, false, pairs, 256, true, &t256);
-    choose_ksplit(tm * ((N + 127) / 128), kblocks, M, N, K, false, pairs, 128, true, &t128);
-    return t256 <= t128 ? 256 : 128;
+    int best = 256;
+    double tb = 0;
+    choose_ksplit(tm * ((N + 255) / 256), kblocks, M, N, K, false, pairs, 256, true, &tb);
+    for (int bn : {192, 128}) {
+        if (bn == 192 && no192) continue;
+        double t = 0;
+        choose_ksplit(tm * ((N + bn - 1) / bn), kblocks, M, N, K, false, pairs, bn, true, &t);
+        if (t < tb) {
+            tb = t;
+            best = bn;
+        }
+    }
+    return best;
 }
 
 template <bool A_MN, bool B_MN>
@@ -1654,11 +1678,14 @@ int dispatch_tc(const float *A, long lda, const float *B, long ldb, int M, int N
                 const GemmEpi &epi, cudaStream_t s, bool split) {
     if (split) return launch_tc<128, A_MN, B_MN, true>(A, lda, B, ldb, M, N, K, epi, s);
     if (pair_gemm_enabled() && M > BM) {
-        // CTA pairs with 256 x 256 or 256 x 128 tiles, whichever the model
-        // below times faster (tile width trades wave fill against the
-        // L2-to-SM bytes per FLOP)
-        const int bn = pair_tile_width(M, N, K);
+        // CTA pairs with 256 x 256, 256 x 192 or 256 x 128 tiles, whichever
+        // the model below times fastest (tile width trades wave fill against
+        // the L2-to-SM bytes per FLOP)
+        // both operands MN-major (the dW products): 192-wide tiles measured
+        // slower than 256 (2304 x 768 x 8192: 70.3 against 66.0 us)
+        const int bn = pair_tile_width(M, N, K, A_MN && B_MN);
         if (bn == 256) return launch_tc2<256, A_MN, B_MN>(A, lda, B, ldb, M, N, K, epi, s);
+        if (bn == 192) return launch_tc2<192, A_MN, B_MN>(A, lda, B, ldb, M, N, K, epi, s);
         return launch_tc2<128, A_MN, B_MN>(A, lda, B, ldb, M, N, K, epi, s);
     }
     // 128 x 256 tiles halve the A traffic per FLOP; take them unless their
