@@ -326,6 +326,14 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// The same arrive without release semantics: for a signal that orders no
+// memory writes - e.g. "the accumulator was read" after tcgen05.wait::ld and
+// tcgen05.fence::before_thread_sync - so the arriving thread does not wait for
+// its earlier global stores to drain.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // 2-D tiled TMA load into this CTA's shared memory only, whose completion is
 // counted on an mbarrier of either CTA of the pair (cluster address).
 __device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap, uint32_t bar_cluster,

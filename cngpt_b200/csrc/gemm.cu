@@ -840,7 +840,10 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     if (c == CH - 1) {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+                        // relaxed: the TMEM reads are complete (tcgen05.wait::ld)
+                        // and the signal orders no memory writes, so it need not
+                        // wait for this warp's stores of the first chunk
+                        if (lane == 0) mbar_arrive_cluster_relaxed(tempty_leader + acc * 8);
                     }
                 };
                 if constexpr (ROWT) {
