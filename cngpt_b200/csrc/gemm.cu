@@ -22,10 +22,14 @@
 //               normwise for one accumulator over K); per-k-block partials keep
 //               3xTF32 at fp32-level accuracy for any K
 //
-// The TF32 CTA-pair kernel (gemm_tc2_kernel: two CTAs of a cluster share one
-// 256-row tile through tcgen05.mma.cta_group::2) runs 16 epilogue warps at
-// BN = 256; they read the accumulator in the 16x256b layout and store from
-// registers (store_frag).
+// The warp roles above are the single-CTA kernel's (gemm_tc_kernel: 3xTF32,
+// short M). The TF32 CTA-pair kernel (gemm_tc2_kernel: two CTAs of a
+// cluster share one 256-row tile through tcgen05.mma.cta_group::2, tile
+// widths 256 / 192 / 128) runs BN / 16 epilogue warps that read the
+// accumulator in the 16x256b layout and store from registers (store_frag),
+// one instantiation per epilogue mode of the training step; the LM head
+// keeps an 8-warp epilogue that transposes through shared memory
+// (store_block) and folds the cross-entropy statistics.
 //
 // Operands may be K-major or MN-major in global memory (the instruction
 // descriptor's transpose bits), so X W^T (forward), dY W (dX) and dY^T X (dW)
